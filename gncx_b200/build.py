@@ -1,0 +1,70 @@
+"""Build the in-tree CUDA library ``gncx_b200/libgncx_llm_core.so`` for sm_100a.
+
+Run ``python -m gncx_b200.build`` (or ``__graft_entry__.build()``).  nvcc
+cross-compiles without a GPU.  Objects go to ``gncx_b200/_build/``; the shared
+library is written next to this file so it travels with the source tree.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+CSRC = HERE / "csrc"
+OUT_DIR = HERE / "_build"
+LIB = HERE / "libgncx_llm_core.so"
+
+SOURCES = ["gemv.cu", "matbatch.cu", "attention.cu", "ops.cu", "capi.cu", "engine.cu"]
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC,-O2,-ffp-contract=off",
+    "-Xptxas", "-warn-spills",
+]
+
+
+def _nvcc() -> str:
+    cand = os.environ.get("NVCC") or "/usr/local/cuda/bin/nvcc"
+    return cand if Path(cand).exists() else "nvcc"
+
+
+def _stale(obj: Path, src: Path) -> bool:
+    if not obj.exists():
+        return True
+    deps = [src] + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list((HERE.parent / "include").glob("*.h"))
+    t = obj.stat().st_mtime
+    return any(d.stat().st_mtime > t for d in deps)
+
+
+def build(verbose: bool = False, force: bool = False) -> Path:
+    OUT_DIR.mkdir(exist_ok=True)
+    nvcc = _nvcc()
+    srcs = [CSRC / s for s in SOURCES if (CSRC / s).exists()]
+    jobs = []
+    for s in srcs:
+        obj = OUT_DIR / (s.stem + ".o")
+        if force or _stale(obj, s):
+            jobs.append([nvcc, *NVCC_FLAGS, "-c", str(s), "-o", str(obj)])
+
+    def run(cmd):
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+        if verbose and r.stderr.strip():
+            print(r.stderr, file=sys.stderr)
+
+    with ThreadPoolExecutor(max_workers=min(8, max(1, len(jobs)))) as ex:
+        list(ex.map(run, jobs))
+    objs = [str(OUT_DIR / (s.stem + ".o")) for s in srcs]
+    if jobs or not LIB.exists() or force:
+        run([nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", str(LIB), *objs,
+             "-lcudart", "-ldl"])
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(verbose=True, force="--force" in sys.argv))

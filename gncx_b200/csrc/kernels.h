@@ -1,0 +1,72 @@
+// kernels.h -- host-side launchers for the B200 hot-path kernels (internal).
+// Every launcher returns a gncx::Status; launch failures map to kErrCuda.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+#include "common.cuh"
+
+namespace gncx {
+
+struct DeviceInfo {
+    int device = -1;
+    int sm_count = 0;
+    int max_smem_optin = 0;
+    int l2_bytes = 0;
+};
+// Properties of the current device (queried once per device).
+const DeviceInfo& device_info();
+
+// ---- GEMV / prefill ----
+int gemv_launch(const uint8_t* w, int32_t type, const float* x, const ActBlock* act, int32_t in_dim,
+                int32_t out_dim, float* y, float softcap, int32_t* err, cudaStream_t st);
+int matbatch_launch(const uint8_t* w, int32_t type, const float* xb, const ActBlock* act, int32_t batch,
+                    int32_t in_dim, int32_t out_dim, float* yb, int32_t* err, cudaStream_t st);
+// x[rows][in_dim] -> ActBlock[rows][in_dim/32]
+int act_quantize_launch(const float* x, int32_t rows, int32_t in_dim, ActBlock* out, cudaStream_t st);
+// Dequantize `rows` rows of `n` weights (row stride = row_bytes(type, n)) to fp32.
+int dequant_launch(const uint8_t* w, int32_t type, int32_t rows, int32_t n, float scale, const int32_t* row_ids,
+                   float* out, cudaStream_t st);
+
+// ---- norms / rope / activations ----
+// out[r] = rmsnorm(x[r]) * w, rows of `dim`; optional residual: x += res first (written back).
+int rmsnorm_launch(const float* x, const float* w, int32_t rows, int32_t dim, float eps, float* out,
+                   cudaStream_t st);
+int rmsnorm_heads_launch(float* v, const float* w, int32_t rows, int32_t n_heads, int32_t head_dim, float eps,
+                         cudaStream_t st);
+// Rotate-half RoPE of `rows` vectors of n_heads heads; per-row positions
+// pos0 + r (pos_list == nullptr) or pos_list[r]; cos/sin from the table
+// [max_pos][head_dim/2] (host-computed with the reference's libm calls).
+int rope_launch(float* v, int32_t rows, int32_t row_stride, int32_t n_heads, int32_t head_dim, int32_t pos0,
+                const float* cos_tab, const float* sin_tab, cudaStream_t st);
+struct RopeTab {
+    float c[256];
+    float s[256];
+};
+// One position, q (nh heads) and/or k (nkv heads); either may be null.
+int rope_tab_launch(float* q, float* k, int32_t nh, int32_t nkv, int32_t hd, const RopeTab& tab, cudaStream_t st);
+int absmax_launch(const float* x, int32_t n, float* out, cudaStream_t st);
+int glu_launch(const float* g, const float* u, int64_t n, float* out, bool gelu, cudaStream_t st);
+int softcap_launch(float* x, int64_t n, float cap, cudaStream_t st);
+
+// ---- attention ----
+struct AttnScratch {
+    float* part;        // partial (max, sum, o[hd]) records
+    int32_t capacity;   // records available
+};
+int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t n_heads, int32_t n_kv,
+                     int32_t head_dim, float scale, int32_t window, float* out, const AttnScratch& scratch,
+                     int32_t* err, cudaStream_t st);
+int32_t attention_scratch_records(int32_t pos, int32_t n_heads, int32_t window);
+
+// ---- sampling ----
+// Penalized greedy argmax (lua/gncx_streamer.lua:1229-1273) -> *out_idx.
+int argmax_penalized_launch(const float* logits, int32_t vocab, const int32_t* recent, int32_t n_recent,
+                            double penalty, int32_t* out_idx, void* scratch, cudaStream_t st);
+size_t argmax_scratch_bytes(int32_t vocab);
+
+// ---- embedding ----
+int embed_launch(const uint8_t* tensor, int32_t type, const int32_t* tokens, int32_t n_tokens, int32_t dim,
+                 float scale, float* out, cudaStream_t st);
+
+}  // namespace gncx

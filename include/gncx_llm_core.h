@@ -1,0 +1,178 @@
+/*
+ * gncx_llm_core.h -- C ABI of the B200 build of the GNC-X hot path.
+ *
+ * Drop-in for the reference library (csrc/gncx_llm_kernels.cpp of
+ * omega-Core-Dev/gnc-x, loaded by lua/gncx_gguf.lua:72-73 and bound by the
+ * ffi.cdef block of lua/gncx_streamer.lua:16-252): the entry points in the
+ * first part carry the reference's names, argument order and types.
+ *
+ * Memory model.  Every float / byte pointer handed to a kernel entry point
+ * must be reachable by the GPU: device memory, managed memory (what
+ * gncx_ram_alloc* returns), or an address inside a file mapped with
+ * gncx_gla_map_readonly (translated to that file's device mirror).  Telemetry
+ * structs and the quant-scale out-parameter stay host memory, as in the
+ * reference.  A pointer the GPU cannot reach is rejected with
+ * GNCX_ERR_NOT_DEVICE_ACCESSIBLE; there is no CPU fallback.
+ *
+ * Errors.  The reference's kernels return void and report nothing.  Here each
+ * call records a status readable with gncx_last_error(); by default every
+ * reference-named call also waits for its GPU work (synchronous mode), so a
+ * caller that reads results on the host, as the Lua orchestrator does, sees
+ * them complete.  gncx_set_synchronous(0) makes calls stream-ordered.
+ */
+#ifndef GNCX_LLM_CORE_H
+#define GNCX_LLM_CORE_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#pragma pack(push, 1)
+/* csrc/gncx_llm_kernels.cpp:267-271 (telemetry only; never read or written here) */
+typedef struct {
+    uint8_t phase_2bit;
+    uint8_t diag_d;
+    uint16_t abs_delta;
+} GNCXCompactToken;
+
+/* :308-313 (host memory; counters updated on the host) */
+typedef struct {
+    uint64_t total_macs_equivalent;
+    uint64_t zero_origin_cancellations;
+    uint64_t zero_weight_skips;
+    uint64_t xfold_bucket_merges;
+} GNCXTelemetryStats;
+#pragma pack(pop)
+
+/* ------------------------------------------------------------------------ */
+/* Reference entry points (same names and signatures)                        */
+/* ------------------------------------------------------------------------ */
+
+/* GGUF file mapping: :327-404, :617-667.  map_readonly mmaps the file on the
+ * host (the loader parses it there) and uploads a device mirror of it. */
+void* gncx_gla_map_readonly(const char* filepath, size_t* out_size);          /* :327 */
+const uint8_t* gncx_gla_get_base_ptr(void* opaque_handle);                      /* :386 */
+void gncx_gla_unmap(void* opaque_handle);                                       /* :391 */
+void gncx_gla_prefetch_range(const uint8_t* mmap_base, size_t offset, size_t num_bytes); /* :617 */
+
+/* Weight arena: :481-612.  Backed by CUDA managed memory, so host loops over
+ * scratch buffers (lua/gncx_streamer.lua:871-873) keep working. */
+void* gncx_ram_alloc_colored(size_t total_bytes, uint8_t k, uint8_t d, uint8_t R); /* :481 */
+void* gncx_ram_alloc(size_t total_bytes);                                        /* :553 */
+uint8_t* gncx_ram_get_ptr(void* ram_handle);                                     /* :561 */
+uint8_t gncx_ram_get_ddr3_bank(void* ram_handle);                                /* :566 */
+uint8_t gncx_ram_get_l1_set(void* ram_handle);                                   /* :571 */
+void gncx_ram_free(void* ram_handle);                                            /* :576 */
+void gncx_ram_copy_chunk(void* ram_handle, size_t dst_offset, const uint8_t* src_base, size_t src_offset,
+                         size_t num_bytes);                                      /* :602 */
+
+/* Embedding rows: :693, :720, :765 */
+void gncx_fetch_token_embedding_q8_0(const uint8_t* mmap_base, size_t tensor_abs_offset, int32_t token_id,
+                                     int32_t embed_dim, float scale_factor, float* out_hidden);
+void gncx_fetch_token_embedding_q6_k(const uint8_t* mmap_base, size_t tensor_abs_offset, int32_t token_id,
+                                     int32_t embed_dim, float scale_factor, float* out_hidden);
+void gncx_fetch_token_embedding_bf16(const uint8_t* mmap_base, size_t tensor_abs_offset, int32_t token_id,
+                                     int32_t embed_dim, float scale_factor, float* out_hidden);
+
+/* RMSNorm: :789 (out_tokens is telemetry and is not written), :895 */
+void gncx_rmsnorm_and_encode_4phase(const float* input_hidden, const uint8_t* mmap_base, size_t norm_weight_offset,
+                                    int32_t dim, float eps, int32_t layer_k, float* out_normed_fp32,
+                                    GNCXCompactToken* out_tokens, float* out_quant_scale);
+void gncx_rmsnorm_inplace_heads(float* vec, const uint8_t* mmap_base, size_t norm_weight_offset, int32_t has_weight,
+                                int32_t n_heads, int32_t head_dim, float eps);
+
+/* Quantized GEMV / prefill GEMM: :1327, :1476, :1495, :1694.
+ * ggml_type 2=Q4_0, 8=Q8_0, 12=Q4_K, 14=Q6_K, 30=BF16; quantized types need
+ * in_dim % 256 == 0. */
+void gncx_xfold_universal_matvec(const uint8_t* mmap_base, size_t weight_abs_offset, int32_t ggml_type,
+                                 const float* in_vec, const GNCXCompactToken* in_tokens, int32_t in_dim,
+                                 int32_t out_dim, float* out_vec, GNCXTelemetryStats* telemetry);
+void gncx_xfold_q4_0_matvec(const uint8_t* mmap_base, size_t weight_abs_offset, const float* in_vec,
+                            const GNCXCompactToken* in_tokens, int32_t in_dim, int32_t out_dim, float* out_vec,
+                            GNCXTelemetryStats* telemetry);
+void gncx_xfold_universal_matbatch(const uint8_t* mmap_base, size_t weight_abs_offset, int32_t ggml_type,
+                                   const float* in_batch, int32_t batch_size, int32_t in_dim, int32_t out_dim,
+                                   float* out_batch, GNCXTelemetryStats* telemetry);
+void gncx_xfold_q4_0_matbatch(const uint8_t* mmap_base, size_t weight_abs_offset, const float* in_batch,
+                              int32_t batch_size, int32_t in_dim, int32_t out_dim, float* out_batch,
+                              GNCXTelemetryStats* telemetry);
+
+/* LM head over the tied embedding, optional tanh softcap: :1713, :1734 */
+void gncx_universal_lm_head_logits(const uint8_t* mmap_base, size_t embd_abs_offset, int32_t ggml_type,
+                                   const float* final_hidden, int32_t embed_dim, int32_t vocab_size, float softcap,
+                                   float* out_logits);
+void gncx_q8_0_lm_head_logits(const uint8_t* mmap_base, size_t embd_abs_offset, const float* final_hidden,
+                              int32_t embed_dim, int32_t vocab_size, float* out_logits);
+
+/* RoPE (rotate-half): :1760, :1865.  q_tokens is telemetry and is not written. */
+void gncx_apply_rope_xor11_ext(float* q_vec, float* k_vec, GNCXCompactToken* q_tokens, const uint8_t* mmap_base,
+                               size_t rope_freqs_offset, int32_t has_rope_freqs, int32_t n_heads, int32_t n_kv_heads,
+                               int32_t head_dim, int32_t pos, float freq_base);
+void gncx_apply_rope_xor11(float* q_vec, float* k_vec, GNCXCompactToken* q_tokens, int32_t n_heads,
+                           int32_t n_kv_heads, int32_t head_dim, int32_t pos, float freq_base);
+
+/* GQA/MQA decode attention over the fp32 KV cache [max_seq][n_kv][head_dim]: :1887, :1996 */
+void gncx_mqa_attention_step_ext(const float* q_vec, const float* k_vec, const float* v_vec, float* k_cache_layer,
+                                 float* v_cache_layer, int32_t pos, int32_t n_heads, int32_t n_kv_heads,
+                                 int32_t head_dim, float attn_scale, int32_t sliding_window, int32_t write_kv,
+                                 float* out_attn_vec);
+void gncx_mqa_attention_step(const float* q_vec, const float* k_vec, const float* v_vec, float* k_cache_layer,
+                             float* v_cache_layer, int32_t pos, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                             float* out_attn_vec);
+
+/* GLU activations: :2018, :2038 */
+void gncx_geglu_activation(const float* gate_vec, const float* up_vec, int32_t ffn_dim, float* out_ffn_vec);
+void gncx_swiglu_activation(const float* gate_vec, const float* up_vec, int32_t ffn_dim, float* out_ffn_vec);
+
+/* ------------------------------------------------------------------------ */
+/* Added entry points (no counterpart in the reference): GPU plumbing        */
+/* ------------------------------------------------------------------------ */
+
+enum {
+    GNCX_OK = 0,
+    GNCX_ERR_INVALID_ARG = 1,
+    GNCX_ERR_UNALIGNED = 2,
+    GNCX_ERR_CUDA = 3,
+    GNCX_ERR_NO_DEVICE = 4,
+    GNCX_ERR_TIMEOUT = 5,
+    GNCX_ERR_NOT_DEVICE_ACCESSIBLE = 6,
+    GNCX_ERR_OUT_OF_MEMORY = 7,
+    GNCX_ERR_CAPACITY = 8
+};
+
+int32_t gncx_last_error(void);               /* first error since the last clear (sticky) */
+const char* gncx_last_error_message(void);
+void gncx_clear_error(void);
+int32_t gncx_sync(void);                     /* wait for queued work; returns and records its status */
+void gncx_set_stream(void* cuda_stream);     /* NULL = the library's own stream */
+void* gncx_get_stream(void);
+void gncx_set_synchronous(int32_t on);       /* 1 (default): reference-named calls wait before returning */
+int32_t gncx_device_count(void);
+int32_t gncx_set_device(int32_t device);
+
+/* Device memory for callers without a CUDA runtime of their own (ctypes, FFI). */
+void* gncx_device_alloc(size_t bytes);
+void gncx_device_free(void* ptr);
+int32_t gncx_memcpy(void* dst, const void* src, size_t bytes); /* any direction, synchronous */
+
+/* Activation re-quantization to the kernels' 48-byte block records
+ * ({float d; int32 sum_lo; int32 sum_hi; int32 pad; int8 qs[32]} per 32 inputs). */
+int32_t gncx_act_quantize(const float* x, int32_t rows, int32_t in_dim, void* act_out);
+/* GEMV from pre-quantized activations (the act-Q8 step shared by Q/K/V or gate/up). */
+int32_t gncx_matvec_preq(const uint8_t* base, size_t offset, int32_t ggml_type, const void* act, int32_t in_dim,
+                         int32_t out_dim, float* out_vec);
+/* Block dequantization of `rows` rows of `n` weights to fp32 (bit-exact with the
+ * reference's row-fetch routines for Q8_0/Q6_K/BF16). */
+int32_t gncx_dequantize_rows(const uint8_t* base, size_t offset, int32_t ggml_type, int32_t rows, int32_t n,
+                             float* out);
+/* Penalized greedy sampling (lua/gncx_streamer.lua:1229-1273) on device logits;
+ * `recent` is a host array.  Returns the token id, or -1 on error. */
+int32_t gncx_sample_greedy(const float* logits, int32_t vocab, const int32_t* recent, int32_t n_recent,
+                           double repeat_penalty);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GNCX_LLM_CORE_H */

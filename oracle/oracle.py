@@ -1,0 +1,247 @@
+"""Python handle on the CPU oracle (TEST INFRASTRUCTURE ONLY).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg use
+this module, and only as the checker / baseline, never as the product path.
+
+Two oracles are exposed with the same numpy-level API:
+  * :class:`Oracle` -- the plain-C restatement in gncx_oracle.c
+    (``oracle/_build/liboracle.so``);
+  * :class:`RefLib` -- the reference's own sources compiled here
+    (``oracle/_ref/libgncx_ref_strict.so`` is the strict-IEEE pin,
+    ``oracle/_ref/libgncx_ref.so`` the as-shipped flags), called through its
+    exported C ABI exactly as its own ctypes harness does
+    (verify_gncx_fixes.py:25-117).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import shutil
+import subprocess
+from ctypes import POINTER, c_char_p, c_double, c_float, c_int32, c_size_t, c_void_p
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_SO = HERE / "_build" / "liboracle.so"
+REF_STRICT_SO = HERE / "_ref" / "libgncx_ref_strict.so"
+REF_NATIVE_SO = HERE / "_ref" / "libgncx_ref.so"
+REFERENCE_SRC = Path(os.environ.get("GNCX_REFERENCE", "/root/reference"))
+
+ACT_DTYPE = np.dtype([("d", "<f4"), ("sum_q", "<i4"), ("sum_lo", "<i4"), ("sum_hi", "<i4"), ("qs", "i1", (32,))])
+
+
+def build(with_reference: bool = True) -> None:
+    """Build liboracle.so and, when the reference sources exist, oracle/_ref."""
+    if shutil.which("make") is None:
+        return
+    subprocess.run(["make", "-s", "-C", str(HERE), "all"], check=True)
+    if with_reference and (REFERENCE_SRC / "csrc" / "gncx_llm_kernels.cpp").exists():
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={REFERENCE_SRC}"], check=True)
+
+
+def _ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(c_void_p)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+class Oracle:
+    """The C restatement."""
+
+    def __init__(self, path: Path = ORACLE_SO):
+        if not Path(path).exists():
+            build(with_reference=False)
+        L = ctypes.CDLL(str(path))
+        self.lib = L
+        L.orc_matvec.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_int32, c_void_p]
+        L.orc_matbatch.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_int32, c_int32, c_void_p]
+        L.orc_lm_head.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_int32, c_float, c_void_p]
+        L.orc_act_quantize.argtypes = [c_void_p, c_int32, c_void_p]
+        L.orc_dequant_row.argtypes = [c_void_p, c_int32, c_int32, c_void_p]
+        L.orc_rmsnorm.argtypes = [c_void_p, c_void_p, c_int32, c_float, c_void_p]
+        L.orc_rmsnorm_heads.argtypes = [c_void_p, c_void_p, c_int32, c_int32, c_float]
+        L.orc_rope_table.argtypes = [c_int32, c_int32, c_float, c_void_p, c_void_p, c_void_p]
+        L.orc_rope.argtypes = [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_float]
+        L.orc_attention_step.argtypes = [c_void_p] * 5 + [c_int32] * 4 + [c_float, c_int32, c_int32, c_void_p]
+        L.orc_swiglu.argtypes = [c_void_p, c_void_p, c_int32, c_void_p]
+        L.orc_geglu.argtypes = [c_void_p, c_void_p, c_int32, c_void_p]
+        L.orc_embed_row.argtypes = [c_void_p, c_int32, c_int32, c_int32, c_float, c_void_p]
+        L.orc_sample_greedy.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_double]
+        L.orc_sample_greedy.restype = c_int32
+        L.orc_fp16_to_fp32.argtypes = [ctypes.c_uint16]
+        L.orc_fp16_to_fp32.restype = c_float
+
+    def matvec(self, w: np.ndarray, t: int, x, out_dim: int) -> np.ndarray:
+        x = _f32(x)
+        y = np.zeros(out_dim, np.float32)
+        self.lib.orc_matvec(_ptr(np.ascontiguousarray(w)), t, _ptr(x), x.size, out_dim, _ptr(y))
+        return y
+
+    def matbatch(self, w: np.ndarray, t: int, xb, out_dim: int) -> np.ndarray:
+        xb = _f32(xb)
+        B, n = xb.shape
+        y = np.zeros((B, out_dim), np.float32)
+        self.lib.orc_matbatch(_ptr(np.ascontiguousarray(w)), t, _ptr(xb), B, n, out_dim, _ptr(y))
+        return y
+
+    def lm_head(self, w, t, h, vocab, softcap=0.0):
+        h = _f32(h)
+        y = np.zeros(vocab, np.float32)
+        self.lib.orc_lm_head(_ptr(np.ascontiguousarray(w)), t, _ptr(h), h.size, vocab, softcap, _ptr(y))
+        return y
+
+    def act_quantize(self, x) -> np.ndarray:
+        x = _f32(x)
+        out = np.zeros(x.size // 32, ACT_DTYPE)
+        self.lib.orc_act_quantize(_ptr(x), x.size, _ptr(out))
+        return out
+
+    def dequant_row(self, row: np.ndarray, t: int, n: int) -> np.ndarray:
+        out = np.zeros(n, np.float32)
+        self.lib.orc_dequant_row(_ptr(np.ascontiguousarray(row)), t, n, _ptr(out))
+        return out
+
+    def rmsnorm(self, x, w, eps) -> np.ndarray:
+        x, w = _f32(x), _f32(w)
+        out = np.zeros_like(x)
+        self.lib.orc_rmsnorm(_ptr(x), _ptr(w), x.size, eps, _ptr(out))
+        return out
+
+    def rmsnorm_heads(self, v, w, n_heads, head_dim, eps) -> np.ndarray:
+        v = _f32(v).copy()
+        self.lib.orc_rmsnorm_heads(_ptr(v), _ptr(None if w is None else _f32(w)), n_heads, head_dim, eps)
+        return v
+
+    def rope_table(self, pos, hd, base, ff=None):
+        c = np.zeros(hd // 2, np.float32)
+        s = np.zeros(hd // 2, np.float32)
+        self.lib.orc_rope_table(pos, hd, base, _ptr(None if ff is None else _f32(ff)), _ptr(c), _ptr(s))
+        return c, s
+
+    def rope(self, q, k, n_heads, n_kv, hd, pos, base, ff=None):
+        q = None if q is None else _f32(q).copy()
+        k = None if k is None else _f32(k).copy()
+        self.lib.orc_rope(_ptr(q), _ptr(k), _ptr(None if ff is None else _f32(ff)), n_heads, n_kv, hd, pos, base)
+        return q, k
+
+    def attention(self, q, k, v, kc, vc, pos, n_heads, n_kv, hd, scale, window=0, write_kv=1):
+        kc, vc = _f32(kc).copy(), _f32(vc).copy()
+        out = np.zeros(n_heads * hd, np.float32)
+        self.lib.orc_attention_step(_ptr(_f32(q)), _ptr(None if k is None else _f32(k)),
+                                    _ptr(None if v is None else _f32(v)), _ptr(kc), _ptr(vc), pos, n_heads, n_kv,
+                                    hd, scale, window, write_kv, _ptr(out))
+        return out, kc, vc
+
+    def glu(self, g, u, gelu=False):
+        g, u = _f32(g), _f32(u)
+        out = np.zeros_like(g)
+        (self.lib.orc_geglu if gelu else self.lib.orc_swiglu)(_ptr(g), _ptr(u), g.size, _ptr(out))
+        return out
+
+    def embed(self, tensor, t, token, dim, scale=1.0):
+        out = np.zeros(dim, np.float32)
+        self.lib.orc_embed_row(_ptr(np.ascontiguousarray(tensor)), t, token, dim, scale, _ptr(out))
+        return out
+
+    def sample_greedy(self, logits, recent, penalty=1.15) -> int:
+        logits = _f32(logits)
+        r = np.ascontiguousarray(recent, dtype=np.int32)
+        return int(self.lib.orc_sample_greedy(_ptr(logits), logits.size, _ptr(r), r.size, penalty))
+
+
+class RefLib:
+    """The reference library built from its sources, called through its C ABI."""
+
+    def __init__(self, path: Path = REF_STRICT_SO):
+        L = ctypes.CDLL(str(path))
+        self.lib = L
+        L.gncx_gla_map_readonly.restype = c_void_p
+        L.gncx_gla_map_readonly.argtypes = [c_char_p, POINTER(c_size_t)]
+        # fills the fp16 table and starts the pool (csrc/gncx_llm_kernels.cpp:327-329);
+        # never unmapped (gncx_gla_unmap stops the pool, :392)
+        self._h = L.gncx_gla_map_readonly(str(path).encode(), None)
+        V = c_void_p
+        L.gncx_xfold_universal_matvec.argtypes = [V, c_size_t, c_int32, V, V, c_int32, c_int32, V, V]
+        L.gncx_xfold_universal_matbatch.argtypes = [V, c_size_t, c_int32, V, c_int32, c_int32, c_int32, V, V]
+        L.gncx_universal_lm_head_logits.argtypes = [V, c_size_t, c_int32, V, c_int32, c_int32, c_float, V]
+        L.gncx_rmsnorm_and_encode_4phase.argtypes = [V, V, c_size_t, c_int32, c_float, c_int32, V, V, V]
+        L.gncx_rmsnorm_inplace_heads.argtypes = [V, V, c_size_t, c_int32, c_int32, c_int32, c_float]
+        L.gncx_apply_rope_xor11_ext.argtypes = [V, V, V, V, c_size_t, c_int32, c_int32, c_int32, c_int32, c_int32,
+                                                c_float]
+        L.gncx_mqa_attention_step_ext.argtypes = [V] * 5 + [c_int32] * 4 + [c_float, c_int32, c_int32, V]
+        L.gncx_swiglu_activation.argtypes = [V, V, c_int32, V]
+        L.gncx_geglu_activation.argtypes = [V, V, c_int32, V]
+        for n in ("q8_0", "q6_k", "bf16"):
+            getattr(L, f"gncx_fetch_token_embedding_{n}").argtypes = [V, c_size_t, c_int32, c_int32, c_float, V]
+
+    def matvec(self, w, t, x, out_dim):
+        x = _f32(x)
+        y = np.zeros(out_dim, np.float32)
+        self.lib.gncx_xfold_universal_matvec(_ptr(np.ascontiguousarray(w)), 0, t, _ptr(x), None, x.size, out_dim,
+                                             _ptr(y), None)
+        return y
+
+    def matbatch(self, w, t, xb, out_dim):
+        xb = _f32(xb)
+        B, n = xb.shape
+        y = np.zeros((B, out_dim), np.float32)
+        self.lib.gncx_xfold_universal_matbatch(_ptr(np.ascontiguousarray(w)), 0, t, _ptr(xb), B, n, out_dim, _ptr(y),
+                                               None)
+        return y
+
+    def lm_head(self, w, t, h, vocab, softcap=0.0):
+        h = _f32(h)
+        y = np.zeros(vocab, np.float32)
+        self.lib.gncx_universal_lm_head_logits(_ptr(np.ascontiguousarray(w)), 0, t, _ptr(h), h.size, vocab, softcap,
+                                               _ptr(y))
+        return y
+
+    def rmsnorm(self, x, w, eps):
+        x, w = _f32(x), _f32(w)
+        out = np.zeros_like(x)
+        self.lib.gncx_rmsnorm_and_encode_4phase(_ptr(x), _ptr(w), 0, x.size, eps, 0, _ptr(out), None, None)
+        return out
+
+    def rmsnorm_heads(self, v, w, n_heads, head_dim, eps):
+        v = _f32(v).copy()
+        wp = None if w is None else _f32(w)
+        self.lib.gncx_rmsnorm_inplace_heads(_ptr(v), _ptr(wp), 0, 0 if w is None else 1, n_heads, head_dim, eps)
+        return v
+
+    def rope(self, q, k, n_heads, n_kv, hd, pos, base, ff=None):
+        q = None if q is None else _f32(q).copy()
+        k = None if k is None else _f32(k).copy()
+        ffa = None if ff is None else _f32(ff)
+        self.lib.gncx_apply_rope_xor11_ext(_ptr(q), _ptr(k), None, _ptr(ffa), 0, 0 if ff is None else 1, n_heads,
+                                           n_kv, hd, pos, base)
+        return q, k
+
+    def attention(self, q, k, v, kc, vc, pos, n_heads, n_kv, hd, scale, window=0, write_kv=1):
+        kc, vc = _f32(kc).copy(), _f32(vc).copy()
+        out = np.zeros(n_heads * hd, np.float32)
+        self.lib.gncx_mqa_attention_step_ext(_ptr(_f32(q)), _ptr(None if k is None else _f32(k)),
+                                             _ptr(None if v is None else _f32(v)), _ptr(kc), _ptr(vc), pos, n_heads,
+                                             n_kv, hd, scale, window, write_kv, _ptr(out))
+        return out, kc, vc
+
+    def glu(self, g, u, gelu=False):
+        g, u = _f32(g), _f32(u)
+        out = np.zeros_like(g)
+        fn = self.lib.gncx_geglu_activation if gelu else self.lib.gncx_swiglu_activation
+        fn(_ptr(g), _ptr(u), g.size, _ptr(out))
+        return out
+
+    def embed(self, tensor, t, token, dim, scale=1.0):
+        out = np.zeros(dim, np.float32)
+        name = {8: "q8_0", 14: "q6_k", 30: "bf16"}[t]
+        getattr(self.lib, f"gncx_fetch_token_embedding_{name}")(_ptr(np.ascontiguousarray(tensor)), 0, token, dim,
+                                                                  scale, _ptr(out))
+        return out
+
+
+def reference_available(strict: bool = True) -> bool:
+    return (REF_STRICT_SO if strict else REF_NATIVE_SO).exists()
