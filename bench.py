@@ -1,0 +1,362 @@
+#!/usr/bin/env python
+"""Benchmark: Q4_K GEMV HBM throughput on B200 (the reference's headline metric).
+
+One step = one decode-matvec pass over the Q4_K shape sweep of the benchmark
+configuration (out x in = 4096x4096, 4096x12288, 12288x4096, 151936x4096),
+weights in native GGUF Q4_K blocks resident in HBM, fp32 activations
+~N(0,1), through the C ABI entry point gncx_xfold_universal_matvec.  The four
+weight tensors total 417 MB per step, larger than the 126 MB L2, so every step
+streams from HBM.
+
+value     = algorithmic bytes (weights + x + y) of all steps on all ranks /
+            device time (CUDA events, max over ranks).
+e2e       = the same through the same entry point with host buffers: each
+            step copies every x from pinned host memory and reads every y back.
+roofline  = the 151936x4096 launch (84% of the bytes) against the measured
+            HBM copy bandwidth in MEASURED_PEAKS.json.
+Multi-GPU: one process per GPU, each streaming its own copy of the sweep
+(the GEMV shards by rows with no exchange): weak scaling.
+
+``--impl reference`` times the reference's own CPU kernels (oracle/_ref, built
+from its sources) on the same sweep with all host threads its pool uses.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Q4_K GEMV HBM GB/s"
+SHAPES = [(4096, 4096), (4096, 12288), (12288, 4096), (151936, 4096)]  # (out, in)
+SWEEP_TYPES = [2, 8, 12, 14]
+
+
+def algo_bytes(t: int, out_dim: int, in_dim: int) -> int:
+    from gncx_b200.core import row_bytes
+    return out_dim * row_bytes(t, in_dim) + 4 * in_dim + 4 * out_dim
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            pass
+    return {}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50", "-i",
+                 str(device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if not self.proc:
+            return None
+        time.sleep(0.12)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            return None
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def gen_weights_gpu(torch, t: int, out_dim: int, in_dim: int, seed: int):
+    """Seeded random blocks generated on the device (same distributions as gncx_b200.synth)."""
+    from gncx_b200.core import BLOCK, Q4_0, Q4_K, Q6_K, Q8_0
+    be, bb = BLOCK[t]
+    n = out_dim * (in_dim // be)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    raw = torch.randint(0, 256, (n, bb), dtype=torch.uint8, device="cuda", generator=g)
+
+    def scales():
+        return torch.randn(n, device="cuda", generator=g).mul_(0.02).abs_().half().view(torch.uint8).view(n, 2)
+
+    if t in (Q4_0, Q8_0, Q4_K):
+        raw[:, 0:2] = scales()
+    if t == Q4_K:
+        raw[:, 2:4] = scales()
+    if t == Q6_K:
+        raw[:, 208:210] = scales()
+    return raw.view(-1)
+
+
+def read_traffic() -> float | None:
+    """DRAM bytes per launch of the 151936x4096 Q4_K GEMV from the committed ncu summary."""
+    p = ROOT / "profiles" / "gemv_q4_k_151936x4096.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def cpu_baseline(seconds: float = 8.0) -> dict:
+    """The reference's CPU matvec (oracle/_ref, as-shipped flags) on the Q4_K sweep."""
+    from gncx_b200 import synth
+    from oracle.oracle import REF_NATIVE_SO, Oracle, RefLib
+    kind = "reference" if REF_NATIVE_SO.exists() else "port"
+    impl = RefLib(REF_NATIVE_SO) if kind == "reference" else Oracle()
+    cores = min(os.cpu_count() or 1, 12) if kind == "reference" else (os.cpu_count() or 1)
+    data = []
+    for i, (o, n) in enumerate(SHAPES):
+        data.append((synth.random_weights_fast(12, o, n, seed=10 + i), synth.random_activations(n, seed=20 + i), o))
+    total_bytes, total_t, reps = 0, 0.0, 0
+    t_end = time.time() + seconds
+    while time.time() < t_end or reps == 0:
+        for w, x, o in data:
+            t0 = time.perf_counter()
+            impl.matvec(w, 12, x, o)
+            total_t += time.perf_counter() - t0
+            total_bytes += algo_bytes(12, o, x.size)
+        reps += 1
+    return {"value": total_bytes / total_t / 1e9, "unit": "GB/s", "cores": cores, "kind": kind,
+            "sample": f"{reps} passes over the Q4_K sweep (all four shapes), {total_t:.1f} s of CPU time"}
+
+
+def run_reference(args) -> None:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from gncx_b200 import synth
+    from oracle.oracle import REF_NATIVE_SO, Oracle, RefLib
+    kind = "reference" if REF_NATIVE_SO.exists() else "port"
+    impl = RefLib(REF_NATIVE_SO) if kind == "reference" else Oracle()
+    cores = min(os.cpu_count() or 1, 12) if kind == "reference" else (os.cpu_count() or 1)
+    data = [(synth.random_weights_fast(12, o, n, seed=10 + i), synth.random_activations(n, seed=20 + i), o)
+            for i, (o, n) in enumerate(SHAPES)]
+    step_bytes = sum(algo_bytes(12, o, x.size) for _, x, o in data)
+    for _ in range(args.warmup):
+        for w, x, o in data:
+            impl.matvec(w, 12, x, o)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for w, x, o in data:
+            impl.matvec(w, 12, x, o)
+    dt = time.perf_counter() - t0
+    value = step_bytes * args.steps / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q4_k weights, int8 x int8 dots, f32 accumulate",
+        "data": "synthetic (seeded GGUF Q4_K blocks, x ~ N(0,1))",
+        "config": {"workload": "Q4_K GEMV sweep 4096x4096, 4096x12288, 12288x4096, 151936x4096 (out x in), batch 1",
+                   "l2": "inputs larger than L2 (417 MB of weights per step)"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind,
+                         "sample": f"{args.steps} full passes over the sweep"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_gpu(args) -> None:
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    from gncx_b200 import core
+    lib = core.load()
+    stream = torch.cuda.current_stream()
+    lib.gncx_set_stream(stream.cuda_stream)
+    lib.gncx_set_synchronous(0)
+    core.check(lib)
+
+    def P(t):
+        return ctypes.c_void_p(t.data_ptr())
+
+    # ---- data resident in HBM
+    weights = [gen_weights_gpu(torch, 12, o, n, seed=1000 * rank + i) for i, (o, n) in enumerate(SHAPES)]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7 + rank)
+    xs = [torch.randn(n, device="cuda", generator=g) for (_, n) in SHAPES]
+    ys = [torch.empty(o, device="cuda") for (o, _) in SHAPES]
+    step_bytes = sum(algo_bytes(12, o, n) for (o, n) in SHAPES)
+    big = len(SHAPES) - 1
+    big_bytes = algo_bytes(12, *SHAPES[big])
+
+    def launch(i):
+        o, n = SHAPES[i]
+        lib.gncx_xfold_universal_matvec(P(weights[i]), 0, 12, P(xs[i]), None, n, o, P(ys[i]), None)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        for i in range(len(SHAPES)):
+            launch(i)
+    core.check(lib)
+    barrier()
+
+    ev_big = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    sampler = ClockSampler(local)
+    time.sleep(0.05)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    start.record(stream)
+    for s in range(args.steps):
+        for i in range(len(SHAPES)):
+            if i == big:
+                ev_big[s][0].record(stream)
+                launch(i)
+                ev_big[s][1].record(stream)
+            else:
+                launch(i)
+    stop.record(stream)
+    barrier()
+    clocks = sampler.stop()
+    core.check(lib)
+    ms = start.elapsed_time(stop)
+    big_ms = statistics.mean(a.elapsed_time(b) for a, b in ev_big)
+    launches = args.steps * len(SHAPES)
+
+    # ---- end to end through the same entry point with host buffers
+    hx = [torch.empty(n, dtype=torch.float32).pin_memory() for (_, n) in SHAPES]
+    hy = [torch.empty(o, dtype=torch.float32).pin_memory() for (o, _) in SHAPES]
+    for i in range(len(SHAPES)):
+        hx[i].copy_(xs[i].cpu())
+    e2e_steps = max(1, min(args.steps, 200))
+
+    def e2e_step():
+        for i in range(len(SHAPES)):
+            xs[i].copy_(hx[i], non_blocking=True)
+            launch(i)
+            hy[i].copy_(ys[i], non_blocking=True)
+
+    for _ in range(min(3, args.warmup)):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    core.check(lib)
+
+    # ---- max over ranks
+    t = torch.tensor([ms, e2e_ms, big_ms], device="cuda")
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms, e2e_ms, big_ms = t.tolist()
+
+    if rank == 0:
+        peaks = measured_peaks()
+        peak = float(peaks.get("hbm_gbs", 6650.0))
+        peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+        value = step_bytes * args.steps * world / (ms / 1e3) / 1e9
+        achieved = big_bytes / (big_ms / 1e3) / 1e9
+        h2d = sum(4 * n for (_, n) in SHAPES)
+        d2h = sum(4 * o for (o, _) in SHAPES)
+        traffic = read_traffic()
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4_k weights, int8 x int8 dots, f32 accumulate",
+            "data": "synthetic (seeded GGUF Q4_K blocks generated on device, x ~ N(0,1))",
+            "config": {"workload": "Q4_K GEMV sweep 4096x4096, 4096x12288, 12288x4096, 151936x4096 (out x in), "
+                                   "batch 1, one matvec call per shape per step",
+                       "l2": "inputs larger than L2 (417 MB of weights per step)",
+                       "parallelism": f"replicas x{world} (rows shard with no exchange)",
+                       "pct_of_hbm_peak": value / world / peak},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "gemv_kernel<Q4_K> 151936x4096", "peak_source": peak_src,
+                         "algorithmic_bytes_per_launch": big_bytes},
+            "e2e": {"value": step_bytes * e2e_steps * world / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "gncx_xfold_universal_matvec, x from pinned host, y back to pinned host"},
+            "gpu_launches": launches,
+            "clocks": clocks,
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="gncx", choices=["gncx", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()
