@@ -203,6 +203,34 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def format_sweep(torch, lib, P, reps: int = 20) -> dict:
+    """GB/s of every format x shape of the GEMV sweep (each timed alone, L2
+    flushed between repetitions by a 256 MB write)."""
+    names = {2: "Q4_0", 8: "Q8_0", 12: "Q4_K", 14: "Q6_K"}
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    res = {}
+    stream = torch.cuda.current_stream()
+    for t in SWEEP_TYPES:
+        for i, (o, n) in enumerate(SHAPES):
+            w = gen_weights_gpu(torch, t, o, n, seed=77 + i)
+            x = torch.randn(n, device="cuda")
+            y = torch.empty(o, device="cuda")
+            times = []
+            for r in range(reps + 2):
+                flush.fill_(float(r))
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                lib.gncx_xfold_universal_matvec(P(w), 0, t, P(x), None, n, o, P(y), None)
+                b.record(stream)
+                torch.cuda.synchronize()
+                if r >= 2:
+                    times.append(a.elapsed_time(b))
+            ms = statistics.median(times)
+            res[f"{names[t]} {o}x{n}"] = {"us": ms * 1e3, "GB/s": algo_bytes(t, o, n) / (ms / 1e3) / 1e9}
+            del w
+    return res
+
+
 def run_gpu(args) -> None:
     import torch
     rank, world, local = dist_env()
@@ -217,8 +245,7 @@ def run_gpu(args) -> None:
         pg = dist
     from gncx_b200 import core
     lib = core.load()
-    stream = torch.cuda.current_stream()
-    lib.gncx_set_stream(stream.cuda_stream)
+    stream = core.bind_torch_stream(lib)
     lib.gncx_set_synchronous(0)
     core.check(lib)
 
@@ -333,6 +360,8 @@ def run_gpu(args) -> None:
             "gpu_launches": launches,
             "clocks": clocks,
         }
+        if not args.no_sweep:
+            line["sweep"] = format_sweep(torch, lib, P)
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
         print(json.dumps(line), flush=True)
@@ -344,11 +373,12 @@ def run_gpu(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="gncx", choices=["gncx", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the per-format sweep table")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

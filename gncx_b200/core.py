@@ -138,6 +138,25 @@ def check(lib: ctypes.CDLL | None = None) -> None:
         raise GncxError(code, msg)
 
 
+def bind_torch_stream(lib: ctypes.CDLL | None = None, device: int | None = None):
+    """Make torch and the library enqueue on one stream.
+
+    torch's default stream has handle 0, which the library reads as "use my
+    own stream"; so a dedicated stream is created, made torch's current
+    stream and handed to the library.  Returns the torch stream.
+    """
+    import torch
+
+    lib = lib or load()
+    if device is not None:
+        torch.cuda.set_device(device)
+    s = torch.cuda.Stream()
+    torch.cuda.set_stream(s)
+    lib.gncx_set_stream(ctypes.c_void_p(s.cuda_stream))
+    check(lib)
+    return s
+
+
 def exported_symbols(lib: ctypes.CDLL | None = None) -> list[str]:
     lib = lib or load()
     return [n for n in _SIGS if getattr(lib, n, None) is not None]

@@ -50,8 +50,7 @@ def gpu():
     lib = core.load()
     torch.cuda.init()
     lib.gncx_set_synchronous(1)
-    lib.gncx_set_stream(torch.cuda.current_stream().cuda_stream)
-    core.check(lib)
+    core.bind_torch_stream(lib)
     return lib
 
 
