@@ -247,6 +247,7 @@ def run_gpu(args) -> None:
     lib = core.load()
     stream = core.bind_torch_stream(lib)
     lib.gncx_set_synchronous(0)
+    lib.gncx_set_weight_prefetch(0 if args.no_prefetch else 1)
     core.check(lib)
 
     def P(t):
@@ -349,6 +350,7 @@ def run_gpu(args) -> None:
                                    "batch 1, one matvec call per shape per step",
                        "l2": "inputs larger than L2 (417 MB of weights per step)",
                        "parallelism": f"replicas x{world} (rows shard with no exchange)",
+                       "weight_prefetch": not args.no_prefetch,
                        "pct_of_hbm_peak": value / world / peak},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
@@ -361,6 +363,7 @@ def run_gpu(args) -> None:
             "clocks": clocks,
         }
         if not args.no_sweep:
+            lib.gncx_set_weight_prefetch(0)  # each sweep entry is timed alone
             line["sweep"] = format_sweep(torch, lib, P)
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
@@ -379,6 +382,8 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the per-format sweep table")
+    ap.add_argument("--no-prefetch", action="store_true",
+                    help="disable weight prefetch across kernel boundaries (programmatic dependent launch)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

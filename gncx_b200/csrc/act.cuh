@@ -12,17 +12,20 @@ namespace gncx {
 // memory; its 16-byte chunk k (k = 2*block + half) is stored at chunk
 // position k ^ (unit & 7), so eight consecutive units reading the same chunk
 // hit eight different bank groups.
+// The per-block scalars live in 16-byte records {d, sum_lo, sum_hi, sum_q},
+// record j of unit u at position u*8 + (j ^ (u & 7)) (same bank spreading).
 struct ActView {
-    const int8_t* qs;  // [units*256], swizzled
-    const float* d;    // [blocks]
-    const int2* s;     // [blocks] (sum of quants 0..15, sum of quants 16..31)
+    const int8_t* qs;   // [units*256], swizzled
+    const float4* rec;  // [units*8], swizzled
 };
 
 __device__ __forceinline__ int act_chunk_pos(int u, int k) { return u * 256 + 16 * (k ^ (u & 7)); }
+__device__ __forceinline__ int act_rec_pos(int b) { return (b & ~7) | ((b & 7) ^ ((b >> 3) & 7)); }
 
 __device__ __forceinline__ uint4 act_chunk(const ActView& a, int u, int k) {
     return *reinterpret_cast<const uint4*>(a.qs + act_chunk_pos(u, k));
 }
+__device__ __forceinline__ float4 act_rec(const ActView& a, int b) { return a.rec[act_rec_pos(b)]; }
 
 // Quantize one 32-input block; returns the 8 packed quant words.
 __device__ __forceinline__ void quantize_block32(const float (&v)[32], uint32_t (&q)[8], float& d, int& lo, int& hi) {
@@ -67,28 +70,70 @@ __device__ __forceinline__ void load_block32(const float* x, bool vec16, float (
     }
 }
 
-// Stage act blocks for `in_dim` inputs into shared memory (thread-strided).
-__device__ __forceinline__ void stage_act_fp32(const float* __restrict__ x, int in_dim, int8_t* qs, float* d,
-                                               int2* s, int tid, int nthreads) {
+// Stage act blocks for `in_dim` inputs into shared memory.  Four threads
+// quantize one 32-input block (8 inputs each; amax and sums via shuffles).
+// Must be called by a multiple of 32 threads, all of them.
+__device__ __forceinline__ void stage_act_fp32(const float* __restrict__ x, int in_dim, int8_t* qs, float4* rec,
+                                               int tid, int nthreads) {
     const int nb = in_dim >> 5;
     const bool vec = (((uintptr_t)x) & 15) == 0;
-    for (int b = tid; b < nb; b += nthreads) {
-        float v[32];
-        load_block32(x + (size_t)b * 32, vec, v);
-        uint32_t q[8];
-        float dd;
-        int lo, hi;
-        quantize_block32(v, q, dd, lo, hi);
-        const int u = b >> 3, j = b & 7;
-        *reinterpret_cast<uint4*>(qs + act_chunk_pos(u, 2 * j)) = make_uint4(q[0], q[1], q[2], q[3]);
-        *reinterpret_cast<uint4*>(qs + act_chunk_pos(u, 2 * j + 1)) = make_uint4(q[4], q[5], q[6], q[7]);
-        d[b] = dd;
-        s[b] = make_int2(lo, hi);
+    const int q4 = tid & 3;
+    for (int base = tid >> 2; base < ((nb + (nthreads >> 2) - 1) / (nthreads >> 2)) * (nthreads >> 2);
+         base += nthreads >> 2) {
+        const int b = base;
+        const bool ok = b < nb;
+        float v[8];
+        if (ok) {
+            const float* src = x + (size_t)b * 32 + q4 * 8;
+            if (vec) {
+                const float4 t0 = reinterpret_cast<const float4*>(src)[0];
+                const float4 t1 = reinterpret_cast<const float4*>(src)[1];
+                v[0] = t0.x; v[1] = t0.y; v[2] = t0.z; v[3] = t0.w; v[4] = t1.x; v[5] = t1.y; v[6] = t1.z; v[7] = t1.w;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = src[i];
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        uint32_t w0 = 0, w1 = 0;
+        int part = 0;
+        float d = 0.0f;
+        if (amax != 0.0f) {
+            const float inv = fdiv(127.0f, amax);
+            d = fdiv(amax, 127.0f);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int qv = __float2int_rn(fmul(v[i], inv));
+                part += qv;
+                if (i < 4) w0 |= ((uint32_t)qv & 0xFFu) << (8 * i);
+                else w1 |= ((uint32_t)qv & 0xFFu) << (8 * (i - 4));
+            }
+        }
+        // lanes q4 = 0,1 hold inputs 0..15, lanes 2,3 inputs 16..31
+        const int pair = part + __shfl_xor_sync(0xffffffffu, part, 1);
+        const int other = __shfl_xor_sync(0xffffffffu, pair, 2);
+        if (ok) {
+            const int u = b >> 3, j = b & 7;
+            // 8-byte piece q4 of the block's 32 quants: chunk 2j + (q4 >> 1), half (q4 & 1)
+            uint2* dst = reinterpret_cast<uint2*>(qs + act_chunk_pos(u, 2 * j + (q4 >> 1)) + 8 * (q4 & 1));
+            *dst = make_uint2(w0, w1);
+            if (q4 == 0) {
+                const int lo = pair, hi = other;
+                rec[act_rec_pos(b)] = make_float4(d, __int_as_float(lo), __int_as_float(hi), __int_as_float(lo + hi));
+            }
+        }
     }
 }
 
-__device__ __forceinline__ void stage_act_blocks(const ActBlock* __restrict__ ab, int in_dim, int8_t* qs, float* d,
-                                                 int2* s, int tid, int nthreads) {
+__device__ __forceinline__ void stage_act_blocks(const ActBlock* __restrict__ ab, int in_dim, int8_t* qs, float4* rec,
+                                                 int tid, int nthreads) {
     const int nb = in_dim >> 5;
     for (int b = tid; b < nb; b += nthreads) {
         const uint4* src = reinterpret_cast<const uint4*>(ab + b);
@@ -96,8 +141,8 @@ __device__ __forceinline__ void stage_act_blocks(const ActBlock* __restrict__ ab
         const int u = b >> 3, j = b & 7;
         *reinterpret_cast<uint4*>(qs + act_chunk_pos(u, 2 * j)) = src[1];
         *reinterpret_cast<uint4*>(qs + act_chunk_pos(u, 2 * j + 1)) = src[2];
-        d[b] = __uint_as_float(h.x);
-        s[b] = make_int2((int)h.y, (int)h.z);
+        rec[act_rec_pos(b)] = make_float4(__uint_as_float(h.x), __uint_as_float(h.y), __uint_as_float(h.z),
+                                          __int_as_float((int)h.y + (int)h.z));
     }
 }
 

@@ -240,6 +240,8 @@ void* gncx_get_stream(void) {
 
 void gncx_set_synchronous(int32_t on) { g_rt.synchronous = on != 0; }
 
+void gncx_set_weight_prefetch(int32_t on) { gemv_set_pdl(on != 0); }
+
 int32_t gncx_device_count(void) {
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess) {

@@ -25,10 +25,7 @@
 
 namespace gncx {
 
-constexpr int kRows = 32;           // rows per tile (4 per compute warp)
-constexpr int kUnitsPerChunk = 8;   // units per row per stage (one per lane)
-constexpr int kComputeWarps = 8;
-constexpr int kGemvThreads = (kComputeWarps + 1) * 32;
+constexpr int kMaxLanesPerRow = 8;  // units per row per stage (one per lane of a row group)
 
 struct GemvArgs {
     const uint8_t* w;
@@ -38,9 +35,10 @@ struct GemvArgs {
     float* y;
     int in_dim, out_dim;
     int upr;                // units per row (in_dim / 256)
-    int upc;                // units per chunk (min(8, upr))
-    int n_chunks;           // ceil(upr / upc)
-    int n_tiles;            // ceil(out_dim / 32)
+    int lpr;                // lanes per row = units per stage (1, 2, 4 or 8)
+    int rows;               // rows per tile = compute threads / lpr
+    int n_chunks;           // ceil(upr / lpr)
+    int n_tiles;            // ceil(out_dim / rows)
     int slot;               // shared bytes per row slot
     int stages;
     float softcap;
@@ -51,20 +49,19 @@ struct GemvSmem {
     uint64_t* full;
     uint64_t* empty;
     int8_t* qs;
-    float* d;
-    int2* s;
+    float4* rec;
     uint8_t* stage0;
 };
 
 __host__ __device__ inline size_t gemv_act_bytes(int in_dim) {
     const int nb = in_dim / 32;
-    return (size_t)in_dim + (size_t)nb * 4 + (size_t)nb * 8;
+    return (size_t)in_dim + (size_t)nb * 16;
 }
 
-__host__ __device__ inline size_t gemv_smem_bytes(int in_dim, int slot, int stages) {
+__host__ __device__ inline size_t gemv_smem_bytes(int in_dim, int rows, int slot, int stages) {
     size_t off = 128;  // barriers
     off += (gemv_act_bytes(in_dim) + 127) & ~(size_t)127;
-    off += (size_t)stages * kRows * slot;
+    off += (size_t)stages * rows * slot;
     return off;
 }
 
@@ -73,40 +70,47 @@ __device__ inline GemvSmem carve(uint8_t* base, int in_dim, int stages) {
     s.full = reinterpret_cast<uint64_t*>(base);
     s.empty = s.full + stages;
     uint8_t* p = base + 128;
-    const int nb = in_dim / 32;
     s.qs = reinterpret_cast<int8_t*>(p);
-    s.d = reinterpret_cast<float*>(p + in_dim);
-    s.s = reinterpret_cast<int2*>(p + in_dim + nb * 4);
+    s.rec = reinterpret_cast<float4*>(p + in_dim);
     s.stage0 = base + 128 + ((gemv_act_bytes(in_dim) + 127) & ~(size_t)127);
     return s;
 }
 
-template <int T, bool ALIGNED, bool PREQ>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs args) {
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// CW compute warps + 1 producer warp.  With programmatic dependent launch the
+// producer streams weights before the preceding kernel on the stream has
+// finished; everything that touches x or y waits for it (griddepcontrol.wait).
+template <int T, bool ALIGNED, bool PREQ, int CW>
+__global__ void __launch_bounds__((CW + 1) * 32, 1) gemv_kernel(const GemvArgs args) {
     constexpr int UB = Fmt<T>::UB, NW = Fmt<T>::NW, E = Fmt<T>::E;
+    constexpr int CT = CW * 32;
     extern __shared__ __align__(128) uint8_t smem[];
     const GemvSmem sm = carve(smem, args.in_dim, args.stages);
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int S = args.stages;
+    const int R = args.rows;
     __shared__ int abort_flag;
 
     if (tid == 0) {
         for (int i = 0; i < S; ++i) {
             mbar_init(&sm.full[i], 1);
-            mbar_init(&sm.empty[i], kComputeWarps);
+            mbar_init(&sm.empty[i], CW);
         }
         abort_flag = 0;
         fence_barrier_init();
     }
     __syncthreads();
+    pdl_launch_dependents();
 
-    if (warp == kComputeWarps) {
-        // ---------------- producer warp ----------------
+    if (warp == CW) {
+        // ---------------- producer warp: one bulk copy per row segment ----------------
         int item = 0;
         for (int tile = blockIdx.x; tile < args.n_tiles; tile += gridDim.x) {
-            const int row0 = tile * kRows;
-            const int nr = min(kRows, args.out_dim - row0);
+            const int row0 = tile * R;
+            const int nr = min(R, args.out_dim - row0);
             for (int c = 0; c < args.n_chunks; ++c, ++item) {
                 const int s = item % S;
                 const int use = item / S;
@@ -119,23 +123,26 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs ar
                         goto producer_done;
                     }
                 }
-                const int u0 = c * args.upc;
-                const int nu = min(args.upc, args.upr - u0);
-                uint32_t bytes = 0;
-                const uint8_t* src = nullptr;
-                if (lane < nr) {
-                    const uint8_t* seg = args.w + (size_t)(row0 + lane) * args.rb + (size_t)u0 * UB;
+                const int u0 = c * args.lpr;
+                const int nu = min(args.lpr, args.upr - u0);
+                uint32_t total = 0;
+                for (int r = lane; r < nr; r += 32) {
+                    const uint8_t* seg = args.w + (size_t)(row0 + r) * args.rb + (size_t)u0 * UB;
                     const uintptr_t a = (uintptr_t)seg & ~(uintptr_t)15;
                     const uintptr_t e = ((uintptr_t)seg + (uintptr_t)nu * UB + 15) & ~(uintptr_t)15;
-                    src = reinterpret_cast<const uint8_t*>(a);
-                    bytes = (uint32_t)(e - a);
+                    total += (uint32_t)(e - a);
                 }
-                uint32_t total = bytes;
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
                 if (lane == 0) mbar_arrive_expect_tx(&sm.full[s], total);
                 __syncwarp();
-                if (lane < nr) bulk_g2s(sm.stage0 + ((size_t)s * kRows + lane) * args.slot, src, bytes, &sm.full[s]);
+                for (int r = lane; r < nr; r += 32) {
+                    const uint8_t* seg = args.w + (size_t)(row0 + r) * args.rb + (size_t)u0 * UB;
+                    const uintptr_t a = (uintptr_t)seg & ~(uintptr_t)15;
+                    const uintptr_t e = ((uintptr_t)seg + (uintptr_t)nu * UB + 15) & ~(uintptr_t)15;
+                    bulk_g2s(sm.stage0 + ((size_t)s * R + r) * args.slot, reinterpret_cast<const void*>(a),
+                             (uint32_t)(e - a), &sm.full[s]);
+                }
             }
         }
     producer_done:
@@ -150,20 +157,22 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs ar
     }
 
     // ---------------- compute warps ----------------
-    if (PREQ) stage_act_blocks(args.act, args.in_dim, sm.qs, sm.d, sm.s, tid, kComputeWarps * 32);
-    else stage_act_fp32(args.x, args.in_dim, sm.qs, sm.d, sm.s, tid, kComputeWarps * 32);
-    asm volatile("bar.sync 1, %0;" ::"r"(kComputeWarps * 32) : "memory");
-    const ActView av{sm.qs, sm.d, sm.s};
+    pdl_wait();  // x / act and y belong to the preceding kernel's world from here on
+    if (PREQ) stage_act_blocks(args.act, args.in_dim, sm.qs, sm.rec, tid, CT);
+    else stage_act_fp32(args.x, args.in_dim, sm.qs, sm.rec, tid, CT);
+    asm volatile("bar.sync 1, %0;" ::"r"(CT) : "memory");
+    const ActView av{sm.qs, sm.rec};
 
-    const int rloc = tid >> 3;       // row within tile, 0..31
-    const int unit = tid & 7;        // unit within chunk
-    const int gbase = lane & ~7;     // first lane of this row's group
+    const int lpr = args.lpr;
+    const int rloc = tid / lpr;          // row within tile
+    const int unit = tid - rloc * lpr;   // unit within chunk
+    const int gbase = lane - unit;       // first lane of this row's group
     const float inv_cap = args.softcap > 0.0f ? fdiv(1.0f, args.softcap) : 0.0f;
 
     int item = 0;
     for (int tile = blockIdx.x; tile < args.n_tiles; tile += gridDim.x) {
-        const int row0 = tile * kRows;
-        const int nr = min(kRows, args.out_dim - row0);
+        const int row0 = tile * R;
+        const int nr = min(R, args.out_dim - row0);
         const bool row_ok = rloc < nr;
         float acc = 0.0f;
         for (int c = 0; c < args.n_chunks; ++c, ++item) {
@@ -174,14 +183,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs ar
                 atomicExch(&abort_flag, 1);
             }
             if (*(volatile int*)&abort_flag) return;
-            const int u0 = c * args.upc;
-            const int nu = min(args.upc, args.upr - u0);
+            const int u0 = c * lpr;
+            const int nu = min(lpr, args.upr - u0);
             float t[E];
 #pragma unroll
             for (int e = 0; e < E; ++e) t[e] = 0.0f;
             if (row_ok && unit < nu) {
                 const uint8_t* seg = args.w + (size_t)(row0 + rloc) * args.rb + (size_t)u0 * UB;
-                const uint8_t* p = sm.stage0 + ((size_t)s * kRows + rloc) * args.slot + ((uintptr_t)seg & 15) +
+                const uint8_t* p = sm.stage0 + ((size_t)s * R + rloc) * args.slot + ((uintptr_t)seg & 15) +
                                    (size_t)unit * UB;
                 uint32_t wv[NW];
                 load_unit_smem<NW, ALIGNED>(p, wv);
@@ -195,7 +204,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs ar
 #pragma unroll
                     for (int e = 0; e < E; ++e) acc = fadd(acc, t[e]);
                 }
-                acc = __shfl_sync(0xffffffffu, acc, gbase | u);
+                acc = __shfl_sync(0xffffffffu, acc, gbase + u);
             }
         }
         if (row_ok && unit == 0) {
@@ -231,27 +240,45 @@ __global__ void gemv_bf16_kernel(const uint8_t* __restrict__ w, size_t rb, const
 
 // ---------------- host launch ----------------
 
-template <int T, bool ALIGNED, bool PREQ>
+static bool g_pdl = false;
+void gemv_set_pdl(bool on) { g_pdl = on; }
+
+template <int T, bool ALIGNED, bool PREQ, int CW>
 static int launch_t(const GemvArgs& a, size_t smem, int grid, cudaStream_t st) {
-    auto k = gemv_kernel<T, ALIGNED, PREQ>;
+    auto k = gemv_kernel<T, ALIGNED, PREQ, CW>;
     static int configured_bytes = 0;  // per instantiation, per process (single device at a time)
     if ((int)smem > configured_bytes) {
         if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return kErrCuda;
         configured_bytes = (int)smem;
     }
-    k<<<grid, kGemvThreads, smem, st>>>(a);
-    return cudaPeekAtLastError() == cudaSuccess ? kOk : kErrCuda;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3((CW + 1) * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = g_pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, a) == cudaSuccess ? kOk : kErrCuda;
 }
 
-template <int T>
+template <int T, int CW>
 static int launch_fmt(const GemvArgs& a, bool aligned, bool preq, size_t smem, int grid, cudaStream_t st) {
     if (aligned) {
         if constexpr (T != kQ6_K) {
-            return preq ? launch_t<T, true, true>(a, smem, grid, st) : launch_t<T, true, false>(a, smem, grid, st);
+            return preq ? launch_t<T, true, true, CW>(a, smem, grid, st) : launch_t<T, true, false, CW>(a, smem, grid, st);
         }
     }
-    return preq ? launch_t<T, false, true>(a, smem, grid, st) : launch_t<T, false, false>(a, smem, grid, st);
+    return preq ? launch_t<T, false, true, CW>(a, smem, grid, st) : launch_t<T, false, false, CW>(a, smem, grid, st);
+}
+
+template <int T>
+static int launch_cw(const GemvArgs& a, int cw, bool aligned, bool preq, size_t smem, int grid, cudaStream_t st) {
+    return cw == 16 ? launch_fmt<T, 16>(a, aligned, preq, smem, grid, st)
+                    : launch_fmt<T, 8>(a, aligned, preq, smem, grid, st);
 }
 
 int gemv_launch(const uint8_t* w, int32_t type, const float* x, const ActBlock* act, int32_t in_dim,
@@ -284,26 +311,36 @@ int gemv_launch(const uint8_t* w, int32_t type, const float* x, const ActBlock* 
     a.in_dim = in_dim;
     a.out_dim = out_dim;
     a.upr = in_dim / 256;
-    a.upc = a.upr < kUnitsPerChunk ? a.upr : kUnitsPerChunk;
-    a.n_chunks = (a.upr + a.upc - 1) / a.upc;
-    a.n_tiles = (out_dim + kRows - 1) / kRows;
-    a.slot = ((a.upc * ub + 15) & ~15) + 32;
+    a.lpr = a.upr >= 8 ? 8 : a.upr >= 4 ? 4 : a.upr >= 2 ? 2 : 1;
+    a.n_chunks = (a.upr + a.lpr - 1) / a.lpr;
+    a.slot = ((a.lpr * ub + 15) & ~15) + 32;
     a.softcap = softcap;
     a.err = err;
     const size_t budget = (size_t)dev.max_smem_optin;
-    int stages = 4;
-    while (stages > 2 && gemv_smem_bytes(in_dim, a.slot, stages) > budget) --stages;
-    if (gemv_smem_bytes(in_dim, a.slot, stages) > budget) return kErrCapacity;
+    // Prefer 16 compute warps (latency hiding) with >= 2 stages; fall back to 8.
+    int cw = 16, stages = 0;
+    for (cw = 16; cw >= 8; cw >>= 1) {
+        const int rows = cw * 32 / a.lpr;
+        stages = 4;
+        while (stages > 2 && gemv_smem_bytes(in_dim, rows, a.slot, stages) > budget) --stages;
+        // few rows: more CTAs beat deeper CTAs
+        const int tiles = (out_dim + rows - 1) / rows;
+        if (gemv_smem_bytes(in_dim, rows, a.slot, stages) <= budget && (cw == 8 || tiles >= dev.sm_count)) break;
+    }
+    if (cw < 8) cw = 8;
+    a.rows = cw * 32 / a.lpr;
     a.stages = stages;
-    const size_t smem = gemv_smem_bytes(in_dim, a.slot, stages);
+    if (gemv_smem_bytes(in_dim, a.rows, a.slot, stages) > budget) return kErrCapacity;
+    a.n_tiles = (out_dim + a.rows - 1) / a.rows;
+    const size_t smem = gemv_smem_bytes(in_dim, a.rows, a.slot, stages);
     const int grid = a.n_tiles < dev.sm_count ? a.n_tiles : dev.sm_count;
     const bool aligned = ((uintptr_t)w % 16 == 0) && (a.rb % 16 == 0) && (ub % 16 == 0);
     const bool preq = act != nullptr;
     switch (type) {
-        case kQ4_0: return launch_fmt<kQ4_0>(a, aligned, preq, smem, grid, st);
-        case kQ8_0: return launch_fmt<kQ8_0>(a, aligned, preq, smem, grid, st);
-        case kQ4_K: return launch_fmt<kQ4_K>(a, aligned, preq, smem, grid, st);
-        default: return launch_fmt<kQ6_K>(a, aligned, preq, smem, grid, st);
+        case kQ4_0: return launch_cw<kQ4_0>(a, cw, aligned, preq, smem, grid, st);
+        case kQ8_0: return launch_cw<kQ8_0>(a, cw, aligned, preq, smem, grid, st);
+        case kQ4_K: return launch_cw<kQ4_K>(a, cw, aligned, preq, smem, grid, st);
+        default: return launch_cw<kQ6_K>(a, cw, aligned, preq, smem, grid, st);
     }
 }
 

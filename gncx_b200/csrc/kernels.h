@@ -20,6 +20,10 @@ const DeviceInfo& device_info();
 // ---- GEMV / prefill ----
 int gemv_launch(const uint8_t* w, int32_t type, const float* x, const ActBlock* act, int32_t in_dim,
                 int32_t out_dim, float* y, float softcap, int32_t* err, cudaStream_t st);
+// Programmatic dependent launch for the GEMV: its weight stream may start
+// before the preceding kernel on the stream completes (weights must not be
+// written by that kernel).  Off by default.
+void gemv_set_pdl(bool on);
 int matbatch_launch(const uint8_t* w, int32_t type, const float* xb, const ActBlock* act, int32_t batch,
                     int32_t in_dim, int32_t out_dim, float* yb, int32_t* err, cudaStream_t st);
 // x[rows][in_dim] -> ActBlock[rows][in_dim/32]

@@ -241,8 +241,11 @@ struct UnitAct {
     const ActView& a;
     int u;
     __device__ __forceinline__ uint4 chunk(int k) const { return act_chunk(a, u, k); }
-    __device__ __forceinline__ float d(int j) const { return a.d[u * 8 + j]; }
-    __device__ __forceinline__ int2 s(int j) const { return a.s[u * 8 + j]; }
+    __device__ __forceinline__ float d(int j) const { return act_rec(a, u * 8 + j).x; }
+    __device__ __forceinline__ int2 s(int j) const {
+        const float4 r = act_rec(a, u * 8 + j);
+        return make_int2(__float_as_int(r.y), __float_as_int(r.z));
+    }
 };
 
 // Format traits: unit bytes, words loaded per unit, terms per unit.

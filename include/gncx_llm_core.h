@@ -149,6 +149,11 @@ int32_t gncx_sync(void);                     /* wait for queued work; returns an
 void gncx_set_stream(void* cuda_stream);     /* NULL = the library's own stream */
 void* gncx_get_stream(void);
 void gncx_set_synchronous(int32_t on);       /* 1 (default): reference-named calls wait before returning */
+/* 1: a GEMV may start streaming its weights before the preceding kernel on
+ * the stream has finished (programmatic dependent launch); its activations
+ * and outputs still wait.  Only valid while weights are not written by GPU
+ * work queued just before the GEMV.  Default 0. */
+void gncx_set_weight_prefetch(int32_t on);
 int32_t gncx_device_count(void);
 int32_t gncx_set_device(int32_t device);
 

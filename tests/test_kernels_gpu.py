@@ -22,12 +22,30 @@ torch = pytest.importorskip("torch")
 ATTN_TOL = 1e-5
 
 
+# Every device buffer made here stays referenced until the test ends: a
+# temporary whose address went to the C ABI must not be freed (and its memory
+# handed to the next upload) before the kernel has read it.
+_KEEP: list = []
+
+
+@pytest.fixture(autouse=True)
+def _keep_buffers():
+    _KEEP.clear()
+    yield
+    torch.cuda.synchronize()
+    _KEEP.clear()
+
+
 def dev(a: np.ndarray):
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    _KEEP.append(t)
+    return t
 
 
 def out(n, dtype=torch.float32):
-    return torch.full((n,), float("nan"), dtype=dtype, device="cuda")
+    t = torch.full((n,), float("nan"), dtype=dtype, device="cuda")
+    _KEEP.append(t)
+    return t
 
 
 def P(t):
