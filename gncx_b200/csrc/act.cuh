@@ -23,9 +23,17 @@ __device__ __forceinline__ int act_chunk_pos(int u, int k) { return u * 256 + 16
 __device__ __forceinline__ int act_rec_pos(int b) { return (b & ~7) | ((b & 7) ^ ((b >> 3) & 7)); }
 
 __device__ __forceinline__ uint4 act_chunk(const ActView& a, int u, int k) {
-    return *reinterpret_cast<const uint4*>(a.qs + act_chunk_pos(u, k));
+    const uint32_t addr = (uint32_t)__cvta_generic_to_shared(a.qs) + act_chunk_pos(u, k);
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
 }
-__device__ __forceinline__ float4 act_rec(const ActView& a, int b) { return a.rec[act_rec_pos(b)]; }
+__device__ __forceinline__ float4 act_rec(const ActView& a, int b) {
+    const uint32_t addr = (uint32_t)__cvta_generic_to_shared(a.rec) + 16 * act_rec_pos(b);
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
 
 // Quantize one 32-input block; returns the 8 packed quant words.
 __device__ __forceinline__ void quantize_block32(const float (&v)[32], uint32_t (&q)[8], float& d, int& lo, int& hi) {

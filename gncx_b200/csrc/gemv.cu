@@ -17,6 +17,7 @@
 //     per-row accumulation bit for bit.
 // HBM traffic is the weight bytes once plus the (L2-resident) activation.
 #include <cuda_runtime.h>
+#include <stdlib.h>
 #include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
@@ -188,16 +189,18 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) gemv_kernel(const GemvArgs a
             float t[E];
 #pragma unroll
             for (int e = 0; e < E; ++e) t[e] = 0.0f;
-            if (row_ok && unit < nu) {
+            uint32_t wv[NW];
+            const bool have = row_ok && unit < nu;
+            if (have) {
                 const uint8_t* seg = args.w + (size_t)(row0 + rloc) * args.rb + (size_t)u0 * UB;
                 const uint8_t* p = sm.stage0 + ((size_t)s * R + rloc) * args.slot + ((uintptr_t)seg & 15) +
                                    (size_t)unit * UB;
-                uint32_t wv[NW];
                 load_unit_smem<NW, ALIGNED>(p, wv);
-                unit_terms<T>(wv, UnitAct{av, u0 + unit}, t);
             }
+            // the unit's bytes are in registers: hand the stage back before computing
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.empty[s]);
+            if (have) unit_terms<T>(wv, UnitAct{av, u0 + unit}, t);
             // Serial chain over this chunk's units, in unit order.
             for (int u = 0; u < nu; ++u) {
                 if (unit == u) {
@@ -242,6 +245,12 @@ __global__ void gemv_bf16_kernel(const uint8_t* __restrict__ w, size_t rb, const
 
 static bool g_pdl = false;
 void gemv_set_pdl(bool on) { g_pdl = on; }
+
+// Tuning overrides (GNCX_GEMV_WARPS = 8|16, GNCX_GEMV_STAGES = 2..4); read once.
+static int env_int(const char* name, int dflt) {
+    const char* v = getenv(name);
+    return v ? atoi(v) : dflt;
+}
 
 template <int T, bool ALIGNED, bool PREQ, int CW>
 static int launch_t(const GemvArgs& a, size_t smem, int grid, cudaStream_t st) {
@@ -318,14 +327,18 @@ int gemv_launch(const uint8_t* w, int32_t type, const float* x, const ActBlock* 
     a.err = err;
     const size_t budget = (size_t)dev.max_smem_optin;
     // Prefer 16 compute warps (latency hiding) with >= 2 stages; fall back to 8.
+    static const int force_cw = env_int("GNCX_GEMV_WARPS", 0);
+    static const int max_stages = env_int("GNCX_GEMV_STAGES", 4);
     int cw = 16, stages = 0;
-    for (cw = 16; cw >= 8; cw >>= 1) {
+    for (cw = (force_cw == 8 ? 8 : 16); cw >= 8; cw >>= 1) {
         const int rows = cw * 32 / a.lpr;
-        stages = 4;
+        stages = max_stages < 2 ? 2 : (max_stages > 4 ? 4 : max_stages);
         while (stages > 2 && gemv_smem_bytes(in_dim, rows, a.slot, stages) > budget) --stages;
         // few rows: more CTAs beat deeper CTAs
         const int tiles = (out_dim + rows - 1) / rows;
-        if (gemv_smem_bytes(in_dim, rows, a.slot, stages) <= budget && (cw == 8 || tiles >= dev.sm_count)) break;
+        if (gemv_smem_bytes(in_dim, rows, a.slot, stages) <= budget &&
+            (cw == 8 || force_cw == 16 || tiles >= dev.sm_count))
+            break;
     }
     if (cw < 8) cw = 8;
     a.rows = cw * 32 / a.lpr;

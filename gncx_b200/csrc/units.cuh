@@ -255,24 +255,35 @@ template <> struct Fmt<kQ8_0> { static constexpr int UB = 272, NW = 68, E = 8; }
 template <> struct Fmt<kQ4_K> { static constexpr int UB = 144, NW = 36, E = 1; };
 template <> struct Fmt<kQ6_K> { static constexpr int UB = 210, NW = 53, E = 1; };
 
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
 // Load NW words of a unit from shared memory at byte address p.
 template <int NW, bool ALIGNED>
 __device__ __forceinline__ void load_unit_smem(const uint8_t* p, uint32_t (&w)[NW]) {
+    const uint32_t sp = (uint32_t)__cvta_generic_to_shared(p);
     if constexpr (ALIGNED) {
         static_assert(NW % 4 == 0, "aligned unit loads need whole 16-byte chunks");
-        const uint4* q = reinterpret_cast<const uint4*>(p);
 #pragma unroll
         for (int i = 0; i < NW / 4; ++i) {
-            const uint4 t = q[i];
+            const uint4 t = lds128(sp + 16 * i);
             w[4 * i] = t.x; w[4 * i + 1] = t.y; w[4 * i + 2] = t.z; w[4 * i + 3] = t.w;
         }
     } else {
-        const uint32_t* a = reinterpret_cast<const uint32_t*>((uintptr_t)p & ~(uintptr_t)3);
-        const uint32_t sh = ((uint32_t)(uintptr_t)p & 3u) * 8u;
-        uint32_t prev = a[0];
+        const uint32_t a = sp & ~3u;
+        const uint32_t sh = (sp & 3u) * 8u;
+        uint32_t prev = lds32(a);
 #pragma unroll
         for (int i = 0; i < NW; ++i) {
-            const uint32_t nxt = a[i + 1];
+            const uint32_t nxt = lds32(a + 4 * (i + 1));
             w[i] = __funnelshift_r(prev, nxt, sh);
             prev = nxt;
         }
