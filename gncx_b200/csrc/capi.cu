@@ -61,6 +61,7 @@ const DeviceInfo& device_info() {
         d.device = dev;
         cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
         cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        cudaDeviceGetAttribute(&d.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
         cudaDeviceGetAttribute(&d.l2_bytes, cudaDevAttrL2CacheSize, dev);
     }
     return d;

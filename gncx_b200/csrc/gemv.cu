@@ -26,7 +26,7 @@
 
 namespace gncx {
 
-constexpr int kMaxLanesPerRow = 8;  // units per row per stage (one per lane of a row group)
+constexpr int kMaxUnitsPerLane = 2;
 
 struct GemvArgs {
     const uint8_t* w;
@@ -35,12 +35,11 @@ struct GemvArgs {
     const ActBlock* act;    // pre-quantized activations (PREQ == true)
     float* y;
     int in_dim, out_dim;
-    int upr;                // units per row (in_dim / 256)
-    int lpr;                // lanes per row = units per stage (1, 2, 4 or 8)
+    int upr;                // units (256 inputs) per row
+    int lpr;                // lanes per row (power of two, <= 32); lane j owns units j, j + lpr
     int rows;               // rows per tile = compute threads / lpr
-    int n_chunks;           // ceil(upr / lpr)
     int n_tiles;            // ceil(out_dim / rows)
-    int slot;               // shared bytes per row slot
+    int stage_bytes;        // shared bytes per stage (rows * rb + 32)
     int stages;
     float softcap;
     int32_t* err;
@@ -59,10 +58,10 @@ __host__ __device__ inline size_t gemv_act_bytes(int in_dim) {
     return (size_t)in_dim + (size_t)nb * 16;
 }
 
-__host__ __device__ inline size_t gemv_smem_bytes(int in_dim, int rows, int slot, int stages) {
+__host__ __device__ inline size_t gemv_smem_bytes(int in_dim, int stage_bytes, int stages) {
     size_t off = 128;  // barriers
     off += (gemv_act_bytes(in_dim) + 127) & ~(size_t)127;
-    off += (size_t)stages * rows * slot;
+    off += (size_t)stages * stage_bytes;
     return off;
 }
 
@@ -80,9 +79,12 @@ __device__ inline GemvSmem carve(uint8_t* base, int in_dim, int stages) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
-// CW compute warps + 1 producer warp.  With programmatic dependent launch the
-// producer streams weights before the preceding kernel on the stream has
-// finished; everything that touches x or y waits for it (griddepcontrol.wait).
+// One pipeline stage = one tile of `rows` consecutive whole rows, which are
+// contiguous in memory and arrive with a single bulk copy (its 16-byte-aligned
+// superset; an aligned 16-byte chunk never crosses a page).  CW compute warps
+// + 1 producer warp.  With programmatic dependent launch the producer streams
+// weights before the preceding kernel on the stream has finished; everything
+// that touches x or y waits for it (griddepcontrol.wait).
 template <int T, bool ALIGNED, bool PREQ, int CW>
 __global__ void __launch_bounds__((CW + 1) * 32, 1) gemv_kernel(const GemvArgs args) {
     constexpr int UB = Fmt<T>::UB, NW = Fmt<T>::NW, E = Fmt<T>::E;
@@ -107,52 +109,30 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) gemv_kernel(const GemvArgs a
     pdl_launch_dependents();
 
     if (warp == CW) {
-        // ---------------- producer warp: one bulk copy per row segment ----------------
+        // ---------------- producer warp: one bulk copy per tile ----------------
         int item = 0;
-        for (int tile = blockIdx.x; tile < args.n_tiles; tile += gridDim.x) {
-            const int row0 = tile * R;
-            const int nr = min(R, args.out_dim - row0);
-            for (int c = 0; c < args.n_chunks; ++c, ++item) {
+        if (lane == 0) {
+            for (int tile = blockIdx.x; tile < args.n_tiles; tile += gridDim.x, ++item) {
                 const int s = item % S;
                 const int use = item / S;
-                if (use > 0) {
-                    bool ok = true;
-                    if (lane == 0) ok = mbar_wait(&sm.empty[s], (use - 1) & 1);
-                    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-                    if (!ok) {
-                        if (lane == 0) { record_error(args.err, kErrTimeout); atomicExch(&abort_flag, 1); }
-                        goto producer_done;
-                    }
+                if (use > 0 && !mbar_wait(&sm.empty[s], (use - 1) & 1)) {
+                    record_error(args.err, kErrTimeout);
+                    atomicExch(&abort_flag, 1);
+                    break;
                 }
-                const int u0 = c * args.lpr;
-                const int nu = min(args.lpr, args.upr - u0);
-                uint32_t total = 0;
-                for (int r = lane; r < nr; r += 32) {
-                    const uint8_t* seg = args.w + (size_t)(row0 + r) * args.rb + (size_t)u0 * UB;
-                    const uintptr_t a = (uintptr_t)seg & ~(uintptr_t)15;
-                    const uintptr_t e = ((uintptr_t)seg + (uintptr_t)nu * UB + 15) & ~(uintptr_t)15;
-                    total += (uint32_t)(e - a);
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-                if (lane == 0) mbar_arrive_expect_tx(&sm.full[s], total);
-                __syncwarp();
-                for (int r = lane; r < nr; r += 32) {
-                    const uint8_t* seg = args.w + (size_t)(row0 + r) * args.rb + (size_t)u0 * UB;
-                    const uintptr_t a = (uintptr_t)seg & ~(uintptr_t)15;
-                    const uintptr_t e = ((uintptr_t)seg + (uintptr_t)nu * UB + 15) & ~(uintptr_t)15;
-                    bulk_g2s(sm.stage0 + ((size_t)s * R + r) * args.slot, reinterpret_cast<const void*>(a),
-                             (uint32_t)(e - a), &sm.full[s]);
-                }
+                const int row0 = tile * R;
+                const int nr = min(R, args.out_dim - row0);
+                const uint8_t* seg = args.w + (size_t)row0 * args.rb;
+                const uintptr_t a = (uintptr_t)seg & ~(uintptr_t)15;
+                const uintptr_t e = ((uintptr_t)seg + (uintptr_t)nr * args.rb + 15) & ~(uintptr_t)15;
+                mbar_arrive_expect_tx(&sm.full[s], (uint32_t)(e - a));
+                bulk_g2s(sm.stage0 + (size_t)s * args.stage_bytes, reinterpret_cast<const void*>(a), (uint32_t)(e - a),
+                         &sm.full[s]);
             }
-        }
-    producer_done:
-        // Wait (bounded) for every copy this warp issued before the CTA may exit.
-        if (lane == 0) {
+            // Wait (bounded) for every copy issued before the CTA may exit.
             const int issued = item;
-            for (int k = max(0, issued - S); k < issued; ++k) {
+            for (int k = max(0, issued - S); k < issued; ++k)
                 if (!mbar_wait(&sm.full[k % S], (k / S) & 1)) record_error(args.err, kErrTimeout);
-            }
         }
         return;
     }
@@ -166,51 +146,54 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) gemv_kernel(const GemvArgs a
 
     const int lpr = args.lpr;
     const int rloc = tid / lpr;          // row within tile
-    const int unit = tid - rloc * lpr;   // unit within chunk
-    const int gbase = lane - unit;       // first lane of this row's group
+    const int j = tid - rloc * lpr;      // lane within the row group
+    const int gbase = lane - j;          // first lane of this row's group
+    const int upr = args.upr;
     const float inv_cap = args.softcap > 0.0f ? fdiv(1.0f, args.softcap) : 0.0f;
 
     int item = 0;
-    for (int tile = blockIdx.x; tile < args.n_tiles; tile += gridDim.x) {
+    for (int tile = blockIdx.x; tile < args.n_tiles; tile += gridDim.x, ++item) {
+        const int s = item % S;
+        const int use = item / S;
+        if (!mbar_wait(&sm.full[s], use & 1)) {
+            record_error(args.err, kErrTimeout);
+            atomicExch(&abort_flag, 1);
+        }
+        if (*(volatile int*)&abort_flag) return;
         const int row0 = tile * R;
         const int nr = min(R, args.out_dim - row0);
         const bool row_ok = rloc < nr;
-        float acc = 0.0f;
-        for (int c = 0; c < args.n_chunks; ++c, ++item) {
-            const int s = item % S;
-            const int use = item / S;
-            if (!mbar_wait(&sm.full[s], use & 1)) {
-                record_error(args.err, kErrTimeout);
-                atomicExch(&abort_flag, 1);
-            }
-            if (*(volatile int*)&abort_flag) return;
-            const int u0 = c * lpr;
-            const int nu = min(lpr, args.upr - u0);
-            float t[E];
+        const uint8_t* tile_src = args.w + (size_t)row0 * args.rb;
+        const uint8_t* row_smem = sm.stage0 + (size_t)s * args.stage_bytes + ((uintptr_t)tile_src & 15) +
+                                  (size_t)rloc * args.rb;
+        float t[kMaxUnitsPerLane][E];
 #pragma unroll
-            for (int e = 0; e < E; ++e) t[e] = 0.0f;
-            uint32_t wv[NW];
-            const bool have = row_ok && unit < nu;
-            if (have) {
-                const uint8_t* seg = args.w + (size_t)(row0 + rloc) * args.rb + (size_t)u0 * UB;
-                const uint8_t* p = sm.stage0 + ((size_t)s * R + rloc) * args.slot + ((uintptr_t)seg & 15) +
-                                   (size_t)unit * UB;
-                load_unit_smem<NW, ALIGNED>(p, wv);
-            }
-            // the unit's bytes are in registers: hand the stage back before computing
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.empty[s]);
-            if (have) unit_terms<T>(wv, UnitAct{av, u0 + unit}, t);
-            // Serial chain over this chunk's units, in unit order.
-            for (int u = 0; u < nu; ++u) {
-                if (unit == u) {
+        for (int k = 0; k < kMaxUnitsPerLane; ++k) {
 #pragma unroll
-                    for (int e = 0; e < E; ++e) acc = fadd(acc, t[e]);
-                }
-                acc = __shfl_sync(0xffffffffu, acc, gbase + u);
+            for (int e = 0; e < E; ++e) t[k][e] = 0.0f;
+            const int u = j + k * lpr;
+            if (row_ok && u < upr) {
+                uint32_t wv[NW];
+                load_unit_smem<NW, ALIGNED>(row_smem + (size_t)u * UB, wv);
+                unit_terms<T>(wv, UnitAct{av, u}, t[k]);
             }
         }
-        if (row_ok && unit == 0) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[s]);
+        // Serial chain over the row's units in unit order (unit u = k*lpr + owner).
+        float acc = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kMaxUnitsPerLane; ++k) {
+            const int nj = min(lpr, upr - k * lpr);
+            for (int o = 0; o < nj; ++o) {
+                if (j == o) {
+#pragma unroll
+                    for (int e = 0; e < E; ++e) acc = fadd(acc, t[k][e]);
+                }
+                acc = __shfl_sync(0xffffffffu, acc, gbase + o);
+            }
+        }
+        if (row_ok && j == 0) {
             float v = acc;
             if (args.softcap > 0.0f) v = fmul(tanh_cr(fmul(v, inv_cap)), args.softcap);
             args.y[row0 + rloc] = v;
@@ -253,14 +236,24 @@ static int env_int(const char* name, int dflt) {
 }
 
 template <int T, bool ALIGNED, bool PREQ, int CW>
-static int launch_t(const GemvArgs& a, size_t smem, int grid, cudaStream_t st) {
+static int launch_t(const GemvArgs& a, size_t smem, int, cudaStream_t st) {
     auto k = gemv_kernel<T, ALIGNED, PREQ, CW>;
     static int configured_bytes = 0;  // per instantiation, per process (single device at a time)
+    static size_t occ_smem = 0;
+    static int occ_blocks = 1;
     if ((int)smem > configured_bytes) {
         if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return kErrCuda;
         configured_bytes = (int)smem;
     }
+    if (smem != occ_smem) {  // resident CTAs per SM for this shared-memory size (registers included)
+        int nb = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k, (CW + 1) * 32, smem) != cudaSuccess) nb = 1;
+        occ_blocks = nb < 1 ? 1 : nb;
+        occ_smem = smem;
+    }
+    const int max_grid = device_info().sm_count * occ_blocks;
+    const int grid = a.n_tiles < max_grid ? a.n_tiles : max_grid;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3((CW + 1) * 32);
@@ -286,8 +279,8 @@ static int launch_fmt(const GemvArgs& a, bool aligned, bool preq, size_t smem, i
 
 template <int T>
 static int launch_cw(const GemvArgs& a, int cw, bool aligned, bool preq, size_t smem, int grid, cudaStream_t st) {
-    return cw == 16 ? launch_fmt<T, 16>(a, aligned, preq, smem, grid, st)
-                    : launch_fmt<T, 8>(a, aligned, preq, smem, grid, st);
+    return cw == 8 ? launch_fmt<T, 8>(a, aligned, preq, smem, grid, st)
+                   : launch_fmt<T, 4>(a, aligned, preq, smem, grid, st);
 }
 
 int gemv_launch(const uint8_t* w, int32_t type, const float* x, const ActBlock* act, int32_t in_dim,
@@ -320,33 +313,33 @@ int gemv_launch(const uint8_t* w, int32_t type, const float* x, const ActBlock* 
     a.in_dim = in_dim;
     a.out_dim = out_dim;
     a.upr = in_dim / 256;
-    a.lpr = a.upr >= 8 ? 8 : a.upr >= 4 ? 4 : a.upr >= 2 ? 2 : 1;
-    a.n_chunks = (a.upr + a.lpr - 1) / a.lpr;
-    a.slot = ((a.lpr * ub + 15) & ~15) + 32;
+    // lanes per row: smallest power of two with <= 2 units per lane
+    int lpr = 1;
+    while (lpr < 32 && lpr * kMaxUnitsPerLane < a.upr) lpr <<= 1;
+    if (lpr * kMaxUnitsPerLane < a.upr) return kErrCapacity;  // in_dim > 16384
+    a.lpr = lpr;
     a.softcap = softcap;
     a.err = err;
     const size_t budget = (size_t)dev.max_smem_optin;
-    // Prefer 16 compute warps (latency hiding) with >= 2 stages; fall back to 8.
     static const int force_cw = env_int("GNCX_GEMV_WARPS", 0);
     static const int max_stages = env_int("GNCX_GEMV_STAGES", 4);
-    int cw = 16, stages = 0;
-    for (cw = (force_cw == 8 ? 8 : 16); cw >= 8; cw >>= 1) {
-        const int rows = cw * 32 / a.lpr;
+    // 8 compute warps unless that leaves SMs idle (then 4) or does not fit.
+    int cw = 8;
+    if (force_cw == 4 || force_cw == 8) cw = force_cw;
+    else if ((out_dim + 256 / lpr - 1) / (256 / lpr) < dev.sm_count) cw = 4;
+    int stages = 0;
+    for (;; cw >>= 1) {
+        a.rows = cw * 32 / lpr;
+        a.stage_bytes = (int)((((size_t)a.rows * a.rb + 15) & ~(size_t)15) + 32);
         stages = max_stages < 2 ? 2 : (max_stages > 4 ? 4 : max_stages);
-        while (stages > 2 && gemv_smem_bytes(in_dim, rows, a.slot, stages) > budget) --stages;
-        // few rows: more CTAs beat deeper CTAs
-        const int tiles = (out_dim + rows - 1) / rows;
-        if (gemv_smem_bytes(in_dim, rows, a.slot, stages) <= budget &&
-            (cw == 8 || force_cw == 16 || tiles >= dev.sm_count))
-            break;
+        while (stages > 2 && gemv_smem_bytes(in_dim, a.stage_bytes, stages) > budget) --stages;
+        if (gemv_smem_bytes(in_dim, a.stage_bytes, stages) <= budget || cw == 4) break;
     }
-    if (cw < 8) cw = 8;
-    a.rows = cw * 32 / a.lpr;
+    if (gemv_smem_bytes(in_dim, a.stage_bytes, stages) > budget) return kErrCapacity;
     a.stages = stages;
-    if (gemv_smem_bytes(in_dim, a.rows, a.slot, stages) > budget) return kErrCapacity;
     a.n_tiles = (out_dim + a.rows - 1) / a.rows;
-    const size_t smem = gemv_smem_bytes(in_dim, a.rows, a.slot, stages);
-    const int grid = a.n_tiles < dev.sm_count ? a.n_tiles : dev.sm_count;
+    const size_t smem = gemv_smem_bytes(in_dim, a.stage_bytes, stages);
+    const int grid = 0;  // chosen from the occupancy of the instantiation
     const bool aligned = ((uintptr_t)w % 16 == 0) && (a.rb % 16 == 0) && (ub % 16 == 0);
     const bool preq = act != nullptr;
     switch (type) {

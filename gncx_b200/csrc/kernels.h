@@ -12,6 +12,7 @@ struct DeviceInfo {
     int device = -1;
     int sm_count = 0;
     int max_smem_optin = 0;
+    int smem_per_sm = 0;
     int l2_bytes = 0;
 };
 // Properties of the current device (queried once per device).
