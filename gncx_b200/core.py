@@ -103,6 +103,18 @@ _SIGS = {
     "gncx_matvec_preq": (c_int32, [P, c_size_t, c_int32, P, c_int32, c_int32, P]),
     "gncx_dequantize_rows": (c_int32, [P, c_size_t, c_int32, c_int32, c_int32, P]),
     "gncx_sample_greedy": (c_int32, [P, c_int32, POINTER(c_int32), c_int32, c_double]),
+    # model engine
+    "gncx_engine_create": (c_void_p, [c_char_p, c_int32]),
+    "gncx_engine_destroy": (None, [c_void_p]),
+    "gncx_engine_hparams": (c_int32, [c_void_p, POINTER(c_int32)]),
+    "gncx_engine_error": (c_char_p, [c_void_p]),
+    "gncx_engine_stream": (c_void_p, [c_void_p]),
+    "gncx_engine_forward_token": (c_int32, [c_void_p, c_int32, c_int32, P]),
+    "gncx_engine_prefill": (c_int32, [c_void_p, POINTER(c_int32), c_int32, P]),
+    "gncx_engine_logits": (c_void_p, [c_void_p]),
+    "gncx_engine_generate": (c_int32, [c_void_p, POINTER(c_int32), c_int32, c_int32, c_double, c_int32,
+                                       POINTER(c_int32)]),
+    "gncx_engine_timing": (c_int32, [c_void_p, POINTER(c_double), POINTER(c_double), POINTER(c_int32)]),
 }
 
 _lib = None

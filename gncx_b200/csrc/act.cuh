@@ -154,4 +154,25 @@ __device__ __forceinline__ void stage_act_blocks(const ActBlock* __restrict__ ab
     }
 }
 
+// One warp quantizes one 32-input block held one value per lane and stores
+// it as an ActBlock (same arithmetic as quantize_block32).
+__device__ __forceinline__ void warp_quantize_store(float v, ActBlock* dst, int lane) {
+    float amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    int q = 0;
+    float d = 0.0f;
+    if (amax != 0.0f) {
+        const float inv = fdiv(127.0f, amax);
+        d = fdiv(amax, 127.0f);
+        q = __float2int_rn(fmul(v, inv));
+    }
+    int s = q;
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);  // sums of lanes 0..15 / 16..31
+    dst->qs[lane] = (int8_t)q;
+    if (lane == 0) { dst->d = d; dst->sum_lo = s; dst->pad = 0; }
+    if (lane == 16) dst->sum_hi = s;
+}
+
 }  // namespace gncx

@@ -1,13 +1,18 @@
 // attention.cu -- GQA / MQA / sliding-window decode attention over an fp32 KV
-// cache (replaces gncx_mqa_attention_step_ext, csrc/gncx_llm_kernels.cpp:1887-1994).
+// cache (replaces gncx_mqa_attention_step_ext, csrc/gncx_llm_kernels.cpp:1887-1994),
+// and the causal prefill form (one query per prompt position, each attending to
+// positions <= its own, as the reference's prefill calls the decode step per
+// token, lua/gncx_streamer.lua:1079-1109).
 //
-// Split-KV ("flash-decoding"): the window [t0, pos] is cut into chunks of up
-// to 64 positions; one CTA per (chunk, KV head) pulls that chunk's K and V
-// head rows into shared memory with cp.async.bulk (one 16-byte-aligned copy per
-// position, rows padded by 8 floats so the 8-lane dot pattern is bank-conflict
-// free), serves every query head of the group from it, and writes a partial
-// record (chunk max, sum of exp, unnormalised output).  A combine kernel merges
-// the records of each head.  Each K/V byte crosses HBM once.
+// Split-KV ("flash-decoding"): a query's window [t0, pos] is cut into chunks;
+// one CTA per (chunk, KV head, query) pulls that chunk's K and V head rows into
+// shared memory with cp.async.bulk (one 16-byte-aligned copy per position, rows
+// padded by 8 floats so the 8-lane dot pattern is bank-conflict free), serves
+// every query head of the group from it, and writes a partial record (chunk
+// max, sum of exp, unnormalised output).  A combine kernel merges the records
+// of each head and can re-quantize the result for the next GEMV.  In decode,
+// each K/V byte crosses HBM once.  The position may live in device memory so a
+// captured CUDA graph replays every token; CTAs past the window exit at once.
 //
 // Scores are bit-identical to the reference's: its q.k is two 4-lane SSE
 // accumulators over steps of 8, folded (l0+l1)+(l2+l3); lane j of an 8-lane
@@ -17,6 +22,7 @@
 //
 // KV cache layout is the reference's: [max_seq][n_kv][head_dim] fp32 per layer.
 #include <cuda_runtime.h>
+#include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
 #include "tma.cuh"
@@ -25,30 +31,7 @@ namespace gncx {
 
 constexpr int kAttnThreads = 128;
 constexpr int kMaxHeadDim = 256;
-constexpr int kMaxChunk = 64;
 constexpr int kRowPad = 8;  // floats of padding per staged K/V row
-
-struct AttnGeom {
-    int t0, len, chunk, n_splits;
-};
-
-static AttnGeom attn_geom(int32_t pos, int32_t n_kv, int32_t window, int sm_count) {
-    AttnGeom g;
-    g.t0 = window > 0 ? (pos - window + 1 > 0 ? pos - window + 1 : 0) : 0;
-    g.len = pos + 1 - g.t0;
-    int c = kMaxChunk;
-    // shorter chunks when the window is small, so every SM gets ~2 CTAs
-    while (c > 16 && (int64_t)((g.len + c - 1) / c) * n_kv < 2 * (int64_t)sm_count) c >>= 1;
-    g.chunk = c;
-    g.n_splits = (g.len + c - 1) / c;
-    return g;
-}
-
-int32_t attention_scratch_records(int32_t pos, int32_t n_heads, int32_t window) {
-    const int32_t t0 = window > 0 ? (pos - window + 1 > 0 ? pos - window + 1 : 0) : 0;
-    const int32_t len = pos + 1 - t0;
-    return n_heads * ((len + 15) / 16);  // the smallest chunk is 16 positions
-}
 
 static size_t attn_smem_bytes(int G, int hd, int chunk) {
     const int rs = hd + kRowPad;
@@ -56,18 +39,28 @@ static size_t attn_smem_bytes(int G, int hd, int chunk) {
            (size_t)2 * G * 4;
 }
 
-// Partial record layout per (head, split): [0] = max, [1] = sum of exp, [2..] = o[hd]
+__device__ __forceinline__ void attn_window(const AttnArgs& a, int z, int& t0, int& len) {
+    const int pos = (a.pos_dev ? *a.pos_dev : a.pos0) + z;
+    t0 = a.window > 0 ? max(0, pos - a.window + 1) : 0;
+    len = pos + 1 - t0;
+}
+
+// Partial record layout per (query, head, split): [0] = max, [1] = sum of exp, [2..] = o[hd]
 template <bool BULK>
-__global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(
-    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc, int n_heads, int n_kv,
-    int hd, float scale, int t0, int len, int chunk, int n_splits, float* __restrict__ part, int32_t* err) {
+__global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnArgs a) {
     extern __shared__ __align__(128) uint8_t smraw[];
-    const int G = n_heads / n_kv;
-    const int kvh = blockIdx.y;
+    const int z = blockIdx.z;
+    int t0, len;
+    attn_window(a, z, t0, len);
+    const int chunk = a.chunk;
     const int split = blockIdx.x;
     const int c0 = split * chunk;
+    if (c0 >= len) return;  // uniform per CTA, before any barrier
+    const int hd = a.hd;
+    const int G = a.n_heads / a.n_kv;
+    const int kvh = blockIdx.y;
     const int cn = min(chunk, len - c0);
-    const int kvd = n_kv * hd;
+    const int kvd = a.n_kv * hd;
     const int rs = hd + kRowPad;
     uint64_t* bar = reinterpret_cast<uint64_t*>(smraw);   // [0] = K, [1] = V
     float* ks = reinterpret_cast<float*>(smraw + 64);     // [chunk][rs]
@@ -93,17 +86,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(
                 mbar_arrive_expect_tx(&bar[1], bytes * cn);
             }
             __syncwarp();
-            for (int p = lane; p < cn; p += 32) bulk_g2s(ks + (size_t)p * rs, kc + row0 + (size_t)p * kvd, bytes, &bar[0]);
-            for (int p = lane; p < cn; p += 32) bulk_g2s(vs + (size_t)p * rs, vc + row0 + (size_t)p * kvd, bytes, &bar[1]);
+            for (int p = lane; p < cn; p += 32) bulk_g2s(ks + (size_t)p * rs, a.kc + row0 + (size_t)p * kvd, bytes, &bar[0]);
+            for (int p = lane; p < cn; p += 32) bulk_g2s(vs + (size_t)p * rs, a.vc + row0 + (size_t)p * kvd, bytes, &bar[1]);
         }
     } else {
         for (int i = tid; i < cn * hd; i += blockDim.x) {
             const int p = i / hd, d = i % hd;
-            ks[(size_t)p * rs + d] = kc[row0 + (size_t)p * kvd + d];
-            vs[(size_t)p * rs + d] = vc[row0 + (size_t)p * kvd + d];
+            ks[(size_t)p * rs + d] = a.kc[row0 + (size_t)p * kvd + d];
+            vs[(size_t)p * rs + d] = a.vc[row0 + (size_t)p * kvd + d];
         }
     }
-    for (int i = tid; i < G * hd; i += blockDim.x) qs[i] = q[(size_t)kvh * G * hd + i];
+    const float* qz = a.q + (size_t)z * a.q_stride + (size_t)kvh * G * hd;
+    for (int i = tid; i < G * hd; i += blockDim.x) qs[i] = qz[i];
     __syncthreads();
     bool timed_out = false;
     if (BULK && !mbar_wait(&bar[0], 0)) timed_out = true;
@@ -126,12 +120,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(
 #pragma unroll
                 for (int m = 0; m < kMaxHeadDim / 8; ++m)
                     if (m < nm) c = fadd(c, fmul(qg[8 * m + j], kr[m]));
-                const float a = fadd(c, __shfl_down_sync(0xffffffffu, c, 4));
-                const float b = fadd(a, __shfl_down_sync(0xffffffffu, a, 1));
-                float dot = fadd(b, __shfl_down_sync(0xffffffffu, b, 2));
+                const float x = fadd(c, __shfl_down_sync(0xffffffffu, c, 4));
+                const float y = fadd(x, __shfl_down_sync(0xffffffffu, x, 1));
+                float dot = fadd(y, __shfl_down_sync(0xffffffffu, y, 2));
                 if (j == 0 && ok) {
                     for (int d = nm * 8; d < hd; ++d) dot = fadd(dot, fmul(qg[d], kt[d]));
-                    sc[g * chunk + p] = fmul(dot, scale);
+                    sc[g * chunk + p] = fmul(dot, a.scale);
                 }
             }
         }
@@ -156,7 +150,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(
     if (BULK && !mbar_wait(&bar[1], 0)) timed_out = true;
     __syncthreads();
     if (timed_out) {
-        if (tid == 0) record_error(err, kErrTimeout);
+        if (tid == 0) record_error(a.err, kErrTimeout);
         return;
     }
 
@@ -175,7 +169,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(
             for (int k = 0; k < 4; ++k) {
                 if (g0 + k < G) {
                     const int h = kvh * G + g0 + k;
-                    float* rec = part + ((size_t)h * n_splits + split) * (hd + 2);
+                    float* rec = a.part + (((size_t)z * a.n_heads + h) * a.max_splits + split) * (hd + 2);
                     rec[2 + d] = acc[k];
                     if (d == 0) { rec[0] = red[2 * (g0 + k)]; rec[1] = red[2 * (g0 + k) + 1]; }
                 }
@@ -184,65 +178,117 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(
     }
 }
 
-// Merge the split records of one head: out = (sum_s o_s * e^(m_s-M)) / (sum_s l_s * e^(m_s-M) + 1e-12).
-__global__ void attn_combine_kernel(const float* __restrict__ part, int n_splits, int hd, float* __restrict__ out) {
-    extern __shared__ float wsm[];  // [n_splits] weights
+// Merge the split records of one (query, head):
+// out = (sum_s o_s * e^(m_s-M)) / (sum_s l_s * e^(m_s-M) + 1e-12); optionally
+// re-quantized (blockDim == hd, one warp per 32 outputs).
+__global__ void attn_combine_kernel(const AttnArgs a) {
+    extern __shared__ float wsm[];  // [max_splits] weights
     __shared__ float s_inv;
-    const int h = blockIdx.x;
-    const float* rec = part + (size_t)h * n_splits * (hd + 2);
+    const int h = blockIdx.x, z = blockIdx.y;
+    const int hd = a.hd;
+    int t0, len;
+    attn_window(a, z, t0, len);
+    const int n = (len + a.chunk - 1) / a.chunk;
+    const float* rec = a.part + ((size_t)z * a.n_heads + h) * a.max_splits * (hd + 2);
     float M = -INFINITY;
-    for (int s = 0; s < n_splits; ++s) M = fmaxf(M, rec[(size_t)s * (hd + 2)]);
-    for (int s = threadIdx.x; s < n_splits; s += blockDim.x) wsm[s] = exp_cr(fsub(rec[(size_t)s * (hd + 2)], M));
+    for (int s = 0; s < n; ++s) M = fmaxf(M, rec[(size_t)s * (hd + 2)]);
+    for (int s = threadIdx.x; s < n; s += blockDim.x) wsm[s] = exp_cr(fsub(rec[(size_t)s * (hd + 2)], M));
     __syncthreads();
     if (threadIdx.x == 0) {
         float L = 0.0f;
-        for (int s = 0; s < n_splits; ++s) L = fadd(L, fmul(rec[(size_t)s * (hd + 2) + 1], wsm[s]));
+        for (int s = 0; s < n; ++s) L = fadd(L, fmul(rec[(size_t)s * (hd + 2) + 1], wsm[s]));
         s_inv = fdiv(1.0f, fadd(L, 1e-12f));
     }
     __syncthreads();
     const float inv = s_inv;
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
         float o = 0.0f;
-        for (int s = 0; s < n_splits; ++s) o = fadd(o, fmul(rec[(size_t)s * (hd + 2) + 2 + d], wsm[s]));
-        out[(size_t)h * hd + d] = fmul(o, inv);
+        for (int s = 0; s < n; ++s) o = fadd(o, fmul(rec[(size_t)s * (hd + 2) + 2 + d], wsm[s]));
+        o = fmul(o, inv);
+        if (a.out) a.out[(size_t)z * a.out_stride + (size_t)h * hd + d] = o;
+        if (a.act_out) {
+            ActBlock* dst = a.act_out + (size_t)z * (a.n_heads * hd / 32) + ((size_t)h * hd + d) / 32;
+            warp_quantize_store(o, dst, d & 31);
+        }
     }
 }
 
-int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t n_heads, int32_t n_kv,
-                     int32_t head_dim, float scale, int32_t window, float* out, const AttnScratch& scratch,
-                     int32_t* err, cudaStream_t st) {
-    if (!q || !kc || !vc || !out || pos < 0 || n_heads <= 0 || n_kv <= 0 || head_dim <= 0) return kErrInvalidArg;
-    if (n_heads % n_kv != 0 || head_dim > kMaxHeadDim || (head_dim & 3)) return kErrInvalidArg;
+int attention_geometry_chunk(int32_t len, int32_t n_kv, int sm_count) {
+    int c = 64;
+    // shorter chunks when the window is small, so every SM gets ~2 CTAs
+    while (c > 16 && (int64_t)((len + c - 1) / c) * n_kv < 2 * (int64_t)sm_count) c >>= 1;
+    return c;
+}
+
+int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
+    const AttnArgs& a = args;
+    if (!a.q || !a.kc || !a.vc || !a.part || a.n_heads <= 0 || a.n_kv <= 0 || a.hd <= 0 || n_tok <= 0)
+        return kErrInvalidArg;
+    if (a.n_heads % a.n_kv != 0 || a.hd > kMaxHeadDim || (a.hd & 3) || a.chunk <= 0 || a.max_splits <= 0)
+        return kErrInvalidArg;
+    if (a.act_out && (a.hd % 32 || a.hd > 1024)) return kErrInvalidArg;
     const DeviceInfo& dev = device_info();
-    const AttnGeom g = attn_geom(pos, n_kv, window, dev.sm_count);
-    if (!scratch.part || (int64_t)n_heads * g.n_splits > scratch.capacity) return kErrCapacity;
-    const int G = n_heads / n_kv;
-    const size_t smem = attn_smem_bytes(G, head_dim, g.chunk);
+    const int G = a.n_heads / a.n_kv;
+    const size_t smem = attn_smem_bytes(G, a.hd, a.chunk);
     if (smem > (size_t)dev.max_smem_optin) return kErrCapacity;
-    const bool bulk = ((uintptr_t)kc % 16 == 0) && ((uintptr_t)vc % 16 == 0);
-    dim3 grid(g.n_splits, n_kv);
+    const bool bulk = ((uintptr_t)a.kc % 16 == 0) && ((uintptr_t)a.vc % 16 == 0);
+    dim3 grid(a.max_splits, a.n_kv, n_tok);
     if (bulk) {
         static size_t set_bytes = 0;
         if (smem > set_bytes) {
             cudaFuncSetAttribute(attn_partial_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             set_bytes = smem;
         }
-        attn_partial_kernel<true><<<grid, kAttnThreads, smem, st>>>(q, kc, vc, n_heads, n_kv, head_dim, scale, g.t0,
-                                                                     g.len, g.chunk, g.n_splits, scratch.part, err);
+        attn_partial_kernel<true><<<grid, kAttnThreads, smem, st>>>(a);
     } else {
         static size_t set_bytes = 0;
         if (smem > set_bytes) {
             cudaFuncSetAttribute(attn_partial_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             set_bytes = smem;
         }
-        attn_partial_kernel<false><<<grid, kAttnThreads, smem, st>>>(q, kc, vc, n_heads, n_kv, head_dim, scale, g.t0,
-                                                                      g.len, g.chunk, g.n_splits, scratch.part, err);
+        attn_partial_kernel<false><<<grid, kAttnThreads, smem, st>>>(a);
     }
-    const size_t csm = (size_t)g.n_splits * 4;
+    const size_t csm = (size_t)a.max_splits * 4;
     if (csm > 48 * 1024)
         cudaFuncSetAttribute(attn_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csm);
-    attn_combine_kernel<<<n_heads, 128, csm, st>>>(scratch.part, g.n_splits, head_dim, out);
+    const int cthreads = (a.act_out || (a.hd % 32 == 0 && a.hd <= 1024)) ? a.hd : 128;
+    attn_combine_kernel<<<dim3(a.n_heads, n_tok), cthreads, csm, st>>>(a);
     return cudaPeekAtLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int32_t attention_scratch_records(int32_t pos, int32_t n_heads, int32_t window) {
+    const int32_t t0 = window > 0 ? (pos - window + 1 > 0 ? pos - window + 1 : 0) : 0;
+    const int32_t len = pos + 1 - t0;
+    return n_heads * ((len + 15) / 16);  // the smallest chunk is 16 positions
+}
+
+int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t n_heads, int32_t n_kv,
+                     int32_t head_dim, float scale, int32_t window, float* out, const AttnScratch& scratch,
+                     int32_t* err, cudaStream_t st) {
+    if (!q || !kc || !vc || !out || pos < 0 || n_heads <= 0 || n_kv <= 0 || head_dim <= 0) return kErrInvalidArg;
+    const int32_t t0 = window > 0 ? (pos - window + 1 > 0 ? pos - window + 1 : 0) : 0;
+    const int32_t len = pos + 1 - t0;
+    AttnArgs a{};
+    a.q = q;
+    a.q_stride = n_heads * head_dim;
+    a.kc = kc;
+    a.vc = vc;
+    a.pos0 = pos;
+    a.pos_dev = nullptr;
+    a.n_heads = n_heads;
+    a.n_kv = n_kv;
+    a.hd = head_dim;
+    a.scale = scale;
+    a.window = window;
+    a.chunk = attention_geometry_chunk(len, n_kv, device_info().sm_count);
+    a.max_splits = (len + a.chunk - 1) / a.chunk;
+    if (!scratch.part || (int64_t)n_heads * a.max_splits > scratch.capacity) return kErrCapacity;
+    a.part = scratch.part;
+    a.out = out;
+    a.out_stride = n_heads * head_dim;
+    a.act_out = nullptr;
+    a.err = err;
+    return attention_run(a, 1, st);
 }
 
 }  // namespace gncx

@@ -82,6 +82,18 @@ __device__ __forceinline__ float bf16_bits_to_float(uint32_t b16) { return __uin
 __device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x); }
 __device__ __forceinline__ float tanh_cr(float x) { return (float)tanh((double)x); }
 
+// GLU activations (csrc/gncx_llm_kernels.cpp:2018-2052), rounding as written there.
+__device__ __forceinline__ float swiglu1(float g, float u) {
+    const float silu = fdiv(g, fadd(1.0f, exp_cr(-g)));
+    return fmul(silu, u);
+}
+__device__ __forceinline__ float geglu1(float x, float u) {
+    const float k0 = 0.7978845608028654f;
+    const float inner = fmul(k0, fadd(x, fmul(fmul(fmul(0.044715f, x), x), x)));
+    const float gelu = fmul(fmul(0.5f, x), fadd(1.0f, tanh_cr(inner)));
+    return fmul(gelu, u);
+}
+
 // Bytes [off, off+4) of a little-endian word array as one word, for a
 // compile-time offset.
 template <int OFF>

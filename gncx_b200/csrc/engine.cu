@@ -1,0 +1,733 @@
+// engine.cu -- the model engine: GGUF load + upload in native block layout,
+// decode step (forward_token + greedy sample) and batched prefill on one GPU.
+//
+// It restates the reference orchestrator lua/gncx_streamer.lua (forward_token
+// :759-965, prefill :968-1208, sample :1229-1273, generate :1276-1311) for the
+// Qwen3 / Llama / Gemma(1,2) decoder families, with the arithmetic of each step
+// done by this library's kernels.  What changes is where things live:
+//   * weights: one HBM arena, tensors in their GGUF block layout; q/k/v rows and
+//     gate/up rows are placed back to back when their types match, so each pair
+//     (triple) is one GEMV;
+//   * per-token state (input token, position, penalty window, output ids) is in
+//     device memory, so a whole decode step -- embedding, 36 layers, LM head,
+//     argmax -- is one captured CUDA graph launch with no host round trip;
+//   * the KV cache is the reference's layout, fp32 [max_seq][n_kv][head_dim].
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "kernels.h"
+
+namespace gncx {
+
+// ---------------------------------------------------------------- GGUF (lua/gncx_gguf.lua:223-306)
+struct GgufTensor {
+    std::vector<uint64_t> dims;
+    int32_t type = 0;
+    uint64_t abs_off = 0;
+    uint64_t nbytes = 0;
+};
+
+struct Gguf {
+    int fd = -1;
+    const uint8_t* base = nullptr;
+    size_t size = 0;
+    std::map<std::string, double> num;
+    std::map<std::string, std::string> str;
+    std::map<std::string, uint64_t> arr_len;
+    std::map<std::string, GgufTensor> tensors;
+    ~Gguf() {
+        if (base) munmap(const_cast<uint8_t*>(base), size);
+        if (fd >= 0) close(fd);
+    }
+};
+
+struct Cursor {
+    const uint8_t* p;
+    const uint8_t* end;
+    bool ok = true;
+    template <class T>
+    T get() {
+        T v{};
+        if (p + sizeof(T) > end) { ok = false; return v; }
+        memcpy(&v, p, sizeof(T));
+        p += sizeof(T);
+        return v;
+    }
+    std::string string() {
+        const uint64_t n = get<uint64_t>();
+        if (!ok || p + n > end) { ok = false; return {}; }
+        std::string s(reinterpret_cast<const char*>(p), n);
+        p += n;
+        return s;
+    }
+};
+
+static bool skip_value(Cursor& c, uint32_t t, double* num_out, std::string* str_out, uint64_t* arr_n) {
+    switch (t) {
+        case 0: { const double v = c.get<uint8_t>(); if (num_out) *num_out = v; return c.ok; }
+        case 1: { const double v = c.get<int8_t>(); if (num_out) *num_out = v; return c.ok; }
+        case 2: { const double v = c.get<uint16_t>(); if (num_out) *num_out = v; return c.ok; }
+        case 3: { const double v = c.get<int16_t>(); if (num_out) *num_out = v; return c.ok; }
+        case 4: { const double v = c.get<uint32_t>(); if (num_out) *num_out = v; return c.ok; }
+        case 5: { const double v = c.get<int32_t>(); if (num_out) *num_out = v; return c.ok; }
+        case 6: { const double v = c.get<float>(); if (num_out) *num_out = v; return c.ok; }
+        case 7: { const double v = c.get<uint8_t>(); if (num_out) *num_out = v; return c.ok; }
+        case 8: { std::string s = c.string(); if (str_out) *str_out = s; return c.ok; }
+        case 9: {
+            const uint32_t et = c.get<uint32_t>();
+            const uint64_t n = c.get<uint64_t>();
+            if (arr_n) *arr_n = n;
+            for (uint64_t i = 0; i < n && c.ok; ++i) skip_value(c, et, nullptr, nullptr, nullptr);
+            return c.ok;
+        }
+        case 10: { const double v = (double)c.get<uint64_t>(); if (num_out) *num_out = v; return c.ok; }
+        case 11: { const double v = (double)c.get<int64_t>(); if (num_out) *num_out = v; return c.ok; }
+        case 12: { const double v = c.get<double>(); if (num_out) *num_out = v; return c.ok; }
+        default: c.ok = false; return false;
+    }
+}
+
+static bool gguf_open(const char* path, Gguf& g, std::string& err) {
+    g.fd = open(path, O_RDONLY);
+    if (g.fd < 0) { err = "cannot open model file"; return false; }
+    struct stat st {};
+    fstat(g.fd, &st);
+    g.size = (size_t)st.st_size;
+    void* m = mmap(nullptr, g.size, PROT_READ, MAP_PRIVATE, g.fd, 0);
+    if (m == MAP_FAILED) { err = "mmap failed"; return false; }
+    g.base = static_cast<const uint8_t*>(m);
+    Cursor c{g.base, g.base + g.size};
+    if (g.size < 24 || memcmp(g.base, "GGUF", 4) != 0) { err = "not a GGUF file"; return false; }
+    c.p += 4;
+    (void)c.get<uint32_t>();  // version
+    const uint64_t n_tensors = c.get<uint64_t>();
+    const uint64_t n_kv = c.get<uint64_t>();
+    for (uint64_t i = 0; i < n_kv && c.ok; ++i) {
+        const std::string key = c.string();
+        const uint32_t t = c.get<uint32_t>();
+        double num = 0;
+        std::string s;
+        uint64_t an = 0;
+        skip_value(c, t, &num, &s, &an);
+        if (t == 8) g.str[key] = s;
+        else if (t == 9) g.arr_len[key] = an;
+        else g.num[key] = num;
+    }
+    std::vector<std::pair<std::string, GgufTensor>> recs;
+    for (uint64_t i = 0; i < n_tensors && c.ok; ++i) {
+        std::string name = c.string();
+        GgufTensor tr;
+        const uint32_t nd = c.get<uint32_t>();
+        for (uint32_t d = 0; d < nd; ++d) tr.dims.push_back(c.get<uint64_t>());
+        tr.type = (int32_t)c.get<uint32_t>();
+        tr.abs_off = c.get<uint64_t>();  // relative for now
+        recs.emplace_back(std::move(name), std::move(tr));
+    }
+    if (!c.ok) { err = "truncated GGUF header"; return false; }
+    uint64_t align = 32;
+    auto it = g.num.find("general.alignment");
+    if (it != g.num.end() && it->second > 0) align = (uint64_t)it->second;
+    const uint64_t hdr = (uint64_t)(c.p - g.base);
+    const uint64_t data = (hdr + align - 1) / align * align;
+    for (auto& r : recs) {
+        uint64_t n = 1;
+        for (auto d : r.second.dims) n *= d;
+        const int be = block_elems(r.second.type), bb = block_bytes(r.second.type);
+        r.second.nbytes = bb ? (n / be) * (uint64_t)bb : 0;
+        r.second.abs_off += data;
+        if (r.second.abs_off + r.second.nbytes > g.size) { err = "tensor data past end of file: " + r.first; return false; }
+        g.tensors[r.first] = r.second;
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------- engine
+struct LayerW {
+    const float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+    const uint8_t *wq = nullptr, *wk = nullptr, *wv = nullptr, *wo = nullptr, *wg = nullptr, *wu = nullptr, *wd = nullptr;
+    int tq = 0, tk = 0, tv = 0, to = 0, tg = 0, tu = 0, td = 0;
+    bool qkv_fused = false, gu_fused = false;
+    float *kc = nullptr, *vc = nullptr;
+};
+
+struct Engine {
+    // hyper-parameters (lua/gncx_streamer.lua:344-441)
+    int arch = 0;  // 0 qwen, 1 llama, 2 gemma
+    int n_layers = 0, dim = 0, nh = 0, nkv = 0, hd = 0, ffn = 0, vocab = 0, max_seq = 0, q_dim = 0, kv_dim = 0;
+    float eps = 1e-6f, rope_base = 10000.0f, softcap = 0.0f, attn_scale = 0.0f, embd_scale = 1.0f;
+    int eos = -1;
+    bool qk_norm = false;
+    const uint8_t* tok_embd = nullptr;
+    int embd_type = 0;
+    const float* out_norm = nullptr;
+    std::vector<LayerW> L;
+    uint8_t* arena = nullptr;
+    size_t arena_bytes = 0;
+    float* kv = nullptr;
+    float *rope_c = nullptr, *rope_s = nullptr;
+    // decode buffers
+    float *hidden = nullptr, *proj = nullptr, *qkv = nullptr, *gu = nullptr, *logits = nullptr, *normed = nullptr;
+    ActBlock *act_d = nullptr, *act_q = nullptr, *act_f = nullptr;
+    float* part = nullptr;
+    int max_splits = 0;
+    DecodeState* st = nullptr;
+    DecodeState* st_host = nullptr;  // pinned staging
+    int32_t* out_ids = nullptr;
+    int out_cap = 0;
+    void* am_scratch = nullptr;
+    int32_t* d_err = nullptr;
+    int32_t* ids_dev = nullptr;
+    int ids_cap = 0;
+    cudaStream_t stream = nullptr;
+    cudaGraphExec_t graph = nullptr;
+    double penalty_graph = -1.0;
+    cudaEvent_t ev[4] = {};
+    double prefill_ms = 0.0, decode_ms = 0.0;
+    int decode_steps = 0;
+    std::string error;
+    // prefill buffers (grown on demand)
+    int pf_cap = 0;
+    float *pf_h = nullptr, *pf_p = nullptr, *pf_qkv = nullptr, *pf_gu = nullptr, *pf_part = nullptr;
+    ActBlock *pf_act = nullptr, *pf_actq = nullptr, *pf_actf = nullptr;
+    size_t pf_part_floats = 0;
+};
+
+static constexpr int kDecodeChunk = 64;    // positions per attention split in decode
+static constexpr int kPrefillGroup = 256;  // prompt positions per attention launch in prefill
+
+#define CK(x)                                             \
+    do {                                                  \
+        const int _st = (x);                              \
+        if (_st != kOk) return _st;                       \
+    } while (0)
+#define CU(x)                                             \
+    do {                                                  \
+        if ((x) != cudaSuccess) return kErrCuda;          \
+    } while (0)
+
+static int gemv(Engine* e, const uint8_t* w, int t, const ActBlock* act, const float* x, int in, int out, float* y,
+                float cap = 0.0f) {
+    return gemv_launch(w, t, t == kBF16 ? x : nullptr, t == kBF16 ? nullptr : act, in, out, y, cap, e->d_err,
+                       e->stream);
+}
+
+// One decode step: forward(st->token at st->pos) and, if `sample`, the
+// penalized argmax that appends the next token and advances the position.
+static int decode_step(Engine* e, bool sample, double penalty) {
+    cudaStream_t s = e->stream;
+    const int D = e->dim, QD = e->q_dim, KVD = e->kv_dim, F = e->ffn;
+    const int qkv_w = QD + 2 * KVD;
+    CK(dequant_launch(e->tok_embd, e->embd_type, 1, D, e->embd_scale, &e->st->token, e->hidden, s));
+    for (int l = 0; l < e->n_layers; ++l) {
+        const LayerW& w = e->L[l];
+        CK(add_norm_quant_launch(e->hidden, l == 0 ? nullptr : e->proj, w.attn_norm, 1, D, e->eps, e->act_d, e->normed,
+                                 s));
+        if (w.qkv_fused) {
+            CK(gemv(e, w.wq, w.tq, e->act_d, e->normed, D, qkv_w, e->qkv));
+        } else {
+            CK(gemv(e, w.wq, w.tq, e->act_d, e->normed, D, QD, e->qkv));
+            CK(gemv(e, w.wk, w.tk, e->act_d, e->normed, D, KVD, e->qkv + QD));
+            CK(gemv(e, w.wv, w.tv, e->act_d, e->normed, D, KVD, e->qkv + QD + KVD));
+        }
+        CK(qkv_post_launch(e->qkv, qkv_w, 1, e->nh, e->nkv, e->hd, w.q_norm, w.k_norm, e->qk_norm, e->eps, e->rope_c,
+                           e->rope_s, 0, &e->st->pos, w.kc, w.vc, s));
+        AttnArgs a{};
+        a.q = e->qkv;
+        a.q_stride = qkv_w;
+        a.kc = w.kc;
+        a.vc = w.vc;
+        a.pos0 = 0;
+        a.pos_dev = &e->st->pos;
+        a.n_heads = e->nh;
+        a.n_kv = e->nkv;
+        a.hd = e->hd;
+        a.scale = e->attn_scale;
+        a.window = 0;
+        a.chunk = kDecodeChunk;
+        a.max_splits = e->max_splits;
+        a.part = e->part;
+        a.out = nullptr;
+        a.out_stride = QD;
+        a.act_out = e->act_q;
+        a.err = e->d_err;
+        CK(attention_run(a, 1, s));
+        CK(gemv(e, w.wo, w.to, e->act_q, nullptr, QD, D, e->proj));
+        CK(add_norm_quant_launch(e->hidden, e->proj, w.ffn_norm, 1, D, e->eps, e->act_d, e->normed, s));
+        if (w.gu_fused) {
+            CK(gemv(e, w.wg, w.tg, e->act_d, e->normed, D, 2 * F, e->gu));
+        } else {
+            CK(gemv(e, w.wg, w.tg, e->act_d, e->normed, D, F, e->gu));
+            CK(gemv(e, w.wu, w.tu, e->act_d, e->normed, D, F, e->gu + F));
+        }
+        CK(glu_quant_launch(e->gu, e->gu + F, 2 * F, F, 1, e->arch == 2, e->act_f, s));
+        CK(gemv(e, w.wd, w.td, e->act_f, nullptr, F, D, e->proj));
+    }
+    CK(add_norm_quant_launch(e->hidden, e->proj, e->out_norm, 1, D, e->eps, e->act_d, e->normed, s));
+    CK(gemv(e, e->tok_embd, e->embd_type, e->act_d, e->normed, D, e->vocab, e->logits, e->softcap));
+    if (sample) CK(argmax_state_launch(e->logits, e->vocab, e->st, penalty, e->out_ids, 1, e->am_scratch, s));
+    return kOk;
+}
+
+static int ensure_prefill(Engine* e, int B) {
+    if (B <= e->pf_cap) return kOk;
+    cudaStreamSynchronize(e->stream);
+    cudaFree(e->pf_h); cudaFree(e->pf_p); cudaFree(e->pf_qkv); cudaFree(e->pf_gu); cudaFree(e->pf_part);
+    cudaFree(e->pf_act); cudaFree(e->pf_actq); cudaFree(e->pf_actf);
+    e->pf_cap = 0;
+    const size_t D = e->dim, QKV = e->q_dim + 2 * e->kv_dim, F = e->ffn;
+    const int grp = B < kPrefillGroup ? B : kPrefillGroup;
+    const size_t splits = (size_t)(B + kDecodeChunk - 1) / kDecodeChunk;
+    e->pf_part_floats = (size_t)grp * e->nh * splits * (e->hd + 2);
+    if (cudaMalloc(&e->pf_h, (size_t)B * D * 4) || cudaMalloc(&e->pf_p, (size_t)B * D * 4) ||
+        cudaMalloc(&e->pf_qkv, (size_t)B * QKV * 4) || cudaMalloc(&e->pf_gu, (size_t)B * 2 * F * 4) ||
+        cudaMalloc(&e->pf_part, e->pf_part_floats * 4) ||
+        cudaMalloc(&e->pf_act, (size_t)B * (D / 32) * sizeof(ActBlock)) ||
+        cudaMalloc(&e->pf_actq, (size_t)B * (e->q_dim / 32) * sizeof(ActBlock)) ||
+        cudaMalloc(&e->pf_actf, (size_t)B * (F / 32) * sizeof(ActBlock))) {
+        cudaGetLastError();
+        return kErrOutOfMemory;
+    }
+    e->pf_cap = B;
+    return kOk;
+}
+
+// lua/gncx_streamer.lua:968-1208 (B >= 2): every layer runs over all prompt
+// positions at once; attention is causal per position (each position sees
+// the positions <= its own, exactly what the reference's per-token loop does).
+static int prefill_batch(Engine* e, int B) {
+    cudaStream_t s = e->stream;
+    const int D = e->dim, QD = e->q_dim, KVD = e->kv_dim, F = e->ffn;
+    const int qkv_w = QD + 2 * KVD;
+    CK(ensure_prefill(e, B));
+    CK(dequant_launch(e->tok_embd, e->embd_type, B, D, e->embd_scale, e->ids_dev, e->pf_h, s));
+    for (int l = 0; l < e->n_layers; ++l) {
+        const LayerW& w = e->L[l];
+        CK(add_norm_quant_launch(e->pf_h, l == 0 ? nullptr : e->pf_p, w.attn_norm, B, D, e->eps, e->pf_act, nullptr, s));
+        if (w.qkv_fused) {
+            CK(matbatch_launch(w.wq, w.tq, nullptr, e->pf_act, B, D, qkv_w, e->pf_qkv, e->d_err, s, qkv_w));
+        } else {
+            CK(matbatch_launch(w.wq, w.tq, nullptr, e->pf_act, B, D, QD, e->pf_qkv, e->d_err, s, qkv_w));
+            CK(matbatch_launch(w.wk, w.tk, nullptr, e->pf_act, B, D, KVD, e->pf_qkv + QD, e->d_err, s, qkv_w));
+            CK(matbatch_launch(w.wv, w.tv, nullptr, e->pf_act, B, D, KVD, e->pf_qkv + QD + KVD, e->d_err, s, qkv_w));
+        }
+        CK(qkv_post_launch(e->pf_qkv, qkv_w, B, e->nh, e->nkv, e->hd, w.q_norm, w.k_norm, e->qk_norm, e->eps, e->rope_c,
+                           e->rope_s, 0, nullptr, w.kc, w.vc, s));
+        for (int z0 = 0; z0 < B; z0 += kPrefillGroup) {
+            const int nz = B - z0 < kPrefillGroup ? B - z0 : kPrefillGroup;
+            AttnArgs a{};
+            a.q = e->pf_qkv + (size_t)z0 * qkv_w;
+            a.q_stride = qkv_w;
+            a.kc = w.kc;
+            a.vc = w.vc;
+            a.pos0 = z0;
+            a.pos_dev = nullptr;
+            a.n_heads = e->nh;
+            a.n_kv = e->nkv;
+            a.hd = e->hd;
+            a.scale = e->attn_scale;
+            a.window = 0;
+            a.chunk = kDecodeChunk;
+            a.max_splits = (z0 + nz + kDecodeChunk - 1) / kDecodeChunk;
+            a.part = e->pf_part;
+            a.out = nullptr;
+            a.out_stride = QD;
+            a.act_out = e->pf_actq + (size_t)z0 * (QD / 32);
+            a.err = e->d_err;
+            if ((size_t)nz * e->nh * a.max_splits * (e->hd + 2) > e->pf_part_floats) return kErrCapacity;
+            CK(attention_run(a, nz, s));
+        }
+        CK(matbatch_launch(w.wo, w.to, nullptr, e->pf_actq, B, QD, D, e->pf_p, e->d_err, s));
+        CK(add_norm_quant_launch(e->pf_h, e->pf_p, w.ffn_norm, B, D, e->eps, e->pf_act, nullptr, s));
+        if (w.gu_fused) {
+            CK(matbatch_launch(w.wg, w.tg, nullptr, e->pf_act, B, D, 2 * F, e->pf_gu, e->d_err, s, 2 * F));
+        } else {
+            CK(matbatch_launch(w.wg, w.tg, nullptr, e->pf_act, B, D, F, e->pf_gu, e->d_err, s, 2 * F));
+            CK(matbatch_launch(w.wu, w.tu, nullptr, e->pf_act, B, D, F, e->pf_gu + F, e->d_err, s, 2 * F));
+        }
+        CK(glu_quant_launch(e->pf_gu, e->pf_gu + F, 2 * F, F, B, e->arch == 2, e->pf_actf, s));
+        CK(matbatch_launch(w.wd, w.td, nullptr, e->pf_actf, B, F, D, e->pf_p, e->d_err, s));
+    }
+    // last position: residual, final norm, LM head (:1185-1205)
+    const size_t last = (size_t)(B - 1) * D;
+    CU(cudaMemcpyAsync(e->hidden, e->pf_h + last, (size_t)D * 4, cudaMemcpyDeviceToDevice, s));
+    CK(add_norm_quant_launch(e->hidden, e->pf_p + last, e->out_norm, 1, D, e->eps, e->act_d, e->normed, s));
+    CK(gemv(e, e->tok_embd, e->embd_type, e->act_d, e->normed, D, e->vocab, e->logits, e->softcap));
+    return kOk;
+}
+
+static int upload_ids(Engine* e, const int32_t* ids, int n) {
+    if (n > e->ids_cap) {
+        cudaStreamSynchronize(e->stream);
+        cudaFree(e->ids_dev);
+        e->ids_dev = nullptr;
+        if (cudaMalloc(&e->ids_dev, (size_t)n * 4) != cudaSuccess) return kErrOutOfMemory;
+        e->ids_cap = n;
+    }
+    CU(cudaMemcpyAsync(e->ids_dev, ids, (size_t)n * 4, cudaMemcpyHostToDevice, e->stream));
+    return kOk;
+}
+
+static int set_state(Engine* e, int token, int pos, const int32_t* all, int n_all, int eos, int max_out) {
+    DecodeState& h = *e->st_host;
+    CU(cudaStreamSynchronize(e->stream));
+    memset(&h, 0, sizeof(h));
+    h.token = token;
+    h.pos = pos;
+    h.n_all = n_all;
+    h.eos = eos;
+    h.max_out = max_out;
+    for (int k = 0; k < n_all && k < kRecentWindow; ++k) {
+        const int idx = n_all - 1 - k;  // the last kRecentWindow tokens
+        h.ring[(idx) % kRecentWindow] = all[idx];
+    }
+    CU(cudaMemcpyAsync(e->st, &h, sizeof(h), cudaMemcpyHostToDevice, e->stream));
+    return kOk;
+}
+
+static int check_device_error(Engine* e) {
+    int32_t h = 0;
+    CU(cudaMemcpyAsync(&h, e->d_err, 4, cudaMemcpyDeviceToHost, e->stream));
+    CU(cudaStreamSynchronize(e->stream));
+    if (h) {
+        cudaMemsetAsync(e->d_err, 0, 4, e->stream);
+        e->error = "device-side wait timed out";
+        return h;
+    }
+    return kOk;
+}
+
+static const LayerW* layer_or_null(const Engine* e, int l) { return l < (int)e->L.size() ? &e->L[l] : nullptr; }
+
+// Load: read hyper-parameters, lay tensors out in one device arena, upload.
+static int engine_load(Engine* e, const char* path, int max_seq, std::string& err) {
+    Gguf g;
+    if (!gguf_open(path, g, err)) return kErrInvalidArg;
+    const std::string arch = g.str.count("general.architecture") ? g.str["general.architecture"] : "qwen3";
+    auto num = [&](const std::string& k, double d) { auto it = g.num.find(arch + "." + k); return it == g.num.end() ? d : it->second; };
+    e->arch = arch.rfind("qwen", 0) == 0 ? 0 : (arch.rfind("llama", 0) == 0 ? 1 : (arch == "gemma" ? 2 : -1));
+    if (e->arch < 0) { err = "unsupported architecture: " + arch; return kErrInvalidArg; }
+    e->n_layers = (int)num("block_count", 0);
+    e->dim = (int)num("embedding_length", 0);
+    e->nh = (int)num("attention.head_count", 0);
+    e->nkv = (int)num("attention.head_count_kv", e->nh);
+    e->hd = (int)num("attention.key_length", e->nh ? e->dim / e->nh : 0);
+    e->ffn = (int)num("feed_forward_length", 0);
+    e->eps = (float)num("attention.layer_norm_rms_epsilon", 1e-6);
+    e->rope_base = (float)num("rope.freq_base", 10000.0);
+    e->softcap = (float)num("final_logit_softcapping", 0.0);
+    e->vocab = g.arr_len.count("tokenizer.ggml.tokens") ? (int)g.arr_len["tokenizer.ggml.tokens"] : 0;
+    e->eos = g.num.count("tokenizer.ggml.eos_token_id") ? (int)g.num["tokenizer.ggml.eos_token_id"] : -1;
+    e->max_seq = max_seq;
+    e->q_dim = e->nh * e->hd;
+    e->kv_dim = e->nkv * e->hd;
+    // Lua doubles, passed to C as float (:846-862, :698-713)
+    e->attn_scale = (float)(1.0 / sqrt((double)e->hd));
+    e->embd_scale = e->arch == 2 ? (float)sqrt((double)e->dim) : 1.0f;
+    if (!e->n_layers || !e->dim || !e->nh || !e->hd || !e->ffn || !e->vocab || max_seq <= 0) {
+        err = "missing hyper-parameters";
+        return kErrInvalidArg;
+    }
+    if (e->dim % 256 || e->q_dim % 256 || e->ffn % 256 || e->hd % 32 || e->hd > 256 || e->nh % e->nkv) {
+        err = "shapes not supported (dims must be multiples of 256, head_dim a multiple of 32 up to 256)";
+        return kErrInvalidArg;
+    }
+    // ---- arena layout
+    auto T = [&](const std::string& n) -> const GgufTensor* { auto it = g.tensors.find(n); return it == g.tensors.end() ? nullptr : &it->second; };
+    struct Item { const GgufTensor* t; size_t off; };
+    std::vector<Item> items;
+    size_t off = 0;
+    auto place = [&](const GgufTensor* t, bool follow) -> size_t {
+        if (!follow) off = (off + 255) & ~(size_t)255;
+        const size_t o = off;
+        items.push_back({t, o});
+        off += t->nbytes;
+        return o;
+    };
+    struct Offs { size_t an, fn, qn, kn, q, k, v, o, gt, up, dn; bool has_qn, has_kn, qkv_f, gu_f; int tq, tk, tv, to, tg, tu, td; };
+    std::vector<Offs> lo(e->n_layers);
+    const char* lin[] = {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"};
+    for (int l = 0; l < e->n_layers; ++l) {
+        const std::string p = "blk." + std::to_string(l) + ".";
+        const GgufTensor* an = T(p + "attn_norm.weight"), *fn = T(p + "ffn_norm.weight");
+        const GgufTensor* lt[7];
+        for (int i = 0; i < 7; ++i) {
+            lt[i] = T(p + lin[i] + ".weight");
+            if (!lt[i]) { err = "missing tensor " + p + lin[i] + ".weight"; return kErrInvalidArg; }
+            const int ty = lt[i]->type;
+            if (ty != kQ4_0 && ty != kQ8_0 && ty != kQ4_K && ty != kQ6_K) { err = "unsupported weight type in " + p + lin[i]; return kErrInvalidArg; }
+        }
+        if (!an || !fn || an->type != kF32 || fn->type != kF32) { err = "missing/non-F32 norm in " + p; return kErrInvalidArg; }
+        Offs& O = lo[l];
+        O.an = place(an, false);
+        O.fn = place(fn, false);
+        const GgufTensor* qn = T(p + "attn_q_norm.weight"), *kn = T(p + "attn_k_norm.weight");
+        O.has_qn = qn && qn->type == kF32;
+        O.has_kn = kn && kn->type == kF32;
+        O.qn = O.has_qn ? place(qn, false) : 0;
+        O.kn = O.has_kn ? place(kn, false) : 0;
+        O.qkv_f = lt[0]->type == lt[1]->type && lt[1]->type == lt[2]->type;
+        O.q = place(lt[0], false);
+        O.k = place(lt[1], O.qkv_f);
+        O.v = place(lt[2], O.qkv_f);
+        O.o = place(lt[3], false);
+        O.gu_f = lt[4]->type == lt[5]->type;
+        O.gt = place(lt[4], false);
+        O.up = place(lt[5], O.gu_f);
+        O.dn = place(lt[6], false);
+        O.tq = lt[0]->type; O.tk = lt[1]->type; O.tv = lt[2]->type; O.to = lt[3]->type;
+        O.tg = lt[4]->type; O.tu = lt[5]->type; O.td = lt[6]->type;
+    }
+    const GgufTensor* emb = T("token_embd.weight");
+    const GgufTensor* onorm = T("output_norm.weight");
+    if (!emb || (emb->type != kQ8_0 && emb->type != kQ6_K && emb->type != kBF16)) {
+        err = "token_embd.weight must be Q8_0, Q6_K or BF16";  // lua/gncx_streamer.lua:700-711
+        return kErrInvalidArg;
+    }
+    if (!onorm || onorm->type != kF32) { err = "missing output_norm.weight"; return kErrInvalidArg; }
+    const size_t emb_off = place(emb, false);
+    const size_t on_off = place(onorm, false);
+    e->embd_type = emb->type;
+    e->arena_bytes = (off + 255) & ~(size_t)255;
+    CU(cudaMalloc(&e->arena, e->arena_bytes));
+    for (const Item& it : items)
+        CU(cudaMemcpyAsync(e->arena + it.off, g.base + it.t->abs_off, it.t->nbytes, cudaMemcpyHostToDevice, e->stream));
+    CU(cudaStreamSynchronize(e->stream));
+    e->tok_embd = e->arena + emb_off;
+    e->out_norm = reinterpret_cast<const float*>(e->arena + on_off);
+    // ---- KV cache
+    const size_t kv_layer = (size_t)max_seq * e->kv_dim;
+    CU(cudaMalloc(&e->kv, kv_layer * 2 * e->n_layers * 4));
+    CU(cudaMemsetAsync(e->kv, 0, kv_layer * 2 * e->n_layers * 4, e->stream));
+    e->L.resize(e->n_layers);
+    e->qk_norm = e->arch == 0;
+    for (int l = 0; l < e->n_layers; ++l) {
+        const Offs& O = lo[l];
+        LayerW& w = e->L[l];
+        w.attn_norm = reinterpret_cast<const float*>(e->arena + O.an);
+        w.ffn_norm = reinterpret_cast<const float*>(e->arena + O.fn);
+        w.q_norm = O.has_qn ? reinterpret_cast<const float*>(e->arena + O.qn) : nullptr;
+        w.k_norm = O.has_kn ? reinterpret_cast<const float*>(e->arena + O.kn) : nullptr;
+        if (e->arch == 0 && (!O.has_qn || !O.has_kn)) e->qk_norm = false;
+        w.wq = e->arena + O.q; w.wk = e->arena + O.k; w.wv = e->arena + O.v; w.wo = e->arena + O.o;
+        w.wg = e->arena + O.gt; w.wu = e->arena + O.up; w.wd = e->arena + O.dn;
+        w.tq = O.tq; w.tk = O.tk; w.tv = O.tv; w.to = O.to; w.tg = O.tg; w.tu = O.tu; w.td = O.td;
+        w.qkv_fused = O.qkv_f;
+        w.gu_fused = O.gu_f;
+        w.kc = e->kv + (size_t)2 * l * kv_layer;
+        w.vc = w.kc + kv_layer;
+    }
+    // ---- RoPE table with the reference's libm calls (:1779-1796), every position
+    const int half = e->hd / 2;
+    std::vector<float> c((size_t)max_seq * half), sn((size_t)max_seq * half), freq(half);
+    for (int i = 0; i < half; ++i) freq[i] = 1.0f / powf(e->rope_base, (float)(2 * i) / (float)e->hd);
+    for (int p = 0; p < max_seq; ++p)
+        for (int i = 0; i < half; ++i) {
+            const float ang = (float)p * freq[i];
+            c[(size_t)p * half + i] = cosf(ang);
+            sn[(size_t)p * half + i] = sinf(ang);
+        }
+    CU(cudaMalloc(&e->rope_c, c.size() * 4));
+    CU(cudaMalloc(&e->rope_s, sn.size() * 4));
+    CU(cudaMemcpy(e->rope_c, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(e->rope_s, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    // ---- decode buffers
+    const size_t D = e->dim, F = e->ffn;
+    e->max_splits = (max_seq + kDecodeChunk - 1) / kDecodeChunk;
+    CU(cudaMalloc(&e->hidden, D * 4));
+    CU(cudaMalloc(&e->normed, D * 4));
+    CU(cudaMalloc(&e->proj, D * 4));
+    CU(cudaMalloc(&e->qkv, (size_t)(e->q_dim + 2 * e->kv_dim) * 4));
+    CU(cudaMalloc(&e->gu, 2 * F * 4));
+    CU(cudaMalloc(&e->logits, (size_t)e->vocab * 4));
+    CU(cudaMalloc(&e->act_d, (D / 32) * sizeof(ActBlock)));
+    CU(cudaMalloc(&e->act_q, (size_t)(e->q_dim / 32) * sizeof(ActBlock)));
+    CU(cudaMalloc(&e->act_f, (F / 32) * sizeof(ActBlock)));
+    CU(cudaMalloc(&e->part, (size_t)e->nh * e->max_splits * (e->hd + 2) * 4));
+    CU(cudaMalloc(&e->st, sizeof(DecodeState)));
+    CU(cudaMallocHost(&e->st_host, sizeof(DecodeState)));
+    CU(cudaMalloc(&e->am_scratch, argmax_state_scratch_bytes()));
+    CU(cudaMalloc(&e->d_err, 4));
+    CU(cudaMemset(e->d_err, 0, 4));
+    e->out_cap = max_seq + 1;
+    CU(cudaMalloc(&e->out_ids, (size_t)e->out_cap * 4));
+    for (auto& ev : e->ev) CU(cudaEventCreate(&ev));
+    (void)layer_or_null;
+    return kOk;
+}
+
+static void engine_free(Engine* e) {
+    if (!e) return;
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    if (e->graph) cudaGraphExecDestroy(e->graph);
+    void* bufs[] = {e->arena, e->kv, e->rope_c, e->rope_s, e->hidden, e->normed, e->proj, e->qkv, e->gu, e->logits,
+                    e->act_d, e->act_q, e->act_f, e->part, e->st, e->am_scratch, e->d_err, e->out_ids, e->ids_dev,
+                    e->pf_h, e->pf_p, e->pf_qkv, e->pf_gu, e->pf_part, e->pf_act, e->pf_actq, e->pf_actf};
+    for (void* b : bufs)
+        if (b) cudaFree(b);
+    if (e->st_host) cudaFreeHost(e->st_host);
+    for (auto& ev : e->ev)
+        if (ev) cudaEventDestroy(ev);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+}
+
+// Capture one decode step (forward + sample) as a graph for `penalty`.
+static int build_graph(Engine* e, double penalty) {
+    if (e->graph && e->penalty_graph == penalty) return kOk;
+    if (e->graph) {
+        cudaGraphExecDestroy(e->graph);
+        e->graph = nullptr;
+    }
+    // One eager forward first: one-time setup (function attributes, occupancy
+    // queries) happens outside the capture.  It writes the KV entry the first
+    // captured step writes again with the same values.
+    CK(decode_step(e, false, penalty));
+    CU(cudaStreamSynchronize(e->stream));
+    cudaGraph_t g = nullptr;
+    CU(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    const int st = decode_step(e, true, penalty);
+    const cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+    if (st != kOk) { if (g) cudaGraphDestroy(g); return st; }
+    if (ce != cudaSuccess) { cudaGetLastError(); return kErrCuda; }
+    const cudaError_t ie = cudaGraphInstantiate(&e->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ie != cudaSuccess) { cudaGetLastError(); e->graph = nullptr; return kErrCuda; }
+    e->penalty_graph = penalty;
+    return kOk;
+}
+
+}  // namespace gncx
+
+using namespace gncx;
+
+// ---------------------------------------------------------------- C ABI
+extern "C" {
+
+void* gncx_engine_create(const char* gguf_path, int32_t max_seq_len) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    Engine* e = new Engine();
+    if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        delete e;
+        return nullptr;
+    }
+    std::string err;
+    gemv_set_pdl(true);  // engine weights are never written while decoding
+    if (engine_load(e, gguf_path, max_seq_len > 0 ? max_seq_len : 4096, err) != kOk) {
+        fprintf(stderr, "gncx_engine_create: %s\n", err.empty() ? "CUDA error" : err.c_str());
+        engine_free(e);
+        return nullptr;
+    }
+    return e;
+}
+
+void gncx_engine_destroy(void* h) { engine_free(static_cast<Engine*>(h)); }
+
+// out[0..11] = n_layers, dim, n_heads, n_kv, head_dim, ffn, vocab, max_seq, eos, arch, embd_type, qk_norm
+int32_t gncx_engine_hparams(void* h, int32_t* out) {
+    Engine* e = static_cast<Engine*>(h);
+    if (!e || !out) return kErrInvalidArg;
+    const int32_t v[12] = {e->n_layers, e->dim, e->nh, e->nkv, e->hd, e->ffn, e->vocab, e->max_seq, e->eos, e->arch,
+                           e->embd_type, e->qk_norm ? 1 : 0};
+    memcpy(out, v, sizeof(v));
+    return kOk;
+}
+
+const char* gncx_engine_error(void* h) { return h ? static_cast<Engine*>(h)->error.c_str() : "null engine"; }
+
+void* gncx_engine_stream(void* h) { return h ? static_cast<Engine*>(h)->stream : nullptr; }
+
+// lua/gncx_streamer.lua:759-965: logits of token `id` at position `pos` (host copy if logits_out).
+int32_t gncx_engine_forward_token(void* h, int32_t id, int32_t pos, float* logits_out) {
+    Engine* e = static_cast<Engine*>(h);
+    if (!e || id < 0 || id >= e->vocab || pos < 0 || pos >= e->max_seq) return kErrInvalidArg;
+    CK(set_state(e, id, pos, nullptr, 0, -1, 0));
+    CK(decode_step(e, false, 1.0));
+    if (logits_out) CU(cudaMemcpyAsync(logits_out, e->logits, (size_t)e->vocab * 4, cudaMemcpyDeviceToHost, e->stream));
+    return check_device_error(e);
+}
+
+// lua/gncx_streamer.lua:968-1208: runs the prompt from position 0, fills the KV cache.
+int32_t gncx_engine_prefill(void* h, const int32_t* ids, int32_t n, float* logits_out) {
+    Engine* e = static_cast<Engine*>(h);
+    if (!e || !ids || n <= 0 || n > e->max_seq) return kErrInvalidArg;
+    for (int i = 0; i < n; ++i)
+        if (ids[i] < 0 || ids[i] >= e->vocab) return kErrInvalidArg;
+    CU(cudaEventRecord(e->ev[0], e->stream));
+    if (n == 1) {
+        CK(set_state(e, ids[0], 0, nullptr, 0, -1, 0));
+        CK(decode_step(e, false, 1.0));
+    } else {
+        CK(upload_ids(e, ids, n));
+        CK(prefill_batch(e, n));
+    }
+    CU(cudaEventRecord(e->ev[1], e->stream));
+    if (logits_out) CU(cudaMemcpyAsync(logits_out, e->logits, (size_t)e->vocab * 4, cudaMemcpyDeviceToHost, e->stream));
+    const int st = check_device_error(e);
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e->ev[0], e->ev[1]);
+    e->prefill_ms = ms;
+    return st;
+}
+
+// Device logits of the last forward/prefill.
+const float* gncx_engine_logits(void* h) { return h ? static_cast<Engine*>(h)->logits : nullptr; }
+
+// lua/gncx_streamer.lua:1276-1311 with token ids: prefill, then greedy decode of
+// up to max_new tokens; every decode step is one CUDA graph launch driven by
+// device-resident state.  Returns the number of ids written (or -status).
+int32_t gncx_engine_generate(void* h, const int32_t* prompt, int32_t n_prompt, int32_t max_new, double penalty,
+                             int32_t eos, int32_t* out_ids) {
+    Engine* e = static_cast<Engine*>(h);
+    if (!e || !prompt || n_prompt <= 0 || max_new < 0 || !out_ids) return -kErrInvalidArg;
+    if (n_prompt >= e->max_seq) return 0;
+    if (max_new > e->max_seq - n_prompt) max_new = e->max_seq - n_prompt;
+    if (max_new == 0) return 0;
+    int st = gncx_engine_prefill(h, prompt, n_prompt, nullptr);
+    if (st != kOk) return -st;
+    if ((st = set_state(e, 0, n_prompt, prompt, n_prompt, eos, max_new)) != kOk) return -st;
+    if ((st = argmax_state_launch(e->logits, e->vocab, e->st, penalty, e->out_ids, 0, e->am_scratch, e->stream)) != kOk)
+        return -st;
+    if ((st = build_graph(e, penalty)) != kOk) return -st;
+    if (cudaEventRecord(e->ev[2], e->stream) != cudaSuccess) return -kErrCuda;
+    for (int i = 1; i < max_new; ++i)
+        if (cudaGraphLaunch(e->graph, e->stream) != cudaSuccess) return -kErrCuda;
+    if (cudaEventRecord(e->ev[3], e->stream) != cudaSuccess) return -kErrCuda;
+    DecodeState& hs = *e->st_host;
+    if (cudaMemcpyAsync(&hs, e->st, sizeof(DecodeState), cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)
+        return -kErrCuda;
+    if ((st = check_device_error(e)) != kOk) return -st;
+    const int n_out = hs.n_out < max_new ? hs.n_out : max_new;
+    if (n_out > 0 && cudaMemcpy(out_ids, e->out_ids, (size_t)n_out * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return -kErrCuda;
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e->ev[2], e->ev[3]);
+    e->decode_ms = ms;
+    e->decode_steps = max_new - 1;
+    return n_out;
+}
+
+// Device time of the last prefill and decode loop (ms) and the decode step count.
+int32_t gncx_engine_timing(void* h, double* prefill_ms, double* decode_ms, int32_t* decode_steps) {
+    Engine* e = static_cast<Engine*>(h);
+    if (!e) return kErrInvalidArg;
+    if (prefill_ms) *prefill_ms = e->prefill_ms;
+    if (decode_ms) *decode_ms = e->decode_ms;
+    if (decode_steps) *decode_steps = e->decode_steps;
+    return kOk;
+}
+
+}  // extern "C"

@@ -1,0 +1,227 @@
+// fused.cu -- the model engine's fused per-token kernels.
+//
+// The fusion boundaries follow the reference's operation order
+// (lua/gncx_streamer.lua:780-965), so every fused result equals the unfused
+// sequence bit for bit:
+//   * residual add -> RMSNorm -> activation re-quantization for the next GEMV
+//     (:871-873 / :906-908 then :793-803 / :876-887, and :955-995 in the GEMV);
+//   * per-head Q/K RMSNorm -> RoPE -> KV-cache write (:813-862);
+//   * SwiGLU / GeGLU -> re-quantization for ffn_down (:893-900);
+//   * penalized greedy argmax -> decode state update (:1229-1311), so the token
+//     loop runs from device memory under one captured CUDA graph per token.
+#include <cuda_runtime.h>
+#include "act.cuh"
+#include "common.cuh"
+#include "kernels.h"
+#include "norm.cuh"
+
+namespace gncx {
+
+static int status() { return cudaPeekAtLastError() == cudaSuccess ? kOk : kErrCuda; }
+
+// ---------------------------------------------------------------- add + norm + quantize
+// One CTA per row: hidden[r] += residual[r] (if given, written back), then
+// y = rmsnorm(hidden[r]) * w, re-quantized to act[r][dim/32] (and optionally
+// stored as fp32 in normed).
+__global__ void __launch_bounds__(256) add_norm_quant_kernel(float* hidden, const float* residual,
+                                                             const float* __restrict__ w, int dim, float eps,
+                                                             ActBlock* act, float* normed) {
+    extern __shared__ float xs[];
+    const size_t base = (size_t)blockIdx.x * dim;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+        float v = hidden[base + i];
+        if (residual) {
+            v = fadd(v, residual[base + i]);
+            hidden[base + i] = v;
+        }
+        xs[i] = v;
+    }
+    __syncthreads();
+    const float inv = rms_inv(xs, dim, eps);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int nb = dim >> 5;
+    for (int b = warp; b < nb; b += nwarps) {
+        const int i = b * 32 + lane;
+        const float v = fmul(fmul(xs[i], inv), w[i]);
+        if (normed) normed[base + i] = v;
+        warp_quantize_store(v, act + (size_t)blockIdx.x * nb + b, lane);
+    }
+}
+
+int add_norm_quant_launch(float* hidden, const float* residual, const float* w, int32_t rows, int32_t dim, float eps,
+                          ActBlock* act, float* normed, cudaStream_t st) {
+    if (!hidden || !w || !act || rows < 0 || dim <= 0 || (dim & 31)) return kErrInvalidArg;
+    if (rows == 0) return kOk;
+    const size_t smem = (size_t)dim * 4;
+    if (smem > 200 * 1024) return kErrCapacity;
+    if (smem > 48 * 1024)
+        cudaFuncSetAttribute(add_norm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    add_norm_quant_kernel<<<rows, 256, smem, st>>>(hidden, residual, w, dim, eps, act, normed);
+    return status();
+}
+
+// ---------------------------------------------------------------- Q/K norm + RoPE + KV write
+// grid (n_heads + 2*n_kv, rows): q heads are normed and rotated in place, k heads
+// normed, rotated and written to the cache at the row's position, v heads copied.
+__global__ void qkv_post_kernel(float* qkv, int row_stride, int nh, int nkv, int hd, const float* __restrict__ qn,
+                                const float* __restrict__ kn, int do_norm, float eps, const float* __restrict__ ct,
+                                const float* __restrict__ stab, int pos0, const int* pos_dev, float* kc, float* vc) {
+    extern __shared__ float xs[];
+    const int x = blockIdx.x, r = blockIdx.y;
+    const int pos = (pos_dev ? *pos_dev : pos0) + r;
+    float* row = qkv + (size_t)r * row_stride;
+    const int kvd = nkv * hd, qd = nh * hd;
+    if (x >= nh + nkv) {
+        const int jv = x - nh - nkv;
+        const float* src = row + qd + kvd + (size_t)jv * hd;
+        float* dst = vc + (size_t)pos * kvd + (size_t)jv * hd;
+        for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = src[i];
+        return;
+    }
+    const bool isq = x < nh;
+    float* vec = isq ? row + (size_t)x * hd : row + qd + (size_t)(x - nh) * hd;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) xs[i] = vec[i];
+    __syncthreads();
+    const float* w = isq ? qn : kn;
+    if (do_norm) {
+        const float inv = rms_inv(xs, hd, eps);
+        for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+            const float v = fmul(xs[i], inv);
+            xs[i] = w ? fmul(v, w[i]) : v;
+        }
+        __syncthreads();
+    }
+    const int half = hd >> 1;
+    float* dst = isq ? vec : kc + (size_t)pos * kvd + (size_t)(x - nh) * hd;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        const float c = ct[(size_t)pos * half + i], s = stab[(size_t)pos * half + i];
+        const float x1 = xs[i], x2 = xs[i + half];
+        dst[i] = fsub(fmul(x1, c), fmul(x2, s));
+        dst[i + half] = fadd(fmul(x2, c), fmul(x1, s));
+    }
+}
+
+int qkv_post_launch(float* qkv, int32_t row_stride, int32_t rows, int32_t nh, int32_t nkv, int32_t hd,
+                    const float* q_norm, const float* k_norm, bool do_norm, float eps, const float* cos_tab,
+                    const float* sin_tab, int32_t pos0, const int32_t* pos_dev, float* kc, float* vc,
+                    cudaStream_t st) {
+    if (!qkv || !cos_tab || !sin_tab || !kc || !vc || rows <= 0 || hd <= 0 || (hd & 1)) return kErrInvalidArg;
+    const int threads = hd >= 256 ? 256 : (hd >= 128 ? 128 : 64);
+    qkv_post_kernel<<<dim3(nh + 2 * nkv, rows), threads, (size_t)hd * 4, st>>>(
+        qkv, row_stride, nh, nkv, hd, q_norm, k_norm, do_norm ? 1 : 0, eps, cos_tab, sin_tab, pos0, pos_dev, kc, vc);
+    return status();
+}
+
+// ---------------------------------------------------------------- GLU + quantize
+// One warp per 32-output block: out = glu(gate, up), re-quantized for ffn_down.
+__global__ void glu_quant_kernel(const float* __restrict__ g, const float* __restrict__ u, int stride, int ffn,
+                                 int rows, int gelu, ActBlock* act) {
+    const int lane = threadIdx.x & 31;
+    const int nbf = ffn >> 5;
+    const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t r = gw / nbf;
+    if (r >= rows) return;  // whole warp
+    const int b = (int)(gw % nbf);
+    const size_t i = (size_t)r * stride + (size_t)b * 32 + lane;
+    const float v = gelu ? geglu1(g[i], u[i]) : swiglu1(g[i], u[i]);
+    warp_quantize_store(v, act + (size_t)r * nbf + b, lane);
+}
+
+int glu_quant_launch(const float* g, const float* u, int32_t stride, int32_t ffn, int32_t rows, bool gelu,
+                     ActBlock* act, cudaStream_t st) {
+    if (!g || !u || !act || ffn <= 0 || (ffn & 31) || rows < 0) return kErrInvalidArg;
+    if (rows == 0) return kOk;
+    const int64_t warps = (int64_t)rows * (ffn >> 5);
+    const int64_t blocks = (warps + 7) / 8;
+    glu_quant_kernel<<<(unsigned)blocks, 256, 0, st>>>(g, u, stride, ffn, rows, gelu ? 1 : 0, act);
+    return status();
+}
+
+// ---------------------------------------------------------------- argmax -> decode state
+// lua/gncx_streamer.lua:1229-1273 (penalty over the last <= 65 tokens, doubles,
+// first maximum wins) feeding generate (:1276-1311): the chosen token becomes
+// the next input, joins the penalty window and the output; EOS stops.
+constexpr int kAmThreads = 256;
+constexpr int kAmBlocks = 148;
+
+struct Best { double v; int i; };
+__device__ __forceinline__ Best pick(Best a, Best b) {
+    return (b.v > a.v || (b.v == a.v && b.i < a.i)) ? b : a;
+}
+
+__device__ Best am_block_best(Best p) {
+    __shared__ double sv[kAmThreads / 32];
+    __shared__ int si[kAmThreads / 32];
+    for (int o = 16; o > 0; o >>= 1) {
+        Best q;
+        q.v = __shfl_xor_sync(0xffffffffu, p.v, o);
+        q.i = __shfl_xor_sync(0xffffffffu, p.i, o);
+        p = pick(p, q);
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = p.v; si[threadIdx.x >> 5] = p.i; }
+    __syncthreads();
+    if (threadIdx.x == 0)
+        for (int k = 1; k < (int)(blockDim.x >> 5); ++k) p = pick(p, Best{sv[k], si[k]});
+    return p;
+}
+
+__global__ void am_state_stage1(const float* __restrict__ logits, int vocab, const DecodeState* st, double penalty,
+                                double* part_v, int* part_i) {
+    const int per = (vocab + gridDim.x - 1) / gridDim.x;
+    const int lo = blockIdx.x * per, hi = min(vocab, lo + per);
+    extern __shared__ unsigned pen[];
+    const int words = (per + 31) / 32;
+    for (int k = threadIdx.x; k < words; k += blockDim.x) pen[k] = 0u;
+    __syncthreads();
+    const int n = st->n_all < kRecentWindow ? st->n_all : kRecentWindow;
+    for (int k = threadIdx.x; k < n; k += blockDim.x) {
+        const int t = st->ring[k];
+        if (t >= lo && t < hi) atomicOr(&pen[(t - lo) >> 5], 1u << ((t - lo) & 31));
+    }
+    __syncthreads();
+    Best b{-1e30, 0};
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        double v = (double)logits[i];
+        if ((pen[(i - lo) >> 5] >> ((i - lo) & 31)) & 1u) v = v > 0.0 ? __ddiv_rn(v, penalty) : __dmul_rn(v, penalty);
+        if (v > b.v) { b.v = v; b.i = i; }
+    }
+    b = am_block_best(b);
+    if (threadIdx.x == 0) { part_v[blockIdx.x] = b.v; part_i[blockIdx.x] = b.i; }
+}
+
+__global__ void am_state_stage2(const double* part_v, const int* part_i, int n, DecodeState* st, int32_t* out_ids,
+                                int advance_pos) {
+    Best b{-1e30, 0};
+    for (int k = threadIdx.x; k < n; k += blockDim.x) b = pick(b, Best{part_v[k], part_i[k]});
+    b = am_block_best(b);
+    if (threadIdx.x == 0 && !st->done) {
+        const int next = b.i;
+        if (next == st->eos) {
+            st->done = 1;
+        } else {
+            if (st->n_out < st->max_out) out_ids[st->n_out] = next;
+            st->n_out += 1;
+            st->ring[st->n_all % kRecentWindow] = next;
+            st->n_all += 1;
+            st->token = next;
+            if (advance_pos) st->pos += 1;
+            if (st->n_out >= st->max_out) st->done = 1;
+        }
+    }
+}
+
+size_t argmax_state_scratch_bytes() { return (size_t)kAmBlocks * (sizeof(double) + sizeof(int)); }
+
+int argmax_state_launch(const float* logits, int32_t vocab, DecodeState* st, double penalty, int32_t* out_ids,
+                        int advance_pos, void* scratch, cudaStream_t s) {
+    if (!logits || !st || !out_ids || !scratch || vocab <= 0) return kErrInvalidArg;
+    double* pv = reinterpret_cast<double*>(scratch);
+    int* pi = reinterpret_cast<int*>(pv + kAmBlocks);
+    const int blocks = vocab < kAmBlocks * 64 ? (vocab + 63) / 64 : kAmBlocks;
+    const int per = (vocab + blocks - 1) / blocks;
+    am_state_stage1<<<blocks, kAmThreads, (size_t)((per + 31) / 32) * 4, s>>>(logits, vocab, st, penalty, pv, pi);
+    am_state_stage2<<<1, kAmThreads, 0, s>>>(pv, pi, blocks, st, out_ids, advance_pos);
+    return status();
+}
+
+}  // namespace gncx

@@ -25,8 +25,9 @@ int gemv_launch(const uint8_t* w, int32_t type, const float* x, const ActBlock* 
 // before the preceding kernel on the stream completes (weights must not be
 // written by that kernel).  Off by default.
 void gemv_set_pdl(bool on);
+// yb[t * ldy + o] (ldy = out_dim when 0)
 int matbatch_launch(const uint8_t* w, int32_t type, const float* xb, const ActBlock* act, int32_t batch,
-                    int32_t in_dim, int32_t out_dim, float* yb, int32_t* err, cudaStream_t st);
+                    int32_t in_dim, int32_t out_dim, float* yb, int32_t* err, cudaStream_t st, int32_t ldy = 0);
 // x[rows][in_dim] -> ActBlock[rows][in_dim/32]
 int act_quantize_launch(const float* x, int32_t rows, int32_t in_dim, ActBlock* out, cudaStream_t st);
 // Dequantize `rows` rows of `n` weights (row stride = row_bytes(type, n)) to fp32.
@@ -55,6 +56,28 @@ int glu_launch(const float* g, const float* u, int64_t n, float* out, bool gelu,
 int softcap_launch(float* x, int64_t n, float cap, cudaStream_t st);
 
 // ---- attention ----
+// General form: n_tok queries; query z sits at position (pos_dev ? *pos_dev : pos0) + z
+// and attends to its window; records [z][head][max_splits] of (hd + 2) floats.
+struct AttnArgs {
+    const float* q;        // query z at q + z * q_stride
+    int q_stride;
+    const float* kc;
+    const float* vc;
+    int pos0;
+    const int* pos_dev;
+    int n_heads, n_kv, hd;
+    float scale;
+    int window;
+    int chunk;             // positions per split
+    int max_splits;        // record capacity per (query, head); splits past the window exit
+    float* part;
+    float* out;            // may be null
+    int out_stride;
+    ActBlock* act_out;     // may be null: re-quantized output [z][n_heads*hd/32]
+    int32_t* err;
+};
+int attention_run(const AttnArgs& a, int32_t n_tok, cudaStream_t st);
+int attention_geometry_chunk(int32_t len, int32_t n_kv, int sm_count);
 struct AttnScratch {
     float* part;        // partial (max, sum, o[hd]) records
     int32_t capacity;   // records available
@@ -69,6 +92,31 @@ int32_t attention_scratch_records(int32_t pos, int32_t n_heads, int32_t window);
 int argmax_penalized_launch(const float* logits, int32_t vocab, const int32_t* recent, int32_t n_recent,
                             double penalty, int32_t* out_idx, void* scratch, cudaStream_t st);
 size_t argmax_scratch_bytes(int32_t vocab);
+
+// ---- fused engine kernels (fused.cu) ----
+constexpr int kRecentWindow = 65;  // tokens the repetition penalty looks back over
+struct DecodeState {
+    int32_t token;     // input token of the next step
+    int32_t pos;       // its position
+    int32_t n_all;     // prompt + generated tokens so far
+    int32_t n_out;     // generated tokens so far
+    int32_t done;
+    int32_t eos;
+    int32_t max_out;
+    int32_t pad;
+    int32_t ring[kRecentWindow];  // last kRecentWindow tokens (any order)
+};
+int add_norm_quant_launch(float* hidden, const float* residual, const float* w, int32_t rows, int32_t dim, float eps,
+                          ActBlock* act, float* normed, cudaStream_t st);
+int qkv_post_launch(float* qkv, int32_t row_stride, int32_t rows, int32_t nh, int32_t nkv, int32_t hd,
+                    const float* q_norm, const float* k_norm, bool do_norm, float eps, const float* cos_tab,
+                    const float* sin_tab, int32_t pos0, const int32_t* pos_dev, float* kc, float* vc,
+                    cudaStream_t st);
+int glu_quant_launch(const float* g, const float* u, int32_t stride, int32_t ffn, int32_t rows, bool gelu,
+                     ActBlock* act, cudaStream_t st);
+size_t argmax_state_scratch_bytes();
+int argmax_state_launch(const float* logits, int32_t vocab, DecodeState* st, double penalty, int32_t* out_ids,
+                        int advance_pos, void* scratch, cudaStream_t s);
 
 // ---- embedding ----
 int embed_launch(const uint8_t* tensor, int32_t type, const int32_t* tokens, int32_t n_tokens, int32_t dim,

@@ -33,7 +33,8 @@ struct TokAct {
 template <int T>
 __global__ void __launch_bounds__(kMbThreads) matbatch_kernel(const uint8_t* __restrict__ w, size_t rb,
                                                                const ActBlock* __restrict__ act, int batch,
-                                                               int in_dim, int out_dim, float* __restrict__ y) {
+                                                               int in_dim, int out_dim, float* __restrict__ y,
+                                                               int ldy) {
     constexpr int UB = Fmt<T>::UB, NW = Fmt<T>::NW, E = Fmt<T>::E;
     constexpr int WS = (UB + 3) / 4 + 2;  // staged words per row (aligned cover + look-ahead)
     __shared__ __align__(16) uint32_t wsm[kMbRows * WS];
@@ -104,7 +105,7 @@ __global__ void __launch_bounds__(kMbThreads) matbatch_kernel(const uint8_t* __r
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int tok = tok0 + tg * 4 + i;
-            if (tok < batch) y[(size_t)tok * out_dim + grow] = acc[i];
+            if (tok < batch) y[(size_t)tok * ldy + grow] = acc[i];
         }
     }
 }
@@ -123,13 +124,15 @@ __global__ void matbatch_bf16_kernel(const uint8_t* __restrict__ w, const float*
 }
 
 int matbatch_launch(const uint8_t* w, int32_t type, const float* xb, const ActBlock* act, int32_t batch,
-                    int32_t in_dim, int32_t out_dim, float* yb, int32_t* err, cudaStream_t st) {
+                    int32_t in_dim, int32_t out_dim, float* yb, int32_t* err, cudaStream_t st, int32_t ldy) {
     (void)err;
+    if (ldy <= 0) ldy = out_dim;
     if (!w || !yb || batch < 0 || in_dim <= 0 || out_dim < 0) return kErrInvalidArg;
     if (batch == 0 || out_dim == 0) return kOk;
     if (type == kBF16) {
         if (!xb) return kErrInvalidArg;
         const int64_t n = (int64_t)batch * out_dim;
+        if (ldy != out_dim) return kErrInvalidArg;
         matbatch_bf16_kernel<<<(int)((n + 255) / 256), 256, 0, st>>>(w, xb, batch, in_dim, out_dim, yb);
         return cudaPeekAtLastError() == cudaSuccess ? kOk : kErrCuda;
     }
@@ -138,10 +141,10 @@ int matbatch_launch(const uint8_t* w, int32_t type, const float* xb, const ActBl
     dim3 grid((out_dim + kMbRows - 1) / kMbRows, (batch + kMbToks - 1) / kMbToks);
     if (grid.y > 65535) return kErrCapacity;
     switch (type) {
-        case kQ4_0: matbatch_kernel<kQ4_0><<<grid, kMbThreads, 0, st>>>(w, rb, act, batch, in_dim, out_dim, yb); break;
-        case kQ8_0: matbatch_kernel<kQ8_0><<<grid, kMbThreads, 0, st>>>(w, rb, act, batch, in_dim, out_dim, yb); break;
-        case kQ4_K: matbatch_kernel<kQ4_K><<<grid, kMbThreads, 0, st>>>(w, rb, act, batch, in_dim, out_dim, yb); break;
-        case kQ6_K: matbatch_kernel<kQ6_K><<<grid, kMbThreads, 0, st>>>(w, rb, act, batch, in_dim, out_dim, yb); break;
+        case kQ4_0: matbatch_kernel<kQ4_0><<<grid, kMbThreads, 0, st>>>(w, rb, act, batch, in_dim, out_dim, yb, ldy); break;
+        case kQ8_0: matbatch_kernel<kQ8_0><<<grid, kMbThreads, 0, st>>>(w, rb, act, batch, in_dim, out_dim, yb, ldy); break;
+        case kQ4_K: matbatch_kernel<kQ4_K><<<grid, kMbThreads, 0, st>>>(w, rb, act, batch, in_dim, out_dim, yb, ldy); break;
+        case kQ6_K: matbatch_kernel<kQ6_K><<<grid, kMbThreads, 0, st>>>(w, rb, act, batch, in_dim, out_dim, yb, ldy); break;
         default: return kErrInvalidArg;
     }
     return cudaPeekAtLastError() == cudaSuccess ? kOk : kErrCuda;

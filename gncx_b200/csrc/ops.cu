@@ -6,6 +6,7 @@
 #include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "norm.cuh"
 
 namespace gncx {
 
@@ -132,44 +133,8 @@ int embed_launch(const uint8_t* tensor, int32_t type, const int32_t* tokens, int
     return dequant_launch(tensor, type, n_tokens, dim, scale, tokens, out, st);
 }
 
-// ---------------- RMSNorm (:789-840, :895-953) ----------------
-// The reference forms sum(x^2) in four fp32 lanes over i = 4k+j (serial in k),
-// widens the lanes to double and adds them in order, adds any tail in double,
-// then inv = 1 / sqrtf((float)(sum/n) + eps) and y = (x * inv) * w.  The four
-// serial chains are reproduced literally by four threads reading the row from
-// shared memory; everything else is parallel.
+// ---------------- RMSNorm (:789-840, :895-953): see norm.cuh ----------------
 constexpr int kNormThreads = 256;
-
-__device__ __forceinline__ float rms_inv(const float* xs, int n, float eps) {
-    // called by all threads; returns inv in every thread
-    __shared__ float s_inv;
-    const int tid = threadIdx.x;
-    if (tid < 32) {
-        float acc = 0.0f;
-        const int n4 = n & ~3;
-        if (tid < 4) {
-#pragma unroll 8
-            for (int i = tid; i < n4; i += 4) {
-                const float v = xs[i];
-                acc = fadd(acc, fmul(v, v));
-            }
-        }
-        const float a1 = __shfl_sync(0xffffffffu, acc, 1);
-        const float a2 = __shfl_sync(0xffffffffu, acc, 2);
-        const float a3 = __shfl_sync(0xffffffffu, acc, 3);
-        if (tid == 0) {
-            double s = __dadd_rn(__dadd_rn(__dadd_rn((double)acc, (double)a1), (double)a2), (double)a3);
-            for (int i = n4; i < n; ++i) {
-                const double v = (double)xs[i];
-                s = __dadd_rn(s, __dmul_rn(v, v));
-            }
-            const float ms = __double2float_rn(__ddiv_rn(s, (double)n));
-            s_inv = fdiv(1.0f, __fsqrt_rn(fadd(ms, eps)));
-        }
-    }
-    __syncthreads();
-    return s_inv;
-}
 
 // One CTA per (row, head); rows of `n_heads * head_dim` floats; out may alias x.
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* x, const float* __restrict__ w, float* out,
@@ -288,17 +253,6 @@ int absmax_launch(const float* x, int32_t n, float* out, cudaStream_t st) {
 }
 
 // ---------------- GLU activations (:2018-2052) ----------------
-__device__ __forceinline__ float swiglu1(float g, float u) {
-    const float silu = fdiv(g, fadd(1.0f, exp_cr(-g)));
-    return fmul(silu, u);
-}
-__device__ __forceinline__ float geglu1(float x, float u) {
-    const float k0 = 0.7978845608028654f;
-    const float inner = fmul(k0, fadd(x, fmul(fmul(fmul(0.044715f, x), x), x)));
-    const float gelu = fmul(fmul(0.5f, x), fadd(1.0f, tanh_cr(inner)));
-    return fmul(gelu, u);
-}
-
 __global__ void glu_kernel(const float* __restrict__ g, const float* __restrict__ u, int64_t n, float* out, int gelu) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         out[i] = gelu ? geglu1(g[i], u[i]) : swiglu1(g[i], u[i]);

@@ -245,3 +245,82 @@ class RefLib:
 
 def reference_available(strict: bool = True) -> bool:
     return (REF_STRICT_SO if strict else REF_NATIVE_SO).exists()
+
+
+class OracleModel:
+    """Whole-model CPU oracle (oracle/gncx_oracle_model.c) over a GGUF file:
+    the reference orchestrator's forward_token / prefill / generate, with the
+    kernels of the reference library itself (``ref_lib``) or of the C
+    restatement (``ref_lib=None``)."""
+
+    NT = 11  # tensors per layer in the descriptor
+
+    class _Desc(ctypes.Structure):
+        _fields_ = [("n_layers", c_int32), ("dim", c_int32), ("n_heads", c_int32), ("n_kv", c_int32),
+                    ("head_dim", c_int32), ("ffn_dim", c_int32), ("vocab", c_int32), ("max_seq", c_int32),
+                    ("eps", c_float), ("rope_base", c_float), ("softcap", c_float), ("arch", c_int32),
+                    ("base", c_void_p), ("tok_embd_off", ctypes.c_uint64), ("tok_embd_type", c_int32),
+                    ("out_norm_off", ctypes.c_uint64), ("off", c_void_p), ("typ", c_void_p)]
+
+    def __init__(self, gguf_path, max_seq: int, ref_lib: Path | None = REF_STRICT_SO):
+        from gncx_b200 import gguf as _gguf
+        o = Oracle()
+        L = o.lib
+        L.orc_model_create.restype = c_void_p
+        L.orc_model_create.argtypes = [c_void_p, c_char_p]
+        L.orc_model_destroy.argtypes = [c_void_p]
+        L.orc_model_forward.restype = c_void_p
+        L.orc_model_forward.argtypes = [c_void_p, c_int32, c_int32]
+        L.orc_model_prefill.restype = c_void_p
+        L.orc_model_prefill.argtypes = [c_void_p, c_void_p, c_int32]
+        L.orc_model_generate.restype = c_int32
+        L.orc_model_generate.argtypes = [c_void_p, c_void_p, c_int32, c_int32, c_double, c_int32, c_void_p]
+        self.lib = L
+        g = _gguf.read(gguf_path)
+        hp = _gguf.model_desc(g)
+        self.hp = hp
+        self.mm = np.memmap(gguf_path, dtype=np.uint8, mode="r")
+        names = ["attn_norm", "attn_q", "attn_k", "attn_v", "attn_q_norm", "attn_k_norm", "attn_output", "ffn_norm",
+                 "ffn_gate", "ffn_up", "ffn_down"]
+        off = np.full((hp["n_layers"], self.NT), np.iinfo(np.uint64).max, dtype=np.uint64)
+        typ = np.zeros((hp["n_layers"], self.NT), dtype=np.int32)
+        for l in range(hp["n_layers"]):
+            for i, n in enumerate(names):
+                t = g.tensors.get(f"blk.{l}.{n}.weight")
+                if t is not None:
+                    off[l, i] = t.abs_offset
+                    typ[l, i] = t.ggml_type
+        self._off, self._typ = off, typ
+        emb = g.tensors["token_embd.weight"]
+        arch = {"qwen": 0, "llam": 1, "gemm": 2}.get(hp["arch"][:4], 0)
+        d = self._Desc(hp["n_layers"], hp["dim"], hp["n_heads"], hp["n_kv"], hp["head_dim"], hp["ffn"], hp["vocab"],
+                       int(max_seq), hp["eps"], hp["rope_base"], hp["softcap"], arch,
+                       self.mm.ctypes.data_as(c_void_p), emb.abs_offset, emb.ggml_type,
+                       g.tensors["output_norm.weight"].abs_offset, off.ctypes.data_as(c_void_p),
+                       typ.ctypes.data_as(c_void_p))
+        lib_path = str(ref_lib).encode() if ref_lib is not None and Path(ref_lib).exists() else None
+        self.kind = "reference" if lib_path else "port"
+        self.h = L.orc_model_create(ctypes.byref(d), lib_path)
+        if not self.h:
+            raise RuntimeError("oracle model creation failed")
+
+    def forward_token(self, tok: int, pos: int) -> np.ndarray:
+        p = self.lib.orc_model_forward(self.h, tok, pos)
+        return np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(c_float)), (self.hp["vocab"],)).copy()
+
+    def prefill(self, ids) -> np.ndarray:
+        a = np.ascontiguousarray(ids, dtype=np.int32)
+        p = self.lib.orc_model_prefill(self.h, a.ctypes.data_as(c_void_p), a.size)
+        return np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(c_float)), (self.hp["vocab"],)).copy()
+
+    def generate(self, prompt, max_new: int, penalty: float = 1.15, eos: int = -1) -> list[int]:
+        a = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(max(1, max_new), np.int32)
+        n = self.lib.orc_model_generate(self.h, a.ctypes.data_as(c_void_p), a.size, max_new, penalty, eos,
+                                        out.ctypes.data_as(c_void_p))
+        return out[:n].tolist()
+
+    def close(self):
+        if self.h:
+            self.lib.orc_model_destroy(self.h)
+            self.h = None
