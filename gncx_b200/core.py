@@ -94,6 +94,8 @@ _SIGS = {
     "gncx_get_stream": (c_void_p, []),
     "gncx_set_synchronous": (None, [c_int32]),
     "gncx_set_weight_prefetch": (None, [c_int32]),
+    "gncx_set_exact_attention": (None, [c_int32]),
+    "gncx_engine_set_exact": (c_int32, [c_void_p, c_int32]),
     "gncx_device_count": (c_int32, []),
     "gncx_set_device": (c_int32, [c_int32]),
     "gncx_device_alloc": (c_void_p, [c_size_t]),

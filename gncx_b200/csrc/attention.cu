@@ -46,7 +46,7 @@ __device__ __forceinline__ void attn_window(const AttnArgs& a, int z, int& t0, i
 }
 
 // Partial record layout per (query, head, split): [0] = max, [1] = sum of exp, [2..] = o[hd]
-template <bool BULK>
+template <bool BULK, bool SCORES_ONLY>
 __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnArgs a) {
     extern __shared__ __align__(128) uint8_t smraw[];
     const int z = blockIdx.z;
@@ -83,17 +83,19 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
             const uint32_t bytes = (uint32_t)hd * 4;
             if (lane == 0) {
                 mbar_arrive_expect_tx(&bar[0], bytes * cn);
-                mbar_arrive_expect_tx(&bar[1], bytes * cn);
+                if (!SCORES_ONLY) mbar_arrive_expect_tx(&bar[1], bytes * cn);
             }
             __syncwarp();
             for (int p = lane; p < cn; p += 32) bulk_g2s(ks + (size_t)p * rs, a.kc + row0 + (size_t)p * kvd, bytes, &bar[0]);
-            for (int p = lane; p < cn; p += 32) bulk_g2s(vs + (size_t)p * rs, a.vc + row0 + (size_t)p * kvd, bytes, &bar[1]);
+            if (!SCORES_ONLY)
+                for (int p = lane; p < cn; p += 32)
+                    bulk_g2s(vs + (size_t)p * rs, a.vc + row0 + (size_t)p * kvd, bytes, &bar[1]);
         }
     } else {
         for (int i = tid; i < cn * hd; i += blockDim.x) {
             const int p = i / hd, d = i % hd;
             ks[(size_t)p * rs + d] = a.kc[row0 + (size_t)p * kvd + d];
-            vs[(size_t)p * rs + d] = a.vc[row0 + (size_t)p * kvd + d];
+            if (!SCORES_ONLY) vs[(size_t)p * rs + d] = a.vc[row0 + (size_t)p * kvd + d];
         }
     }
     const float* qz = a.q + (size_t)z * a.q_stride + (size_t)kvh * G * hd;
@@ -125,10 +127,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
                 float dot = fadd(y, __shfl_down_sync(0xffffffffu, y, 2));
                 if (j == 0 && ok) {
                     for (int d = nm * 8; d < hd; ++d) dot = fadd(dot, fmul(qg[d], kt[d]));
-                    sc[g * chunk + p] = fmul(dot, a.scale);
+                    const float sv = fmul(dot, a.scale);
+                    if (SCORES_ONLY)
+                        a.scores[((size_t)z * a.n_heads + kvh * G + g) * a.score_cap + c0 + p] = sv;
+                    else
+                        sc[g * chunk + p] = sv;
                 }
             }
         }
+    }
+    if (SCORES_ONLY) {  // the K copies have all landed (waited above)
+        if (timed_out && tid == 0) record_error(a.err, kErrTimeout);
+        return;
     }
     __syncthreads();
 
@@ -213,11 +223,63 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
     }
 }
 
+// Exact softmax * V in the reference's order (:1960-1987): max over the
+// window, e_t = exp(s_t - max) (correctly rounded here; the reference uses the
+// host expf), sum_exp serially over t, inv = 1/(sum_exp + 1e-12),
+// out[d] += (e_t * inv) * v_t[d] serially over t.  One CTA per (query, head).
+__global__ void attn_exact_kernel(const AttnArgs a) {
+    const int h = blockIdx.x, z = blockIdx.y;
+    const int hd = a.hd, G = a.n_heads / a.n_kv, kvh = h / G, kvd = a.n_kv * hd;
+    int t0, len;
+    attn_window(a, z, t0, len);
+    float* sc = a.scores + ((size_t)z * a.n_heads + h) * a.score_cap;
+    __shared__ float red[32];
+    __shared__ float s_inv;
+    float mx = -1e30f;  // the reference starts its running max at -1e30
+    for (int t = threadIdx.x; t < len; t += blockDim.x) mx = fmaxf(mx, sc[t]);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int k = 1; k < (int)(blockDim.x >> 5); ++k) mx = fmaxf(mx, red[k]);
+    for (int t = threadIdx.x; t < len; t += blockDim.x) sc[t] = exp_cr(fsub(sc[t], mx));
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float sum = 0.0f;
+        for (int t = 0; t < len; ++t) sum = fadd(sum, sc[t]);
+        s_inv = fdiv(1.0f, fadd(sum, 1e-12f));
+    }
+    __syncthreads();
+    const float inv = s_inv;
+    const float* vbase = a.vc + (size_t)t0 * kvd + (size_t)kvh * hd;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float o = 0.0f;
+#pragma unroll 8
+        for (int t = 0; t < len; ++t) o = fadd(o, fmul(fmul(sc[t], inv), vbase[(size_t)t * kvd + d]));
+        if (a.out) a.out[(size_t)z * a.out_stride + (size_t)h * hd + d] = o;
+        if (a.act_out) {
+            ActBlock* dst = a.act_out + (size_t)z * (a.n_heads * hd / 32) + ((size_t)h * hd + d) / 32;
+            warp_quantize_store(o, dst, d & 31);
+        }
+    }
+}
+
 int attention_geometry_chunk(int32_t len, int32_t n_kv, int sm_count) {
     int c = 64;
     // shorter chunks when the window is small, so every SM gets ~2 CTAs
     while (c > 16 && (int64_t)((len + c - 1) / c) * n_kv < 2 * (int64_t)sm_count) c >>= 1;
     return c;
+}
+
+template <bool BULK, bool SCORES_ONLY>
+static void launch_partial(const AttnArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
+    static size_t set_bytes = 0;
+    if (smem > set_bytes) {
+        cudaFuncSetAttribute(attn_partial_kernel<BULK, SCORES_ONLY>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+        set_bytes = smem;
+    }
+    attn_partial_kernel<BULK, SCORES_ONLY><<<grid, kAttnThreads, smem, st>>>(a);
 }
 
 int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
@@ -233,21 +295,17 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
     if (smem > (size_t)dev.max_smem_optin) return kErrCapacity;
     const bool bulk = ((uintptr_t)a.kc % 16 == 0) && ((uintptr_t)a.vc % 16 == 0);
     dim3 grid(a.max_splits, a.n_kv, n_tok);
-    if (bulk) {
-        static size_t set_bytes = 0;
-        if (smem > set_bytes) {
-            cudaFuncSetAttribute(attn_partial_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            set_bytes = smem;
-        }
-        attn_partial_kernel<true><<<grid, kAttnThreads, smem, st>>>(a);
-    } else {
-        static size_t set_bytes = 0;
-        if (smem > set_bytes) {
-            cudaFuncSetAttribute(attn_partial_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            set_bytes = smem;
-        }
-        attn_partial_kernel<false><<<grid, kAttnThreads, smem, st>>>(a);
+    if (a.exact) {
+        if (!a.scores || a.score_cap < a.max_splits * a.chunk) return kErrCapacity;
+        if (a.act_out && a.hd > 1024) return kErrInvalidArg;
+        if (bulk) launch_partial<true, true>(a, grid, smem, st);
+        else launch_partial<false, true>(a, grid, smem, st);
+        const int threads = (a.act_out || (a.hd % 32 == 0 && a.hd <= 1024)) ? a.hd : 128;
+        attn_exact_kernel<<<dim3(a.n_heads, n_tok), threads, 0, st>>>(a);
+        return cudaPeekAtLastError() == cudaSuccess ? kOk : kErrCuda;
     }
+    if (bulk) launch_partial<true, false>(a, grid, smem, st);
+    else launch_partial<false, false>(a, grid, smem, st);
     const size_t csm = (size_t)a.max_splits * 4;
     if (csm > 48 * 1024)
         cudaFuncSetAttribute(attn_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csm);
@@ -264,7 +322,7 @@ int32_t attention_scratch_records(int32_t pos, int32_t n_heads, int32_t window) 
 
 int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t n_heads, int32_t n_kv,
                      int32_t head_dim, float scale, int32_t window, float* out, const AttnScratch& scratch,
-                     int32_t* err, cudaStream_t st) {
+                     int32_t* err, cudaStream_t st, float* exact_scores) {
     if (!q || !kc || !vc || !out || pos < 0 || n_heads <= 0 || n_kv <= 0 || head_dim <= 0) return kErrInvalidArg;
     const int32_t t0 = window > 0 ? (pos - window + 1 > 0 ? pos - window + 1 : 0) : 0;
     const int32_t len = pos + 1 - t0;
@@ -288,6 +346,9 @@ int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t 
     a.out_stride = n_heads * head_dim;
     a.act_out = nullptr;
     a.err = err;
+    a.exact = exact_scores != nullptr;
+    a.scores = exact_scores;
+    a.score_cap = a.max_splits * a.chunk;
     return attention_run(a, 1, st);
 }
 

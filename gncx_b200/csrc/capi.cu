@@ -243,6 +243,9 @@ void gncx_set_synchronous(int32_t on) { g_rt.synchronous = on != 0; }
 
 void gncx_set_weight_prefetch(int32_t on) { gemv_set_pdl(on != 0); }
 
+static bool g_exact_attention = false;
+void gncx_set_exact_attention(int32_t on) { g_exact_attention = on != 0; }
+
 int32_t gncx_device_count(void) {
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess) {
@@ -622,10 +625,14 @@ void gncx_mqa_attention_step_ext(const float* q_vec, const float* k_vec, const f
         cudaMemcpyAsync(vc + (size_t)pos * kvd, v, kvd * 4, cudaMemcpyDefault, stream());
     }
     const int32_t recs = attention_scratch_records(pos, n_heads, window);
-    float* part = reinterpret_cast<float*>(workspace((size_t)recs * (hd + 2) * 4));
-    if (!part) return;
+    const size_t part_bytes = align256((size_t)recs * (hd + 2) * 4);
+    const size_t score_floats = (size_t)n_heads * (((size_t)pos + 1 + 63) / 64 * 64);
+    uint8_t* ws = workspace(part_bytes + (g_exact_attention ? score_floats * 4 : 0));
+    if (!ws) return;
+    float* part = reinterpret_cast<float*>(ws);
+    float* scores = g_exact_attention ? reinterpret_cast<float*>(ws + part_bytes) : nullptr;
     finish(attention_launch(q, kc, vc, pos, n_heads, n_kv, hd, attn_scale, window, out, AttnScratch{part, recs},
-                            g_rt.d_err, stream()));
+                            g_rt.d_err, stream(), scores));
 }
 
 void gncx_mqa_attention_step(const float* q_vec, const float* k_vec, const float* v_vec, float* k_cache,

@@ -180,6 +180,9 @@ struct Engine {
     ActBlock *act_d = nullptr, *act_q = nullptr, *act_f = nullptr;
     float* part = nullptr;
     int max_splits = 0;
+    bool exact = false;      // exact serial softmax in attention
+    float* scores = nullptr; // [n_heads][max_splits * chunk] (decode, exact mode)
+    int graph_exact = -1;
     DecodeState* st = nullptr;
     DecodeState* st_host = nullptr;  // pinned staging
     int32_t* out_ids = nullptr;
@@ -198,6 +201,8 @@ struct Engine {
     // prefill buffers (grown on demand)
     int pf_cap = 0;
     float *pf_h = nullptr, *pf_p = nullptr, *pf_qkv = nullptr, *pf_gu = nullptr, *pf_part = nullptr;
+    float* pf_scores = nullptr;
+    size_t pf_score_cap = 0;
     ActBlock *pf_act = nullptr, *pf_actq = nullptr, *pf_actf = nullptr;
     size_t pf_part_floats = 0;
 };
@@ -260,6 +265,9 @@ static int decode_step(Engine* e, bool sample, double penalty) {
         a.out_stride = QD;
         a.act_out = e->act_q;
         a.err = e->d_err;
+        a.exact = e->exact ? 1 : 0;
+        a.scores = e->scores;
+        a.score_cap = e->max_splits * kDecodeChunk;
         CK(attention_run(a, 1, s));
         CK(gemv(e, w.wo, w.to, e->act_q, nullptr, QD, D, e->proj));
         CK(add_norm_quant_launch(e->hidden, e->proj, w.ffn_norm, 1, D, e->eps, e->act_d, e->normed, s));
@@ -282,7 +290,8 @@ static int ensure_prefill(Engine* e, int B) {
     if (B <= e->pf_cap) return kOk;
     cudaStreamSynchronize(e->stream);
     cudaFree(e->pf_h); cudaFree(e->pf_p); cudaFree(e->pf_qkv); cudaFree(e->pf_gu); cudaFree(e->pf_part);
-    cudaFree(e->pf_act); cudaFree(e->pf_actq); cudaFree(e->pf_actf);
+    cudaFree(e->pf_act); cudaFree(e->pf_actq); cudaFree(e->pf_actf); cudaFree(e->pf_scores);
+    e->pf_scores = nullptr;
     e->pf_cap = 0;
     const size_t D = e->dim, QKV = e->q_dim + 2 * e->kv_dim, F = e->ffn;
     const int grp = B < kPrefillGroup ? B : kPrefillGroup;
@@ -293,10 +302,12 @@ static int ensure_prefill(Engine* e, int B) {
         cudaMalloc(&e->pf_part, e->pf_part_floats * 4) ||
         cudaMalloc(&e->pf_act, (size_t)B * (D / 32) * sizeof(ActBlock)) ||
         cudaMalloc(&e->pf_actq, (size_t)B * (e->q_dim / 32) * sizeof(ActBlock)) ||
-        cudaMalloc(&e->pf_actf, (size_t)B * (F / 32) * sizeof(ActBlock))) {
+        cudaMalloc(&e->pf_actf, (size_t)B * (F / 32) * sizeof(ActBlock)) ||
+        cudaMalloc(&e->pf_scores, (size_t)grp * e->nh * splits * kDecodeChunk * 4)) {
         cudaGetLastError();
         return kErrOutOfMemory;
     }
+    e->pf_score_cap = splits * kDecodeChunk;
     e->pf_cap = B;
     return kOk;
 }
@@ -343,6 +354,9 @@ static int prefill_batch(Engine* e, int B) {
             a.out_stride = QD;
             a.act_out = e->pf_actq + (size_t)z0 * (QD / 32);
             a.err = e->d_err;
+            a.exact = e->exact ? 1 : 0;
+            a.scores = e->pf_scores;
+            a.score_cap = (int)e->pf_score_cap;
             if ((size_t)nz * e->nh * a.max_splits * (e->hd + 2) > e->pf_part_floats) return kErrCapacity;
             CK(attention_run(a, nz, s));
         }
@@ -553,6 +567,7 @@ static int engine_load(Engine* e, const char* path, int max_seq, std::string& er
     CU(cudaMalloc(&e->act_q, (size_t)(e->q_dim / 32) * sizeof(ActBlock)));
     CU(cudaMalloc(&e->act_f, (F / 32) * sizeof(ActBlock)));
     CU(cudaMalloc(&e->part, (size_t)e->nh * e->max_splits * (e->hd + 2) * 4));
+    CU(cudaMalloc(&e->scores, (size_t)e->nh * e->max_splits * kDecodeChunk * 4));
     CU(cudaMalloc(&e->st, sizeof(DecodeState)));
     CU(cudaMallocHost(&e->st_host, sizeof(DecodeState)));
     CU(cudaMalloc(&e->am_scratch, argmax_state_scratch_bytes()));
@@ -569,7 +584,7 @@ static void engine_free(Engine* e) {
     if (!e) return;
     if (e->stream) cudaStreamSynchronize(e->stream);
     if (e->graph) cudaGraphExecDestroy(e->graph);
-    void* bufs[] = {e->arena, e->kv, e->rope_c, e->rope_s, e->hidden, e->normed, e->proj, e->qkv, e->gu, e->logits,
+    void* bufs[] = {e->scores, e->pf_scores, e->arena, e->kv, e->rope_c, e->rope_s, e->hidden, e->normed, e->proj, e->qkv, e->gu, e->logits,
                     e->act_d, e->act_q, e->act_f, e->part, e->st, e->am_scratch, e->d_err, e->out_ids, e->ids_dev,
                     e->pf_h, e->pf_p, e->pf_qkv, e->pf_gu, e->pf_part, e->pf_act, e->pf_actq, e->pf_actf};
     for (void* b : bufs)
@@ -583,7 +598,7 @@ static void engine_free(Engine* e) {
 
 // Capture one decode step (forward + sample) as a graph for `penalty`.
 static int build_graph(Engine* e, double penalty) {
-    if (e->graph && e->penalty_graph == penalty) return kOk;
+    if (e->graph && e->penalty_graph == penalty && e->graph_exact == (int)e->exact) return kOk;
     if (e->graph) {
         cudaGraphExecDestroy(e->graph);
         e->graph = nullptr;
@@ -603,6 +618,7 @@ static int build_graph(Engine* e, double penalty) {
     cudaGraphDestroy(g);
     if (ie != cudaSuccess) { cudaGetLastError(); e->graph = nullptr; return kErrCuda; }
     e->penalty_graph = penalty;
+    e->graph_exact = (int)e->exact;
     return kOk;
 }
 
@@ -643,6 +659,15 @@ int32_t gncx_engine_hparams(void* h, int32_t* out) {
     const int32_t v[12] = {e->n_layers, e->dim, e->nh, e->nkv, e->hd, e->ffn, e->vocab, e->max_seq, e->eos, e->arch,
                            e->embd_type, e->qk_norm ? 1 : 0};
     memcpy(out, v, sizeof(v));
+    return kOk;
+}
+
+// 1: exact serial softmax in attention (bit-exact with the reference up to expf
+// rounding); 0 (default): split-KV softmax.
+int32_t gncx_engine_set_exact(void* h, int32_t on) {
+    Engine* e = static_cast<Engine*>(h);
+    if (!e) return kErrInvalidArg;
+    e->exact = on != 0;
     return kOk;
 }
 

@@ -75,6 +75,12 @@ struct AttnArgs {
     int out_stride;
     ActBlock* act_out;     // may be null: re-quantized output [z][n_heads*hd/32]
     int32_t* err;
+    // exact mode: scores go to `scores` [z][head][score_cap] and the softmax sum
+    // and the probability-weighted V sum are formed serially in position order,
+    // as the reference does (bit-exact up to the host libm's expf rounding).
+    int exact;
+    float* scores;
+    int score_cap;
 };
 int attention_run(const AttnArgs& a, int32_t n_tok, cudaStream_t st);
 int attention_geometry_chunk(int32_t len, int32_t n_kv, int sm_count);
@@ -82,9 +88,11 @@ struct AttnScratch {
     float* part;        // partial (max, sum, o[hd]) records
     int32_t capacity;   // records available
 };
+// exact_scores: null for the split-KV softmax, else n_heads * (window rounded up
+// to 64) floats for the exact serial softmax.
 int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t n_heads, int32_t n_kv,
                      int32_t head_dim, float scale, int32_t window, float* out, const AttnScratch& scratch,
-                     int32_t* err, cudaStream_t st);
+                     int32_t* err, cudaStream_t st, float* exact_scores = nullptr);
 int32_t attention_scratch_records(int32_t pos, int32_t n_heads, int32_t window);
 
 // ---- sampling ----

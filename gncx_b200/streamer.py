@@ -16,7 +16,8 @@ from . import core
 
 
 class GNCXStreamer:
-    def __init__(self, model_path: str | Path, max_seq_len: int = 4096, device: int | None = None):
+    def __init__(self, model_path: str | Path, max_seq_len: int = 4096, device: int | None = None,
+                 exact_attention: bool = False):
         self.lib = core.load()
         if device is not None:
             if self.lib.gncx_set_device(int(device)) != 0:
@@ -28,6 +29,12 @@ class GNCXStreamer:
         self.lib.gncx_engine_hparams(self.handle, hp)
         (self.n_layers, self.embed_dim, self.n_heads, self.n_kv_heads, self.head_dim, self.ffn_dim, self.vocab_size,
          self.max_seq_len, self.eos_id, self.arch, self.embd_type, self.qk_norm) = list(hp)
+        self.set_exact_attention(exact_attention)
+
+    def set_exact_attention(self, on: bool) -> None:
+        """Exact serial softmax (the reference's summation order; bit-exact up to
+        expf rounding) or the split-KV softmax (default, ~1e-6 relative)."""
+        self.lib.gncx_engine_set_exact(self.handle, 1 if on else 0)
 
     # -- lifecycle --------------------------------------------------------
     def close(self) -> None:

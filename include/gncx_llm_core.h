@@ -154,6 +154,10 @@ void gncx_set_synchronous(int32_t on);       /* 1 (default): reference-named cal
  * and outputs still wait.  Only valid while weights are not written by GPU
  * work queued just before the GEMV.  Default 0. */
 void gncx_set_weight_prefetch(int32_t on);
+/* 1: attention forms its softmax sum and weighted V sum serially in position
+ * order, as the reference does (bit-exact up to expf rounding; slower at long
+ * context).  0 (default): split-KV softmax, ~1e-6 relative. */
+void gncx_set_exact_attention(int32_t on);
 int32_t gncx_device_count(void);
 int32_t gncx_set_device(int32_t device);
 

@@ -44,12 +44,13 @@ def _check_logits(lg):
 
 @pytest.mark.parametrize("wtype", [Q4_K, Q6_K, Q8_0])
 def test_tiny_model_stream(tmp_path, oracle_model_cls, wtype):
+    """Exact-softmax mode: the token stream is identical to the reference's."""
     from gncx_b200.streamer import GNCXStreamer
     path = gguf.write_random_model(tmp_path / "tiny.gguf", TINY, seed=3, wtype=wtype)
     rng = np.random.default_rng(wtype)
     prompt = rng.integers(0, TINY["vocab"], 37).tolist()
-    ref = oracle_model_cls(path, 160, )
-    with GNCXStreamer(path, max_seq_len=160) as eng:
+    ref = oracle_model_cls(path, 160)
+    with GNCXStreamer(path, max_seq_len=160, exact_attention=True) as eng:
         lg = eng.prefill(prompt)
         lr = ref.prefill(prompt)
         _check_logits(lr)
@@ -75,6 +76,26 @@ def test_tiny_model_stream(tmp_path, oracle_model_cls, wtype):
         assert len(set(want)) > 20  # a diverse stream
 
 
+@pytest.mark.parametrize("wtype", [Q4_K, Q6_K])
+def test_tiny_model_fast_attention(tmp_path, oracle_model_cls, wtype):
+    """Split-KV softmax mode: logits within tolerance at every step."""
+    from gncx_b200.streamer import GNCXStreamer
+    path = gguf.write_random_model(tmp_path / "tiny.gguf", TINY, seed=6, wtype=wtype)
+    prompt = np.random.default_rng(7).integers(0, TINY["vocab"], 50).tolist()
+    ref = oracle_model_cls(path, 128)
+    with GNCXStreamer(path, max_seq_len=128) as eng:
+        lg, lr = eng.prefill(prompt), ref.prefill(prompt)
+        assert rel(lg, lr) <= 1e-4
+        ids = list(prompt)
+        for step in range(24):
+            t = ref_sample(lr, ids)
+            ids.append(t)
+            lr = ref.forward_token(t, len(ids) - 1)
+            lg = eng.forward_token(t, len(ids) - 1)
+            assert rel(lg, lr) <= 1e-4, step
+    ref.close()
+
+
 def ref_sample(logits, recent, penalty=1.15):
     from oracle.oracle import Oracle
     return Oracle().sample_greedy(logits, recent, penalty)
@@ -91,13 +112,19 @@ def test_qwen3_0p6b_config(tmp_path, oracle_model_cls):
     lr = ref.prefill(prompt)
     ref.close()
     _check_logits(lr)
-    with GNCXStreamer(path, max_seq_len=128 + 256) as eng:
+    with GNCXStreamer(path, max_seq_len=128 + 256, exact_attention=True) as eng:
         lg = eng.prefill(prompt)
         assert rel(lg, lr) <= LOGIT_TOL
         got = eng.generate_ids(prompt, 256, 1.15, eos_id=-1)
         t = eng.timing()
+        eng.set_exact_attention(False)
+        fast = eng.generate_ids(prompt, 256, 1.15, eos_id=-1)
     assert got == want
     assert t["decode_steps"] == 255 and t["decode_ms"] > 0
+    # split-KV mode: report how far it agrees (a near-tie may flip late)
+    agree = next((i for i, (a, b) in enumerate(zip(fast, want)) if a != b), len(want))
+    print(f"split-KV softmax stream agrees for {agree} of {len(want)} tokens")
+    assert agree >= 64
 
 
 def test_engine_rejects_bad_input(tmp_path):
