@@ -231,6 +231,55 @@ def format_sweep(torch, lib, P, reps: int = 20) -> dict:
     return res
 
 
+def decode_bench(args, torch) -> dict:
+    """Benchmark configuration 5: random-init 8B-shaped Qwen3 decoder (Q4_K
+    weights, Q6_K tied head), 2048-token seeded prompt prefilled through the
+    batched prefill path, then greedy decode; device-timed."""
+    import tempfile
+
+    from gncx_b200 import gguf
+    from gncx_b200.streamer import GNCXStreamer
+    tmp = Path(os.environ.get("GNCX_BENCH_DIR", tempfile.gettempdir()))
+    path = tmp / f"gncx_bench_{args.model}_{args.seed}.gguf"
+    t0 = time.time()
+    if not path.exists():
+        gguf.write_random_model(path, args.model, seed=args.seed)
+    write_s = time.time() - t0
+    prompt = np.random.default_rng(args.seed).integers(0, 151936, args.prompt).tolist()
+    res = {"model": args.model, "prompt": args.prompt, "new_tokens": args.new_tokens, "weights": "Q4_K, Q6_K head",
+           "model_write_s": round(write_s, 1)}
+    with GNCXStreamer(path, max_seq_len=args.prompt + args.new_tokens) as eng:
+        modes = [m for m in args.decode_modes.split(",") if m]
+        for mode, exact in (("split_kv", False), ("exact_softmax", True)):
+            if mode not in modes:
+                continue
+            eng.set_exact_attention(exact)
+            eng.generate_ids(prompt[:64], 8, eos_id=-1)  # warm-up (graph capture)
+            ids = eng.generate_ids(prompt, args.new_tokens, eos_id=-1)
+            t = eng.timing()
+            res[mode] = {"decode_tok_s": t["decode_steps"] / (t["decode_ms"] / 1e3),
+                         "ms_per_token": t["decode_ms"] / max(1, t["decode_steps"]),
+                         "prefill_tok_s": args.prompt / (t["prefill_ms"] / 1e3), "prefill_ms": t["prefill_ms"],
+                         "tokens": len(ids), "first_ids": ids[:8]}
+    # reference CPU decode on the same file (bounded sample)
+    if not args.no_cpu_baseline:
+        from oracle.oracle import REF_NATIVE_SO, OracleModel
+        ref = OracleModel(path, 64, REF_NATIVE_SO)
+        ref.prefill(prompt[:8])
+        t1 = time.perf_counter()
+        n = 3
+        tok = prompt[8]
+        for i in range(n):
+            ref.forward_token(tok, 8 + i)
+        dt = time.perf_counter() - t1
+        ref.close()
+        res["cpu_reference"] = {"decode_tok_s": n / dt, "kind": ref.kind, "cores": min(os.cpu_count() or 1, 12),
+                                "sample": f"{n} decode steps after an 8-token prefill, pool of min(cores,12) threads"}
+        if "split_kv" in res:
+            res["speedup_vs_cpu_decode"] = res["split_kv"]["decode_tok_s"] / res["cpu_reference"]["decode_tok_s"]
+    return res
+
+
 def run_gpu(args) -> None:
     import torch
     rank, world, local = dist_env()
@@ -365,6 +414,10 @@ def run_gpu(args) -> None:
         if not args.no_sweep:
             lib.gncx_set_weight_prefetch(0)  # each sweep entry is timed alone
             line["sweep"] = format_sweep(torch, lib, P)
+        if not args.no_decode:
+            del weights
+            torch.cuda.empty_cache()
+            line["decode"] = decode_bench(args, torch)
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
         print(json.dumps(line), flush=True)
@@ -382,6 +435,12 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the per-format sweep table")
+    ap.add_argument("--no-decode", action="store_true", help="skip the 8B-shape decode/prefill measurement")
+    ap.add_argument("--model", default="qwen3-8b", choices=["qwen3-8b", "qwen3-0.6b"])
+    ap.add_argument("--prompt", type=int, default=2048)
+    ap.add_argument("--new-tokens", type=int, default=512)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--decode-modes", default="split_kv,exact_softmax")
     ap.add_argument("--no-prefetch", action="store_true",
                     help="disable weight prefetch across kernel boundaries (programmatic dependent launch)")
     args = ap.parse_args()
