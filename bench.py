@@ -441,11 +441,15 @@ def main() -> None:
     ap.add_argument("--new-tokens", type=int, default=512)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--decode-modes", default="split_kv,exact_softmax")
+    ap.add_argument("--shapes", default="", help="override the timed GEMV shapes, e.g. 4096x12288,24576x4096 (out x in)")
     ap.add_argument("--no-prefetch", action="store_true",
                     help="disable weight prefetch across kernel boundaries (programmatic dependent launch)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.shapes:
+        global SHAPES
+        SHAPES = [tuple(int(v) for v in sh.split("x")) for sh in args.shapes.split(",")]
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -60,8 +60,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
     const int G = a.n_heads / a.n_kv;
     const int kvh = blockIdx.y;
     const int cn = min(chunk, len - c0);
-    const int kvd = a.n_kv * hd;
-    const int rs = hd + kRowPad;
+    // head-major caches hold a chunk's positions contiguously: one bulk copy,
+    // dense rows; otherwise one copy per position into padded rows
+    const bool contig = a.kv_pos_stride == hd;
+    const int rs = contig ? hd : hd + kRowPad;
     uint64_t* bar = reinterpret_cast<uint64_t*>(smraw);   // [0] = K, [1] = V
     float* ks = reinterpret_cast<float*>(smraw + 64);     // [chunk][rs]
     float* vs = ks + (size_t)chunk * rs;                  // [chunk][rs]
@@ -70,7 +72,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
     float* red = sc + (size_t)G * chunk;                  // [G][2]
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
-    const size_t row0 = (size_t)(t0 + c0) * kvd + (size_t)kvh * hd;
+    const size_t row0 = (size_t)(t0 + c0) * a.kv_pos_stride + (size_t)kvh * a.kv_head_stride;
+    const size_t ps = (size_t)a.kv_pos_stride;
 
     if (BULK) {
         if (tid == 0) {
@@ -86,16 +89,23 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
                 if (!SCORES_ONLY) mbar_arrive_expect_tx(&bar[1], bytes * cn);
             }
             __syncwarp();
-            for (int p = lane; p < cn; p += 32) bulk_g2s(ks + (size_t)p * rs, a.kc + row0 + (size_t)p * kvd, bytes, &bar[0]);
-            if (!SCORES_ONLY)
-                for (int p = lane; p < cn; p += 32)
-                    bulk_g2s(vs + (size_t)p * rs, a.vc + row0 + (size_t)p * kvd, bytes, &bar[1]);
+            if (contig) {
+                if (lane == 0) {
+                    bulk_g2s(ks, a.kc + row0, bytes * cn, &bar[0]);
+                    if (!SCORES_ONLY) bulk_g2s(vs, a.vc + row0, bytes * cn, &bar[1]);
+                }
+            } else {
+                for (int p = lane; p < cn; p += 32) bulk_g2s(ks + (size_t)p * rs, a.kc + row0 + p * ps, bytes, &bar[0]);
+                if (!SCORES_ONLY)
+                    for (int p = lane; p < cn; p += 32)
+                        bulk_g2s(vs + (size_t)p * rs, a.vc + row0 + p * ps, bytes, &bar[1]);
+            }
         }
     } else {
         for (int i = tid; i < cn * hd; i += blockDim.x) {
             const int p = i / hd, d = i % hd;
-            ks[(size_t)p * rs + d] = a.kc[row0 + (size_t)p * kvd + d];
-            if (!SCORES_ONLY) vs[(size_t)p * rs + d] = a.vc[row0 + (size_t)p * kvd + d];
+            ks[(size_t)p * rs + d] = a.kc[row0 + p * ps + d];
+            if (!SCORES_ONLY) vs[(size_t)p * rs + d] = a.vc[row0 + p * ps + d];
         }
     }
     const float* qz = a.q + (size_t)z * a.q_stride + (size_t)kvh * G * hd;
@@ -192,7 +202,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
 // out = (sum_s o_s * e^(m_s-M)) / (sum_s l_s * e^(m_s-M) + 1e-12); optionally
 // re-quantized (blockDim == hd, one warp per 32 outputs).
 __global__ void attn_combine_kernel(const AttnArgs a) {
-    extern __shared__ float wsm[];  // [max_splits] weights
+    extern __shared__ float wsm[];  // [max_splits] weights, then [max_splits] sums
+    __shared__ float red[32];
     __shared__ float s_inv;
     const int h = blockIdx.x, z = blockIdx.y;
     const int hd = a.hd;
@@ -200,19 +211,31 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
     attn_window(a, z, t0, len);
     const int n = (len + a.chunk - 1) / a.chunk;
     const float* rec = a.part + ((size_t)z * a.n_heads + h) * a.max_splits * (hd + 2);
+    float* lsm = wsm + a.max_splits;
     float M = -INFINITY;
-    for (int s = 0; s < n; ++s) M = fmaxf(M, rec[(size_t)s * (hd + 2)]);
-    for (int s = threadIdx.x; s < n; s += blockDim.x) wsm[s] = exp_cr(fsub(rec[(size_t)s * (hd + 2)], M));
+    for (int s = threadIdx.x; s < n; s += blockDim.x) {
+        const float m = rec[(size_t)s * (hd + 2)];
+        wsm[s] = m;
+        lsm[s] = rec[(size_t)s * (hd + 2) + 1];
+        M = fmaxf(M, m);
+    }
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = M;
+    __syncthreads();
+    M = red[0];
+    for (int k = 1; k < (int)(blockDim.x >> 5); ++k) M = fmaxf(M, red[k]);
+    for (int s = threadIdx.x; s < n; s += blockDim.x) wsm[s] = exp_cr(fsub(wsm[s], M));
     __syncthreads();
     if (threadIdx.x == 0) {
         float L = 0.0f;
-        for (int s = 0; s < n; ++s) L = fadd(L, fmul(rec[(size_t)s * (hd + 2) + 1], wsm[s]));
+        for (int s = 0; s < n; ++s) L = fadd(L, fmul(lsm[s], wsm[s]));
         s_inv = fdiv(1.0f, fadd(L, 1e-12f));
     }
     __syncthreads();
     const float inv = s_inv;
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
         float o = 0.0f;
+#pragma unroll 8
         for (int s = 0; s < n; ++s) o = fadd(o, fmul(rec[(size_t)s * (hd + 2) + 2 + d], wsm[s]));
         o = fmul(o, inv);
         if (a.out) a.out[(size_t)z * a.out_stride + (size_t)h * hd + d] = o;
@@ -229,7 +252,7 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
 // out[d] += (e_t * inv) * v_t[d] serially over t.  One CTA per (query, head).
 __global__ void attn_exact_kernel(const AttnArgs a) {
     const int h = blockIdx.x, z = blockIdx.y;
-    const int hd = a.hd, G = a.n_heads / a.n_kv, kvh = h / G, kvd = a.n_kv * hd;
+    const int hd = a.hd, G = a.n_heads / a.n_kv, kvh = h / G;
     int t0, len;
     attn_window(a, z, t0, len);
     float* sc = a.scores + ((size_t)z * a.n_heads + h) * a.score_cap;
@@ -251,11 +274,12 @@ __global__ void attn_exact_kernel(const AttnArgs a) {
     }
     __syncthreads();
     const float inv = s_inv;
-    const float* vbase = a.vc + (size_t)t0 * kvd + (size_t)kvh * hd;
+    const float* vbase = a.vc + (size_t)t0 * a.kv_pos_stride + (size_t)kvh * a.kv_head_stride;
+    const size_t ps = (size_t)a.kv_pos_stride;
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
         float o = 0.0f;
-#pragma unroll 8
-        for (int t = 0; t < len; ++t) o = fadd(o, fmul(fmul(sc[t], inv), vbase[(size_t)t * kvd + d]));
+#pragma unroll 16
+        for (int t = 0; t < len; ++t) o = fadd(o, fmul(fmul(sc[t], inv), vbase[(size_t)t * ps + d]));
         if (a.out) a.out[(size_t)z * a.out_stride + (size_t)h * hd + d] = o;
         if (a.act_out) {
             ActBlock* dst = a.act_out + (size_t)z * (a.n_heads * hd / 32) + ((size_t)h * hd + d) / 32;
@@ -306,7 +330,7 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
     }
     if (bulk) launch_partial<true, false>(a, grid, smem, st);
     else launch_partial<false, false>(a, grid, smem, st);
-    const size_t csm = (size_t)a.max_splits * 4;
+    const size_t csm = (size_t)a.max_splits * 8;
     if (csm > 48 * 1024)
         cudaFuncSetAttribute(attn_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csm);
     const int cthreads = (a.act_out || (a.hd % 32 == 0 && a.hd <= 1024)) ? a.hd : 128;
@@ -331,6 +355,8 @@ int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t 
     a.q_stride = n_heads * head_dim;
     a.kc = kc;
     a.vc = vc;
+    a.kv_pos_stride = n_kv * head_dim;  // the reference's [pos][n_kv][head_dim]
+    a.kv_head_stride = head_dim;
     a.pos0 = pos;
     a.pos_dev = nullptr;
     a.n_heads = n_heads;

@@ -11,7 +11,9 @@
 //   * per-token state (input token, position, penalty window, output ids) is in
 //     device memory, so a whole decode step -- embedding, 36 layers, LM head,
 //     argmax -- is one captured CUDA graph launch with no host round trip;
-//   * the KV cache is the reference's layout, fp32 [max_seq][n_kv][head_dim].
+//   * the KV cache is fp32 like the reference's, laid out head-major
+//     [n_kv][max_seq][head_dim] so a run of positions of one head is contiguous
+//     (one bulk copy per attention chunk).
 #include <cuda_runtime.h>
 #include <fcntl.h>
 #include <math.h>
@@ -245,12 +247,14 @@ static int decode_step(Engine* e, bool sample, double penalty) {
             CK(gemv(e, w.wv, w.tv, e->act_d, e->normed, D, KVD, e->qkv + QD + KVD));
         }
         CK(qkv_post_launch(e->qkv, qkv_w, 1, e->nh, e->nkv, e->hd, w.q_norm, w.k_norm, e->qk_norm, e->eps, e->rope_c,
-                           e->rope_s, 0, &e->st->pos, w.kc, w.vc, s));
+                           e->rope_s, 0, &e->st->pos, w.kc, w.vc, e->hd, (int64_t)e->max_seq * e->hd, s));
         AttnArgs a{};
         a.q = e->qkv;
         a.q_stride = qkv_w;
         a.kc = w.kc;
         a.vc = w.vc;
+        a.kv_pos_stride = e->hd;  // head-major cache: [n_kv][max_seq][head_dim]
+        a.kv_head_stride = e->max_seq * e->hd;
         a.pos0 = 0;
         a.pos_dev = &e->st->pos;
         a.n_heads = e->nh;
@@ -332,7 +336,7 @@ static int prefill_batch(Engine* e, int B) {
             CK(matbatch_launch(w.wv, w.tv, nullptr, e->pf_act, B, D, KVD, e->pf_qkv + QD + KVD, e->d_err, s, qkv_w));
         }
         CK(qkv_post_launch(e->pf_qkv, qkv_w, B, e->nh, e->nkv, e->hd, w.q_norm, w.k_norm, e->qk_norm, e->eps, e->rope_c,
-                           e->rope_s, 0, nullptr, w.kc, w.vc, s));
+                           e->rope_s, 0, nullptr, w.kc, w.vc, e->hd, (int64_t)e->max_seq * e->hd, s));
         for (int z0 = 0; z0 < B; z0 += kPrefillGroup) {
             const int nz = B - z0 < kPrefillGroup ? B - z0 : kPrefillGroup;
             AttnArgs a{};
@@ -340,6 +344,8 @@ static int prefill_batch(Engine* e, int B) {
             a.q_stride = qkv_w;
             a.kc = w.kc;
             a.vc = w.vc;
+            a.kv_pos_stride = e->hd;
+            a.kv_head_stride = e->max_seq * e->hd;
             a.pos0 = z0;
             a.pos_dev = nullptr;
             a.n_heads = e->nh;

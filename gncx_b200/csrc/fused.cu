@@ -65,7 +65,8 @@ int add_norm_quant_launch(float* hidden, const float* residual, const float* w, 
 // normed, rotated and written to the cache at the row's position, v heads copied.
 __global__ void qkv_post_kernel(float* qkv, int row_stride, int nh, int nkv, int hd, const float* __restrict__ qn,
                                 const float* __restrict__ kn, int do_norm, float eps, const float* __restrict__ ct,
-                                const float* __restrict__ stab, int pos0, const int* pos_dev, float* kc, float* vc) {
+                                const float* __restrict__ stab, int pos0, const int* pos_dev, float* kc, float* vc,
+                                int64_t kps, int64_t khs) {
     extern __shared__ float xs[];
     const int x = blockIdx.x, r = blockIdx.y;
     const int pos = (pos_dev ? *pos_dev : pos0) + r;
@@ -74,7 +75,7 @@ __global__ void qkv_post_kernel(float* qkv, int row_stride, int nh, int nkv, int
     if (x >= nh + nkv) {
         const int jv = x - nh - nkv;
         const float* src = row + qd + kvd + (size_t)jv * hd;
-        float* dst = vc + (size_t)pos * kvd + (size_t)jv * hd;
+        float* dst = vc + (size_t)pos * kps + (size_t)jv * khs;
         for (int i = threadIdx.x; i < hd; i += blockDim.x) dst[i] = src[i];
         return;
     }
@@ -92,7 +93,7 @@ __global__ void qkv_post_kernel(float* qkv, int row_stride, int nh, int nkv, int
         __syncthreads();
     }
     const int half = hd >> 1;
-    float* dst = isq ? vec : kc + (size_t)pos * kvd + (size_t)(x - nh) * hd;
+    float* dst = isq ? vec : kc + (size_t)pos * kps + (size_t)(x - nh) * khs;
     for (int i = threadIdx.x; i < half; i += blockDim.x) {
         const float c = ct[(size_t)pos * half + i], s = stab[(size_t)pos * half + i];
         const float x1 = xs[i], x2 = xs[i + half];
@@ -104,11 +105,12 @@ __global__ void qkv_post_kernel(float* qkv, int row_stride, int nh, int nkv, int
 int qkv_post_launch(float* qkv, int32_t row_stride, int32_t rows, int32_t nh, int32_t nkv, int32_t hd,
                     const float* q_norm, const float* k_norm, bool do_norm, float eps, const float* cos_tab,
                     const float* sin_tab, int32_t pos0, const int32_t* pos_dev, float* kc, float* vc,
-                    cudaStream_t st) {
+                    int64_t kv_pos_stride, int64_t kv_head_stride, cudaStream_t st) {
     if (!qkv || !cos_tab || !sin_tab || !kc || !vc || rows <= 0 || hd <= 0 || (hd & 1)) return kErrInvalidArg;
     const int threads = hd >= 256 ? 256 : (hd >= 128 ? 128 : 64);
     qkv_post_kernel<<<dim3(nh + 2 * nkv, rows), threads, (size_t)hd * 4, st>>>(
-        qkv, row_stride, nh, nkv, hd, q_norm, k_norm, do_norm ? 1 : 0, eps, cos_tab, sin_tab, pos0, pos_dev, kc, vc);
+        qkv, row_stride, nh, nkv, hd, q_norm, k_norm, do_norm ? 1 : 0, eps, cos_tab, sin_tab, pos0, pos_dev, kc, vc,
+        kv_pos_stride, kv_head_stride);
     return status();
 }
 

@@ -63,6 +63,8 @@ struct AttnArgs {
     int q_stride;
     const float* kc;
     const float* vc;
+    int kv_pos_stride;     // floats between positions (reference layout: n_kv*hd; head-major: hd)
+    int kv_head_stride;    // floats between kv heads (reference layout: hd; head-major: max_seq*hd)
     int pos0;
     const int* pos_dev;
     int n_heads, n_kv, hd;
@@ -119,7 +121,7 @@ int add_norm_quant_launch(float* hidden, const float* residual, const float* w, 
 int qkv_post_launch(float* qkv, int32_t row_stride, int32_t rows, int32_t nh, int32_t nkv, int32_t hd,
                     const float* q_norm, const float* k_norm, bool do_norm, float eps, const float* cos_tab,
                     const float* sin_tab, int32_t pos0, const int32_t* pos_dev, float* kc, float* vc,
-                    cudaStream_t st);
+                    int64_t kv_pos_stride, int64_t kv_head_stride, cudaStream_t st);
 int glu_quant_launch(const float* g, const float* u, int32_t stride, int32_t ffn, int32_t rows, bool gelu,
                      ActBlock* act, cudaStream_t st);
 size_t argmax_state_scratch_bytes();

@@ -11,20 +11,52 @@ namespace gncx {
 // serial chains are reproduced literally by four threads reading the row from
 // shared memory; everything else is parallel.
 
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
+}
+
+// Serial sum over k of xs[4k+j]^2 (one of the reference's four SSE lanes).
+// The next batch's loads are issued (volatile, so in program order) before
+// the current batch's adds, so only the fadd chain is serial.
+__device__ __forceinline__ float lane_sumsq(const float* xs, int j, int cnt) {
+    constexpr int B = 16;
+    const uint32_t base = (uint32_t)__cvta_generic_to_shared(xs) + 4u * (uint32_t)j;
+    float acc = 0.0f;
+    const int kmain = cnt & ~(B - 1);
+    if (kmain > 0) {
+        float cur[B], nxt[B];
+#pragma unroll
+        for (int i = 0; i < B; ++i) cur[i] = lds_f32(base + 16u * i);
+        for (int k = 0; k < kmain; k += B) {
+            const bool more = k + B < kmain;
+            if (more) {
+#pragma unroll
+                for (int i = 0; i < B; ++i) nxt[i] = lds_f32(base + 16u * (k + B + i));
+            }
+#pragma unroll
+            for (int i = 0; i < B; ++i) acc = fadd(acc, fmul(cur[i], cur[i]));
+            if (more) {
+#pragma unroll
+                for (int i = 0; i < B; ++i) cur[i] = nxt[i];
+            }
+        }
+    }
+    for (int k = kmain; k < cnt; ++k) {
+        const float v = lds_f32(base + 16u * k);
+        acc = fadd(acc, fmul(v, v));
+    }
+    return acc;
+}
+
 __device__ __forceinline__ float rms_inv(const float* xs, int n, float eps) {
     // called by all threads; returns inv in every thread
     __shared__ float s_inv;
     const int tid = threadIdx.x;
     if (tid < 32) {
-        float acc = 0.0f;
         const int n4 = n & ~3;
-        if (tid < 4) {
-#pragma unroll 8
-            for (int i = tid; i < n4; i += 4) {
-                const float v = xs[i];
-                acc = fadd(acc, fmul(v, v));
-            }
-        }
+        const float acc = tid < 4 ? lane_sumsq(xs, tid, n4 >> 2) : 0.0f;
         const float a1 = __shfl_sync(0xffffffffu, acc, 1);
         const float a2 = __shfl_sync(0xffffffffu, acc, 2);
         const float a3 = __shfl_sync(0xffffffffu, acc, 3);
