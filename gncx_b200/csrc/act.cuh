@@ -154,25 +154,64 @@ __device__ __forceinline__ void stage_act_blocks(const ActBlock* __restrict__ ab
     }
 }
 
-// One warp quantizes one 32-input block held one value per lane and stores
-// it as an ActBlock (same arithmetic as quantize_block32).
-__device__ __forceinline__ void warp_quantize_store(float v, ActBlock* dst, int lane) {
+// Bytes of a staged activation vector: the GEMV's shared-memory act layout
+// (swizzled quants, then swizzled {d, sum_lo, sum_hi, sum_q} records), which
+// producers write to global memory so the GEMV loads it with one bulk copy.
+__host__ __device__ inline size_t staged_act_bytes(int in_dim) { return (size_t)in_dim + (size_t)(in_dim / 32) * 16; }
+
+// Warp-level quantization of one 32-input block (one value per lane): the
+// block's quants, scale and sums.
+__device__ __forceinline__ void warp_quantize(float v, int lane, int& q, float& d, int& s) {
     float amax = fabsf(v);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    int q = 0;
-    float d = 0.0f;
+    q = 0;
+    d = 0.0f;
     if (amax != 0.0f) {
         const float inv = fdiv(127.0f, amax);
         d = fdiv(amax, 127.0f);
         q = __float2int_rn(fmul(v, inv));
     }
-    int s = q;
+    s = q;
 #pragma unroll
     for (int o = 1; o < 16; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);  // sums of lanes 0..15 / 16..31
+}
+
+// ... stored into a staged activation vector (block b of in_dim inputs).
+__device__ __forceinline__ void warp_quantize_store_staged(float v, uint8_t* staged, int in_dim, int b, int lane) {
+    int q, s;
+    float d;
+    warp_quantize(v, lane, q, d, s);
+    const int u = b >> 3, j = b & 7;
+    staged[act_chunk_pos(u, 2 * j + (lane >> 4)) + (lane & 15)] = (uint8_t)(int8_t)q;
+    const int hi = __shfl_sync(0xffffffffu, s, 16);
+    if (lane == 0) {
+        float4* rec = reinterpret_cast<float4*>(staged + in_dim);
+        rec[act_rec_pos(b)] = make_float4(d, __int_as_float(s), __int_as_float(hi), __int_as_float(s + hi));
+    }
+}
+
+// One warp quantizes one 32-input block held one value per lane and stores
+// it as an ActBlock (same arithmetic as quantize_block32).
+__device__ __forceinline__ void warp_quantize_store(float v, ActBlock* dst, int lane) {
+    int q, s;
+    float d;
+    warp_quantize(v, lane, q, d, s);
     dst->qs[lane] = (int8_t)q;
     if (lane == 0) { dst->d = d; dst->sum_lo = s; dst->pad = 0; }
     if (lane == 16) dst->sum_hi = s;
+}
+
+// Staged or block output of a producer kernel: `staged` (one vector, the
+// GEMV's shared-memory layout) when non-null, else ActBlocks.
+struct ActOut {
+    ActBlock* blocks;   // [rows][dim/32]
+    uint8_t* staged;    // [staged_act_bytes(dim)], single row
+};
+
+__device__ __forceinline__ void act_out_store(const ActOut& o, float v, int dim, size_t row, int b, int lane) {
+    if (o.staged) warp_quantize_store_staged(v, o.staged, dim, b, lane);
+    else warp_quantize_store(v, o.blocks + row * (size_t)(dim >> 5) + b, lane);
 }
 
 }  // namespace gncx

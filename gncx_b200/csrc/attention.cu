@@ -5,38 +5,66 @@
 // token, lua/gncx_streamer.lua:1079-1109).
 //
 // Split-KV ("flash-decoding"): a query's window [t0, pos] is cut into chunks;
-// one CTA per (chunk, KV head, query) pulls that chunk's K and V head rows into
-// shared memory with cp.async.bulk (one 16-byte-aligned copy per position, rows
-// padded by 8 floats so the 8-lane dot pattern is bank-conflict free), serves
-// every query head of the group from it, and writes a partial record (chunk
-// max, sum of exp, unnormalised output).  A combine kernel merges the records
-// of each head and can re-quantize the result for the next GEMV.  In decode,
-// each K/V byte crosses HBM once.  The position may live in device memory so a
-// captured CUDA graph replays every token; CTAs past the window exit at once.
+// one CTA per (chunk, KV head, query) stages that chunk's K and V head rows in
+// shared memory (16-byte cp.async copies into rows padded by 4 floats, so that
+// eight threads reading eight different rows hit eight different bank groups),
+// serves every query head of the group from it, and writes a partial record
+// (chunk max, sum of exp, unnormalised output).  The records of a (query, KV
+// head) are merged either by the last of its CTAs to finish (a per-(query, KV
+// head) arrival counter; the merge also re-quantizes the output for the next
+// GEMV) or by a separate combine kernel.  In decode each K/V byte crosses HBM
+// once.  The position may live in device memory so a captured CUDA graph
+// replays every token; CTAs past the window exit at once.
 //
 // Scores are bit-identical to the reference's: its q.k is two 4-lane SSE
-// accumulators over steps of 8, folded (l0+l1)+(l2+l3); lane j of an 8-lane
-// group owns the chain over d = 8m + j and the fold is done with shuffles.
-// The softmax sums are formed in a different order, so outputs agree with
-// the reference to ~1e-6 relative.
+// accumulators over steps of 8, folded (l0+l1)+(l2+l3), i.e. eight serial
+// chains over d = 8m + j (j = 0..7), folded ((c0+c4)+(c1+c5))+((c2+c6)+(c3+c7));
+// one thread runs the eight chains of one (position, head).  The split-KV
+// softmax sums are formed in a different order from the reference's serial
+// ones, so those outputs agree to ~1e-6 relative.  Exact mode keeps the
+// reference's order: scores only here, then attn_exact_softmax_kernel (serial
+// sum of exp over the window) and attn_exact_pv_kernel (serial sum over t of
+// (e_t * inv) * v_t[d] for every output element).
 //
-// KV cache layout is the reference's: [max_seq][n_kv][head_dim] fp32 per layer.
+// KV cache layout: rows of head_dim floats at kc + t * kv_pos_stride +
+// kvh * kv_head_stride (the reference's [pos][n_kv][head_dim], or the engine's
+// head-major [n_kv][max_seq][head_dim]).
 #include <cuda_runtime.h>
 #include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
-#include "tma.cuh"
 
 namespace gncx {
 
-constexpr int kAttnThreads = 128;
+constexpr int kAttnThreads = 256;
 constexpr int kMaxHeadDim = 256;
-constexpr int kRowPad = 8;  // floats of padding per staged K/V row
+constexpr int kRowPad = 4;    // floats of padding per staged K/V row
+constexpr int kScorePad = 8;  // floats of padding per score row
+__host__ __device__ inline int attn_q_stride(int hd) { return hd + 4; }  // padded q rows
 
-static size_t attn_smem_bytes(int G, int hd, int chunk) {
-    const int rs = hd + kRowPad;
-    return 64 /*barriers*/ + (size_t)2 * chunk * rs * 4 + (size_t)G * hd * 4 + (size_t)G * chunk * 4 +
-           (size_t)2 * G * 4;
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Floats of the K/V staging area, which the merge reuses for its weights.
+// (also the scratch of the position-group reduction: kAttnThreads * 8 floats)
+__host__ __device__ inline size_t attn_kv_floats(int G, int hd, int chunk, int max_splits) {
+    size_t n = (size_t)2 * chunk * (hd + kRowPad);
+    const size_t merge = (size_t)2 * G * max_splits;
+    if (merge > n) n = merge;
+    if ((size_t)kAttnThreads * 8 > n) n = (size_t)kAttnThreads * 8;
+    return (n + 3) & ~(size_t)3;  // keeps the q rows that follow 16-byte aligned
+}
+
+static size_t attn_smem_bytes(int G, int hd, int chunk, int max_splits) {
+    const int G4 = (G + 3) & ~3;
+    return attn_kv_floats(G, hd, chunk, max_splits) * 4 + (size_t)G * attn_q_stride(hd) * 4 +
+           (size_t)G * (chunk + kScorePad) * 4 + (size_t)chunk * G4 * 4 + (size_t)2 * G * 4;
 }
 
 __device__ __forceinline__ void attn_window(const AttnArgs& a, int z, int& t0, int& len) {
@@ -45,10 +73,143 @@ __device__ __forceinline__ void attn_window(const AttnArgs& a, int z, int& t0, i
     len = pos + 1 - t0;
 }
 
-// Partial record layout per (query, head, split): [0] = max, [1] = sum of exp, [2..] = o[hd]
-template <bool BULK, bool SCORES_ONLY>
+constexpr int kMergeBatch = 32;  // split records loaded per round trip in a merge
+
+// Merge the n split records of heads h0 .. h0+G-1 of query z:
+// out = (sum_s o_s * e^(m_s-M)) / (sum_s l_s * e^(m_s-M) + 1e-12), serial in s.
+// `wsm` / `lsm` hold G*n floats each, `s_inv` G floats; called by whole CTAs.
+__device__ void attn_merge(const AttnArgs& a, int z, int h0, int G, int n, float* wsm, float* lsm, float* s_inv) {
+    const int hd = a.hd;
+    const size_t R = attn_record_floats(hd);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
+    for (int i = tid; i < G * n; i += nthr) {
+        const int g = i / n, s = i - g * n;
+        const float* rec = a.part + (((size_t)z * a.n_heads + h0 + g) * a.max_splits + s) * R;
+        wsm[i] = __ldcg(rec);
+        lsm[i] = __ldcg(rec + 1);
+    }
+    __syncthreads();
+    for (int g = warp; g < G; g += nthr >> 5) {
+        float M = -INFINITY;
+        for (int s = lane; s < n; s += 32) M = fmaxf(M, wsm[g * n + s]);
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        for (int s = lane; s < n; s += 32) wsm[g * n + s] = exp_cr(fsub(wsm[g * n + s], M));
+    }
+    __syncthreads();
+    if (tid < G) {
+        float L = 0.0f;
+        for (int s = 0; s < n; ++s) L = fadd(L, fmul(lsm[tid * n + s], wsm[tid * n + s]));
+        s_inv[tid] = fdiv(1.0f, fadd(L, 1e-12f));
+    }
+    __syncthreads();
+    for (int i = tid; i < G * hd; i += nthr) {
+        const int g = i / hd, d = i - g * hd;
+        const int h = h0 + g;
+        const float* rec = a.part + ((size_t)z * a.n_heads + h) * a.max_splits * R + 4 + d;
+        const float* w = wsm + g * n;
+        float o = 0.0f;
+        for (int s0 = 0; s0 < n; s0 += kMergeBatch) {
+            float v[kMergeBatch];  // a batch of records in flight at once
+#pragma unroll
+            for (int b = 0; b < kMergeBatch; ++b) v[b] = s0 + b < n ? __ldcg(rec + (size_t)(s0 + b) * R) : 0.0f;
+#pragma unroll
+            for (int b = 0; b < kMergeBatch; ++b)
+                if (s0 + b < n) o = fadd(o, fmul(v[b], w[s0 + b]));
+        }
+        o = fmul(o, s_inv[g]);
+        if (a.out) a.out[(size_t)z * a.out_stride + (size_t)h * hd + d] = o;
+        if (a.act_out.blocks || a.act_out.staged)
+            act_out_store(a.act_out, o, a.n_heads * hd, (size_t)z, (h * hd + d) >> 5, d & 31);
+    }
+}
+
+// ---- per-chunk building blocks shared by the split-KV kernels ----
+// Scores of positions [0, cn) of a staged chunk; task t = (position t / G, head
+// t % G), so the G lanes of one position read the same K row (one shared-memory
+// wavefront serves eight positions).  store(g, p, q.k) receives the unscaled dot.
+template <class Store>
+__device__ __forceinline__ void chunk_scores(const float* ks, int rs, const float* qs, int qrs, int G, int hd, int cn,
+                                             Store store) {
+    const int nm = hd >> 3;
+    for (int task = threadIdx.x; task < G * cn; task += blockDim.x) {
+        const int p = task / G, g = task - p * G;
+        const float* kr = ks + (size_t)p * rs;
+        const float* qg = qs + (size_t)g * qrs;
+        float c[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) c[j] = 0.0f;
+#pragma unroll 4
+        for (int m = 0; m < nm; ++m) {
+            const float4 k0 = *reinterpret_cast<const float4*>(kr + 8 * m);
+            const float4 k1 = *reinterpret_cast<const float4*>(kr + 8 * m + 4);
+            const float4 q0 = *reinterpret_cast<const float4*>(qg + 8 * m);
+            const float4 q1 = *reinterpret_cast<const float4*>(qg + 8 * m + 4);
+            c[0] = fadd(c[0], fmul(q0.x, k0.x));
+            c[1] = fadd(c[1], fmul(q0.y, k0.y));
+            c[2] = fadd(c[2], fmul(q0.z, k0.z));
+            c[3] = fadd(c[3], fmul(q0.w, k0.w));
+            c[4] = fadd(c[4], fmul(q1.x, k1.x));
+            c[5] = fadd(c[5], fmul(q1.y, k1.y));
+            c[6] = fadd(c[6], fmul(q1.z, k1.z));
+            c[7] = fadd(c[7], fmul(q1.w, k1.w));
+        }
+        float dot = fadd(fadd(fadd(c[0], c[4]), fadd(c[1], c[5])), fadd(fadd(c[2], c[6]), fadd(c[3], c[7])));
+        for (int d = nm * 8; d < hd; ++d) dot = fadd(dot, fmul(qg[d], kr[d]));
+        store(g, p, dot);
+    }
+}
+
+constexpr int kPvHeads = 8;  // query heads accumulated per pass over V
+
+// acc[i] += sum over this thread's positions p = pg, pg + npg, ... of
+// e[p][g0 + i] * v[p][d]; e is position-major with row stride G4 (a multiple
+// of 4), so one broadcast vector load serves four heads.
+__device__ __forceinline__ void chunk_pv(const float* vs, int rs, const float* es, int G4, int g0, int ng, int cn,
+                                         int d, int pg, int npg, float (&acc)[kPvHeads]) {
+    for (int p = pg; p < cn; p += npg) {
+        const float v = vs[(size_t)p * rs + d];
+        const float4 e0 = *reinterpret_cast<const float4*>(es + (size_t)p * G4 + g0);
+        acc[0] = fmaf(e0.x, v, acc[0]);
+        acc[1] = fmaf(e0.y, v, acc[1]);
+        acc[2] = fmaf(e0.z, v, acc[2]);
+        acc[3] = fmaf(e0.w, v, acc[3]);
+        if (ng > 4) {
+            const float4 e1 = *reinterpret_cast<const float4*>(es + (size_t)p * G4 + g0 + 4);
+            acc[4] = fmaf(e1.x, v, acc[4]);
+            acc[5] = fmaf(e1.y, v, acc[5]);
+            acc[6] = fmaf(e1.z, v, acc[6]);
+            acc[7] = fmaf(e1.w, v, acc[7]);
+        }
+    }
+}
+
+// Sum acc over the npg position groups through `scr` (npg * kPvHeads * hd
+// floats) and hand out(i, d, value) each (head g0 + i, column d) once.
+template <class Out>
+__device__ __forceinline__ void pv_reduce(const float (&acc)[kPvHeads], int ng, int hd, int d, int pg, int npg,
+                                          bool active, float* scr, Out out) {
+    if (npg == 1) {
+        if (active)
+            for (int i = 0; i < ng; ++i) out(i, d, acc[i]);
+        return;
+    }
+    if (active)
+        for (int i = 0; i < ng; ++i) scr[((size_t)pg * kPvHeads + i) * hd + d] = acc[i];
+    __syncthreads();
+    for (int t = threadIdx.x; t < ng * hd; t += blockDim.x) {
+        const int i = t / hd, dd = t - i * hd;
+        float v = scr[(size_t)i * hd + dd];
+        for (int q = 1; q < npg; ++q) v += scr[((size_t)q * kPvHeads + i) * hd + dd];
+        out(i, dd, v);
+    }
+    __syncthreads();
+}
+
+// Partial record per (query, head, split): [0] = max, [1] = sum of exp, [4..] = o[hd]
+template <bool VEC, bool SCORES_ONLY>
 __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnArgs a) {
-    extern __shared__ __align__(128) uint8_t smraw[];
+    extern __shared__ __align__(16) uint8_t smraw[];
+    __shared__ int s_last;
     const int z = blockIdx.z;
     int t0, len;
     attn_window(a, z, t0, len);
@@ -58,234 +219,257 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
     if (c0 >= len) return;  // uniform per CTA, before any barrier
     const int hd = a.hd;
     const int G = a.n_heads / a.n_kv;
+    const int G4 = (G + 3) & ~3;
     const int kvh = blockIdx.y;
     const int cn = min(chunk, len - c0);
-    // head-major caches hold a chunk's positions contiguously: one bulk copy,
-    // dense rows; otherwise one copy per position into padded rows
-    const bool contig = a.kv_pos_stride == hd;
-    const int rs = contig ? hd : hd + kRowPad;
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smraw);   // [0] = K, [1] = V
-    float* ks = reinterpret_cast<float*>(smraw + 64);     // [chunk][rs]
-    float* vs = ks + (size_t)chunk * rs;                  // [chunk][rs]
-    float* qs = vs + (size_t)chunk * rs;                  // [G][hd]
-    float* sc = qs + (size_t)G * hd;                      // [G][chunk]
-    float* red = sc + (size_t)G * chunk;                  // [G][2]
+    const int rs = hd + kRowPad;
+    const int n_split = (len + chunk - 1) / chunk;
+    float* ks = reinterpret_cast<float*>(smraw);                                  // [chunk][rs]
+    float* vs = ks + (size_t)chunk * rs;                                           // [chunk][rs]
+    const int qrs = attn_q_stride(hd), sld = chunk + kScorePad;
+    float* qs = ks + attn_kv_floats(G, hd, chunk, a.max_splits);                   // [G][qrs]
+    float* sc = qs + (size_t)G * qrs;                                              // [G][sld]
+    float* es = sc + (size_t)G * sld;                                              // [chunk][G4]
+    float* red = es + (size_t)chunk * G4;                                          // [G][2]
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const size_t row0 = (size_t)(t0 + c0) * a.kv_pos_stride + (size_t)kvh * a.kv_head_stride;
     const size_t ps = (size_t)a.kv_pos_stride;
 
-    if (BULK) {
-        if (tid == 0) {
-            mbar_init(&bar[0], 1);
-            mbar_init(&bar[1], 1);
-            fence_barrier_init();
-        }
-        __syncthreads();
-        if (warp == 0) {
-            const uint32_t bytes = (uint32_t)hd * 4;
-            if (lane == 0) {
-                mbar_arrive_expect_tx(&bar[0], bytes * cn);
-                if (!SCORES_ONLY) mbar_arrive_expect_tx(&bar[1], bytes * cn);
-            }
-            __syncwarp();
-            if (contig) {
-                if (lane == 0) {
-                    bulk_g2s(ks, a.kc + row0, bytes * cn, &bar[0]);
-                    if (!SCORES_ONLY) bulk_g2s(vs, a.vc + row0, bytes * cn, &bar[1]);
-                }
-            } else {
-                for (int p = lane; p < cn; p += 32) bulk_g2s(ks + (size_t)p * rs, a.kc + row0 + p * ps, bytes, &bar[0]);
-                if (!SCORES_ONLY)
-                    for (int p = lane; p < cn; p += 32)
-                        bulk_g2s(vs + (size_t)p * rs, a.vc + row0 + p * ps, bytes, &bar[1]);
-            }
+    // ---- stage K (copy group 0) and V (group 1) ----
+    if (VEC) {
+        // thread -> one 16-byte piece c of rows p0, p0 + step, ...
+        const int cpr = hd >> 2, step = kAttnThreads / cpr;
+        const int c = tid % cpr, p0 = tid / cpr;
+        const bool on = tid < step * cpr;
+        if (on)
+            for (int p = p0; p < cn; p += step) cp_async16(ks + (size_t)p * rs + 4 * c, a.kc + row0 + p * ps + 4 * c);
+        cp_async_commit();
+        if (!SCORES_ONLY) {
+            if (on)
+                for (int p = p0; p < cn; p += step)
+                    cp_async16(vs + (size_t)p * rs + 4 * c, a.vc + row0 + p * ps + 4 * c);
+            cp_async_commit();
         }
     } else {
-        for (int i = tid; i < cn * hd; i += blockDim.x) {
-            const int p = i / hd, d = i % hd;
+        for (int i = tid; i < cn * hd; i += kAttnThreads) {
+            const int p = i / hd, d = i - p * hd;
             ks[(size_t)p * rs + d] = a.kc[row0 + p * ps + d];
             if (!SCORES_ONLY) vs[(size_t)p * rs + d] = a.vc[row0 + p * ps + d];
         }
     }
     const float* qz = a.q + (size_t)z * a.q_stride + (size_t)kvh * G * hd;
-    for (int i = tid; i < G * hd; i += blockDim.x) qs[i] = qz[i];
-    __syncthreads();
-    bool timed_out = false;
-    if (BULK && !mbar_wait(&bar[0], 0)) timed_out = true;
-
-    // ---- scores: 8 lanes per position, lane j owns the chain over d = 8m + j ----
-    const int j = lane & 7, slot = lane >> 3;  // 4 positions per warp per step
-    const int nm = hd >> 3;
-    if (!timed_out) {
-        for (int p0 = warp * 4; p0 < cn; p0 += (kAttnThreads / 32) * 4) {
-            const int p = p0 + slot;
-            const bool ok = p < cn;
-            const float* kt = ks + (size_t)(ok ? p : 0) * rs;
-            float kr[kMaxHeadDim / 8];
-#pragma unroll
-            for (int m = 0; m < kMaxHeadDim / 8; ++m)
-                if (m < nm) kr[m] = kt[8 * m + j];
-            for (int g = 0; g < G; ++g) {
-                const float* qg = qs + g * hd;
-                float c = 0.0f;
-#pragma unroll
-                for (int m = 0; m < kMaxHeadDim / 8; ++m)
-                    if (m < nm) c = fadd(c, fmul(qg[8 * m + j], kr[m]));
-                const float x = fadd(c, __shfl_down_sync(0xffffffffu, c, 4));
-                const float y = fadd(x, __shfl_down_sync(0xffffffffu, x, 1));
-                float dot = fadd(y, __shfl_down_sync(0xffffffffu, y, 2));
-                if (j == 0 && ok) {
-                    for (int d = nm * 8; d < hd; ++d) dot = fadd(dot, fmul(qg[d], kt[d]));
-                    const float sv = fmul(dot, a.scale);
-                    if (SCORES_ONLY)
-                        a.scores[((size_t)z * a.n_heads + kvh * G + g) * a.score_cap + c0 + p] = sv;
-                    else
-                        sc[g * chunk + p] = sv;
-                }
-            }
-        }
-    }
-    if (SCORES_ONLY) {  // the K copies have all landed (waited above)
-        if (timed_out && tid == 0) record_error(a.err, kErrTimeout);
-        return;
+    for (int i = tid; i < G * hd; i += kAttnThreads) qs[(size_t)(i / hd) * qrs + i % hd] = qz[i];
+    if (VEC) {
+        if (SCORES_ONLY) cp_async_wait<0>();
+        else cp_async_wait<1>();
     }
     __syncthreads();
 
-    // ---- per head: chunk max, exp, sum ----
+    // ---- scores (the reference's eight chains per dot) ----
+    if (SCORES_ONLY) {
+        float* row = a.scores + ((size_t)z * a.n_heads + kvh * G) * a.score_cap + c0;
+        const int cap = a.score_cap;
+        const float scale = a.scale;
+        chunk_scores(ks, rs, qs, qrs, G, hd, cn,
+                     [&](int g, int p, float dot) { row[(size_t)g * cap + p] = fmul(dot, scale); });
+        return;  // the K copies have all landed (waited above)
+    }
+    {
+        const float scale = a.scale;
+        chunk_scores(ks, rs, qs, qrs, G, hd, cn, [&](int g, int p, float dot) { sc[g * sld + p] = fmul(dot, scale); });
+    }
+    __syncthreads();
+
+    // ---- per head: chunk max, exp (position-major copy for the PV), sum ----
     for (int g = warp; g < G; g += kAttnThreads / 32) {
         float mx = -INFINITY;
-        for (int p = lane; p < cn; p += 32) mx = fmaxf(mx, sc[g * chunk + p]);
+        for (int p = lane; p < cn; p += 32) mx = fmaxf(mx, sc[g * sld + p]);
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         float sum = 0.0f;
         for (int p = lane; p < cn; p += 32) {
-            const float e = exp_cr(fsub(sc[g * chunk + p], mx));
-            sc[g * chunk + p] = e;
+            const float e = exp_cr(fsub(sc[g * sld + p], mx));
+            es[(size_t)p * G4 + g] = e;
             sum += e;
         }
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
         if (lane == 0) { red[2 * g] = mx; red[2 * g + 1] = sum; }
     }
-    // always wait (bounded) for the V copies, so none is in flight when the CTA exits
-    if (BULK && !mbar_wait(&bar[1], 0)) timed_out = true;
+    for (int i = tid; i < cn * (G4 - G); i += kAttnThreads) es[(size_t)(i / (G4 - G)) * G4 + G + i % (G4 - G)] = 0.0f;
+    if (VEC) cp_async_wait<0>();
     __syncthreads();
-    if (timed_out) {
-        if (tid == 0) record_error(a.err, kErrTimeout);
-        return;
-    }
 
-    // ---- o[g][d] = sum_p e[g][p] * v[p][d] ----
-    for (int d = tid; d < hd; d += blockDim.x) {
-        for (int g0 = 0; g0 < G; g0 += 4) {
-            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 4
-            for (int p = 0; p < cn; ++p) {
-                const float v = vs[(size_t)p * rs + d];
+    // ---- o[g][d] = sum_p e[p][g] * v[p][d] ----
+    const int npg = kAttnThreads / hd > 0 ? kAttnThreads / hd : 1;
+    const int d = tid % hd, pg = tid / hd;
+    const bool active = pg < npg && d < hd && tid < npg * hd;
+    for (int g0 = 0; g0 < G; g0 += kPvHeads) {
+        const int ng = min(kPvHeads, G - g0);
+        float acc[kPvHeads];
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    if (g0 + k < G) acc[k] = fadd(acc[k], fmul(sc[(g0 + k) * chunk + p], v));
-            }
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                if (g0 + k < G) {
-                    const int h = kvh * G + g0 + k;
-                    float* rec = a.part + (((size_t)z * a.n_heads + h) * a.max_splits + split) * (hd + 2);
-                    rec[2 + d] = acc[k];
-                    if (d == 0) { rec[0] = red[2 * (g0 + k)]; rec[1] = red[2 * (g0 + k) + 1]; }
-                }
-            }
-        }
+        for (int i = 0; i < kPvHeads; ++i) acc[i] = 0.0f;
+        if (active)
+            for (int dd = d; dd < hd; dd += npg * hd) chunk_pv(vs, rs, es, G4, g0, ng, cn, dd, pg, npg, acc);
+        pv_reduce(acc, ng, hd, d, pg, npg, active, ks, [&](int i, int dd, float v) {
+            const int h = kvh * G + g0 + i;
+            float* rec = a.part + (((size_t)z * a.n_heads + h) * a.max_splits + split) * attn_record_floats(hd);
+            rec[4 + dd] = v;
+            if (dd == 0) { rec[0] = red[2 * (g0 + i)]; rec[1] = red[2 * (g0 + i) + 1]; }
+        });
     }
+    if (!a.counters) return;
+
+    // ---- the last CTA of this (query, KV head) to finish merges its records ----
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&a.counters[(size_t)z * a.n_kv + kvh], 1) == n_split - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    attn_merge(a, z, kvh * G, G, n_split, ks, ks + (size_t)G * a.max_splits, red);
+    if (tid == 0) a.counters[(size_t)z * a.n_kv + kvh] = 0;  // ready for the next launch
 }
 
-// Merge the split records of one (query, head):
-// out = (sum_s o_s * e^(m_s-M)) / (sum_s l_s * e^(m_s-M) + 1e-12); optionally
-// re-quantized (blockDim == hd, one warp per 32 outputs).
+// Merge the split records of one (query, head) when no arrival counters are given.
 __global__ void attn_combine_kernel(const AttnArgs a) {
     extern __shared__ float wsm[];  // [max_splits] weights, then [max_splits] sums
-    __shared__ float red[32];
-    __shared__ float s_inv;
+    __shared__ float s_inv[1];
     const int h = blockIdx.x, z = blockIdx.y;
-    const int hd = a.hd;
     int t0, len;
     attn_window(a, z, t0, len);
     const int n = (len + a.chunk - 1) / a.chunk;
-    const float* rec = a.part + ((size_t)z * a.n_heads + h) * a.max_splits * (hd + 2);
-    float* lsm = wsm + a.max_splits;
-    float M = -INFINITY;
-    for (int s = threadIdx.x; s < n; s += blockDim.x) {
-        const float m = rec[(size_t)s * (hd + 2)];
-        wsm[s] = m;
-        lsm[s] = rec[(size_t)s * (hd + 2) + 1];
-        M = fmaxf(M, m);
-    }
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = M;
-    __syncthreads();
-    M = red[0];
-    for (int k = 1; k < (int)(blockDim.x >> 5); ++k) M = fmaxf(M, red[k]);
-    for (int s = threadIdx.x; s < n; s += blockDim.x) wsm[s] = exp_cr(fsub(wsm[s], M));
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float L = 0.0f;
-        for (int s = 0; s < n; ++s) L = fadd(L, fmul(lsm[s], wsm[s]));
-        s_inv = fdiv(1.0f, fadd(L, 1e-12f));
-    }
-    __syncthreads();
-    const float inv = s_inv;
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        float o = 0.0f;
-#pragma unroll 8
-        for (int s = 0; s < n; ++s) o = fadd(o, fmul(rec[(size_t)s * (hd + 2) + 2 + d], wsm[s]));
-        o = fmul(o, inv);
-        if (a.out) a.out[(size_t)z * a.out_stride + (size_t)h * hd + d] = o;
-        if (a.act_out) {
-            ActBlock* dst = a.act_out + (size_t)z * (a.n_heads * hd / 32) + ((size_t)h * hd + d) / 32;
-            warp_quantize_store(o, dst, d & 31);
-        }
-    }
+    attn_merge(a, z, h, 1, n, wsm, wsm + a.max_splits, s_inv);
 }
 
-// Exact softmax * V in the reference's order (:1960-1987): max over the
-// window, e_t = exp(s_t - max) (correctly rounded here; the reference uses the
-// host expf), sum_exp serially over t, inv = 1/(sum_exp + 1e-12),
-// out[d] += (e_t * inv) * v_t[d] serially over t.  One CTA per (query, head).
-__global__ void attn_exact_kernel(const AttnArgs a) {
+// ---- exact mode (:1960-1987) ----
+// Softmax in the reference's order: max over the window (its running max
+// starts at -1e30), e_t = exp(s_t - max) (correctly rounded here; the reference
+// uses the host expf), sum_exp serially over t, inv = 1/(sum_exp + 1e-12); the
+// scores are replaced by p_t = e_t * inv.  One CTA per (head, query).
+constexpr int kExactThreads = 256;
+__global__ void __launch_bounds__(kExactThreads) attn_exact_softmax_kernel(const AttnArgs a) {
     const int h = blockIdx.x, z = blockIdx.y;
-    const int hd = a.hd, G = a.n_heads / a.n_kv, kvh = h / G;
     int t0, len;
     attn_window(a, z, t0, len);
     float* sc = a.scores + ((size_t)z * a.n_heads + h) * a.score_cap;
     __shared__ float red[32];
     __shared__ float s_inv;
-    float mx = -1e30f;  // the reference starts its running max at -1e30
-    for (int t = threadIdx.x; t < len; t += blockDim.x) mx = fmaxf(mx, sc[t]);
+    const int tid = threadIdx.x;
+    float mx = -1e30f;
+    for (int t = tid; t < len; t += kExactThreads) mx = fmaxf(mx, sc[t]);
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
     __syncthreads();
     mx = red[0];
-    for (int k = 1; k < (int)(blockDim.x >> 5); ++k) mx = fmaxf(mx, red[k]);
-    for (int t = threadIdx.x; t < len; t += blockDim.x) sc[t] = exp_cr(fsub(sc[t], mx));
+    for (int k = 1; k < kExactThreads / 32; ++k) mx = fmaxf(mx, red[k]);
+    for (int t = tid; t < len; t += kExactThreads) sc[t] = exp_cr(fsub(sc[t], mx));
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
+        // serial sum; the vector loads run ahead of the dependent adds
         float sum = 0.0f;
-        for (int t = 0; t < len; ++t) sum = fadd(sum, sc[t]);
+        const int n4 = ((uintptr_t)sc & 15) == 0 ? (len & ~3) : 0;
+        const float4* s4 = reinterpret_cast<const float4*>(sc);
+#pragma unroll 8
+        for (int i = 0; i < (n4 >> 2); ++i) {
+            const float4 v = s4[i];
+            sum = fadd(fadd(fadd(fadd(sum, v.x), v.y), v.z), v.w);
+        }
+        for (int t = n4; t < len; ++t) sum = fadd(sum, sc[t]);
         s_inv = fdiv(1.0f, fadd(sum, 1e-12f));
     }
     __syncthreads();
     const float inv = s_inv;
-    const float* vbase = a.vc + (size_t)t0 * a.kv_pos_stride + (size_t)kvh * a.kv_head_stride;
+    for (int t = tid; t < len; t += kExactThreads) sc[t] = fmul(sc[t], inv);
+}
+
+// out[h][d] = sum over t (serial) of p_t * v_t[d].  One CTA per (KV head,
+// group of up to 8 query heads, slice of kExactSlice output columns, query);
+// thread (g, d) runs one chain.  V rows and p stream through double-buffered
+// shared memory in tiles of kExactTile positions.
+constexpr int kExactSlice = 32;
+constexpr int kExactTile = 64;
+constexpr int kExactHeads = kExactThreads / kExactSlice;  // 8
+template <bool VEC>
+__global__ void __launch_bounds__(kExactThreads) attn_exact_pv_kernel(const AttnArgs a) {
+    __shared__ __align__(16) float vt[2][kExactTile][kExactSlice];
+    __shared__ __align__(16) float pt[2][kExactHeads][kExactTile];
+    const int slices = (a.hd + kExactSlice - 1) / kExactSlice;
+    const int G = a.n_heads / a.n_kv;
+    const int hgroups = (G + kExactHeads - 1) / kExactHeads;
+    int bx = blockIdx.x;
+    const int slice = bx % slices;
+    bx /= slices;
+    const int hg = bx % hgroups;
+    const int kvh = bx / hgroups;
+    const int z = blockIdx.y;
+    const int d0 = slice * kExactSlice;
+    const int g0 = hg * kExactHeads;
+    const int ng = min(kExactHeads, G - g0);
+    int t0, len;
+    attn_window(a, z, t0, len);
+    const int tid = threadIdx.x;
+    const int g = tid / kExactSlice, dl = tid % kExactSlice;
+    const int nd = min(kExactSlice, a.hd - d0);
+    const bool active = g < ng && dl < nd;
+    const float* vbase = a.vc + (size_t)t0 * a.kv_pos_stride + (size_t)kvh * a.kv_head_stride + d0;
     const size_t ps = (size_t)a.kv_pos_stride;
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        float o = 0.0f;
-#pragma unroll 16
-        for (int t = 0; t < len; ++t) o = fadd(o, fmul(fmul(sc[t], inv), vbase[(size_t)t * ps + d]));
-        if (a.out) a.out[(size_t)z * a.out_stride + (size_t)h * hd + d] = o;
-        if (a.act_out) {
-            ActBlock* dst = a.act_out + (size_t)z * (a.n_heads * hd / 32) + ((size_t)h * hd + d) / 32;
-            warp_quantize_store(o, dst, d & 31);
+    const float* pbase = a.scores + ((size_t)z * a.n_heads + kvh * G + g0) * a.score_cap;
+    const int n_tiles = (len + kExactTile - 1) / kExactTile;
+    auto issue = [&](int tile, int buf) {
+        const int tb = tile * kExactTile;
+        const int tn = min(kExactTile, len - tb);
+        if (VEC) {
+            const int vp = nd >> 2;  // 16-byte pieces per V row slice
+            for (int i = tid; i < tn * vp; i += kExactThreads) {
+                const int t = i / vp, c = i - t * vp;
+                cp_async16(&vt[buf][t][4 * c], vbase + (size_t)(tb + t) * ps + 4 * c);
+            }
+            const int pp = (tn + 3) >> 2;  // 16-byte pieces of p per head
+            for (int i = tid; i < ng * pp; i += kExactThreads) {
+                const int gg = i / pp, c = i - gg * pp;
+                cp_async16(&pt[buf][gg][4 * c], pbase + (size_t)gg * a.score_cap + tb + 4 * c);
+            }
+        } else {
+            for (int i = tid; i < tn * nd; i += kExactThreads) {
+                const int t = i / nd, c = i - t * nd;
+                vt[buf][t][c] = vbase[(size_t)(tb + t) * ps + c];
+            }
+            for (int i = tid; i < ng * tn; i += kExactThreads) {
+                const int gg = i / tn, t = i - gg * tn;
+                pt[buf][gg][t] = pbase[(size_t)gg * a.score_cap + tb + t];
+            }
         }
+        cp_async_commit();
+    };
+    float o = 0.0f;
+    issue(0, 0);
+    for (int tile = 0; tile < n_tiles; ++tile) {
+        const int buf = tile & 1;
+        if (tile + 1 < n_tiles) issue(tile + 1, buf ^ 1);
+        else cp_async_commit();  // an empty group keeps the wait count uniform
+        cp_async_wait<1>();
+        __syncthreads();
+        const int tn = min(kExactTile, len - tile * kExactTile);
+        if (active) {
+            const float* pp = pt[buf][g];
+#pragma unroll 16
+            for (int t = 0; t < tn; ++t) o = fadd(o, fmul(pp[t], vt[buf][t][dl]));
+        }
+        __syncthreads();  // the buffer is refilled two tiles on
     }
+    if (!active) return;
+    const int h = kvh * G + g0 + g;
+    a.out[(size_t)z * a.out_stride + (size_t)h * a.hd + d0 + dl] = o;
+}
+
+// Re-quantize exact-mode outputs for the next GEMV (one warp per 32 outputs).
+__global__ void attn_exact_quant_kernel(const AttnArgs a) {
+    const int z = blockIdx.y;
+    const int dim = a.n_heads * a.hd;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i - (int)(threadIdx.x & 31) >= dim) return;  // whole warp
+    const float o = a.out[(size_t)z * a.out_stride + i];
+    act_out_store(a.act_out, o, dim, (size_t)z, i >> 5, threadIdx.x & 31);
 }
 
 int attention_geometry_chunk(int32_t len, int32_t n_kv, int sm_count) {
@@ -295,15 +479,17 @@ int attention_geometry_chunk(int32_t len, int32_t n_kv, int sm_count) {
     return c;
 }
 
-template <bool BULK, bool SCORES_ONLY>
-static void launch_partial(const AttnArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
+template <bool VEC, bool SCORES_ONLY>
+static cudaError_t launch_partial(const AttnArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
     static size_t set_bytes = 0;
     if (smem > set_bytes) {
-        cudaFuncSetAttribute(attn_partial_kernel<BULK, SCORES_ONLY>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
+        const cudaError_t e = cudaFuncSetAttribute(attn_partial_kernel<VEC, SCORES_ONLY>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
         set_bytes = smem;
     }
-    attn_partial_kernel<BULK, SCORES_ONLY><<<grid, kAttnThreads, smem, st>>>(a);
+    attn_partial_kernel<VEC, SCORES_ONLY><<<grid, kAttnThreads, smem, st>>>(a);
+    return cudaPeekAtLastError();
 }
 
 int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
@@ -312,29 +498,45 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
         return kErrInvalidArg;
     if (a.n_heads % a.n_kv != 0 || a.hd > kMaxHeadDim || (a.hd & 3) || a.chunk <= 0 || a.max_splits <= 0)
         return kErrInvalidArg;
-    if (a.act_out && (a.hd % 32 || a.hd > 1024)) return kErrInvalidArg;
+    const bool act = a.act_out.blocks || a.act_out.staged;
+    if (act && a.hd % 32) return kErrInvalidArg;
+    if (a.act_out.staged && (n_tok != 1 || (a.n_heads * a.hd) % 256 || ((uintptr_t)a.act_out.staged & 15)))
+        return kErrInvalidArg;
     const DeviceInfo& dev = device_info();
     const int G = a.n_heads / a.n_kv;
-    const size_t smem = attn_smem_bytes(G, a.hd, a.chunk);
+    const size_t smem = attn_smem_bytes(G, a.hd, a.chunk, a.max_splits);
     if (smem > (size_t)dev.max_smem_optin) return kErrCapacity;
-    const bool bulk = ((uintptr_t)a.kc % 16 == 0) && ((uintptr_t)a.vc % 16 == 0);
+    const bool vec = ((uintptr_t)a.kc % 16 == 0) && ((uintptr_t)a.vc % 16 == 0) && (a.kv_pos_stride % 4 == 0) &&
+                     (a.kv_head_stride % 4 == 0);
     dim3 grid(a.max_splits, a.n_kv, n_tok);
+    cudaError_t e;
     if (a.exact) {
-        if (!a.scores || a.score_cap < a.max_splits * a.chunk) return kErrCapacity;
-        if (a.act_out && a.hd > 1024) return kErrInvalidArg;
-        if (bulk) launch_partial<true, true>(a, grid, smem, st);
-        else launch_partial<false, true>(a, grid, smem, st);
-        const int threads = (a.act_out || (a.hd % 32 == 0 && a.hd <= 1024)) ? a.hd : 128;
-        attn_exact_kernel<<<dim3(a.n_heads, n_tok), threads, 0, st>>>(a);
+        if (!a.scores || a.score_cap < a.max_splits * a.chunk || (a.score_cap & 3)) return kErrCapacity;
+        if (!a.out) return kErrInvalidArg;
+        e = vec ? launch_partial<true, true>(a, grid, smem, st) : launch_partial<false, true>(a, grid, smem, st);
+        if (e != cudaSuccess) return kErrCuda;
+        attn_exact_softmax_kernel<<<dim3(a.n_heads, n_tok), kExactThreads, 0, st>>>(a);
+        const int slices = (a.hd + kExactSlice - 1) / kExactSlice;
+        const int hgroups = (G + kExactHeads - 1) / kExactHeads;
+        const dim3 pv_grid(a.n_kv * hgroups * slices, n_tok);
+        if (vec && ((uintptr_t)a.scores & 15) == 0)
+            attn_exact_pv_kernel<true><<<pv_grid, kExactThreads, 0, st>>>(a);
+        else
+            attn_exact_pv_kernel<false><<<pv_grid, kExactThreads, 0, st>>>(a);
+        if (act) {
+            const int dim = a.n_heads * a.hd;
+            attn_exact_quant_kernel<<<dim3((dim + 255) / 256, n_tok), 256, 0, st>>>(a);
+        }
         return cudaPeekAtLastError() == cudaSuccess ? kOk : kErrCuda;
     }
-    if (bulk) launch_partial<true, false>(a, grid, smem, st);
-    else launch_partial<false, false>(a, grid, smem, st);
+    e = vec ? launch_partial<true, false>(a, grid, smem, st) : launch_partial<false, false>(a, grid, smem, st);
+    if (e != cudaSuccess) return kErrCuda;
+    if (a.counters) return kOk;  // merged by the last CTA of each (query, KV head)
     const size_t csm = (size_t)a.max_splits * 8;
-    if (csm > 48 * 1024)
-        cudaFuncSetAttribute(attn_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csm);
-    const int cthreads = (a.act_out || (a.hd % 32 == 0 && a.hd <= 1024)) ? a.hd : 128;
-    attn_combine_kernel<<<dim3(a.n_heads, n_tok), cthreads, csm, st>>>(a);
+    if (csm > 48 * 1024 &&
+        cudaFuncSetAttribute(attn_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csm) != cudaSuccess)
+        return kErrCuda;
+    attn_combine_kernel<<<dim3(a.n_heads, n_tok), 128, csm, st>>>(a);
     return cudaPeekAtLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
@@ -346,7 +548,7 @@ int32_t attention_scratch_records(int32_t pos, int32_t n_heads, int32_t window) 
 
 int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t n_heads, int32_t n_kv,
                      int32_t head_dim, float scale, int32_t window, float* out, const AttnScratch& scratch,
-                     int32_t* err, cudaStream_t st, float* exact_scores) {
+                     int32_t* err, cudaStream_t st, float* exact_scores, int* counters) {
     if (!q || !kc || !vc || !out || pos < 0 || n_heads <= 0 || n_kv <= 0 || head_dim <= 0) return kErrInvalidArg;
     const int32_t t0 = window > 0 ? (pos - window + 1 > 0 ? pos - window + 1 : 0) : 0;
     const int32_t len = pos + 1 - t0;
@@ -370,11 +572,12 @@ int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t 
     a.part = scratch.part;
     a.out = out;
     a.out_stride = n_heads * head_dim;
-    a.act_out = nullptr;
+    a.act_out = ActOut{nullptr, nullptr};
     a.err = err;
     a.exact = exact_scores != nullptr;
     a.scores = exact_scores;
     a.score_cap = a.max_splits * a.chunk;
+    a.counters = counters;
     return attention_run(a, 1, st);
 }
 

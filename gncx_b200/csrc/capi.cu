@@ -35,8 +35,10 @@ struct Runtime {
     int32_t* h_err = nullptr;  // pinned
     uint8_t* ws = nullptr;
     size_t ws_bytes = 0;
+    int* attn_counters = nullptr;  // kAttnCounters arrival counters, zero between launches
     std::vector<Mapping> maps;
 };
+static constexpr int kAttnCounters = 8192;
 
 static Runtime g_rt;
 static std::mutex g_maps_mu;
@@ -87,12 +89,14 @@ static int32_t ensure_init() {
         g_rt.device = dev;
         if ((e = cudaStreamCreateWithFlags(&g_rt.own, cudaStreamNonBlocking)) != cudaSuccess ||
             (e = cudaMalloc(&g_rt.d_err, sizeof(int32_t))) != cudaSuccess ||
-            (e = cudaMallocHost(&g_rt.h_err, sizeof(int32_t))) != cudaSuccess) {
+            (e = cudaMallocHost(&g_rt.h_err, sizeof(int32_t))) != cudaSuccess ||
+            (e = cudaMalloc(&g_rt.attn_counters, kAttnCounters * sizeof(int))) != cudaSuccess) {
             set_error(kErrCuda, cuda_msg(e));
             g_rt.device = -1;
             return kErrCuda;
         }
         cudaMemset(g_rt.d_err, 0, sizeof(int32_t));
+        cudaMemset(g_rt.attn_counters, 0, kAttnCounters * sizeof(int));
         g_rt.stream = g_rt.own;
         device_info();
     }
@@ -625,14 +629,15 @@ void gncx_mqa_attention_step_ext(const float* q_vec, const float* k_vec, const f
         cudaMemcpyAsync(vc + (size_t)pos * kvd, v, kvd * 4, cudaMemcpyDefault, stream());
     }
     const int32_t recs = attention_scratch_records(pos, n_heads, window);
-    const size_t part_bytes = align256((size_t)recs * (hd + 2) * 4);
+    const size_t part_bytes = align256((size_t)recs * attn_record_floats(hd) * 4);
     const size_t score_floats = (size_t)n_heads * (((size_t)pos + 1 + 63) / 64 * 64);
     uint8_t* ws = workspace(part_bytes + (g_exact_attention ? score_floats * 4 : 0));
     if (!ws) return;
     float* part = reinterpret_cast<float*>(ws);
     float* scores = g_exact_attention ? reinterpret_cast<float*>(ws + part_bytes) : nullptr;
+    int* counters = (int64_t)n_heads * hd / 32 <= kAttnCounters ? g_rt.attn_counters : nullptr;
     finish(attention_launch(q, kc, vc, pos, n_heads, n_kv, hd, attn_scale, window, out, AttnScratch{part, recs},
-                            g_rt.d_err, stream(), scores));
+                            g_rt.d_err, stream(), scores, counters));
 }
 
 void gncx_mqa_attention_step(const float* q_vec, const float* k_vec, const float* v_vec, float* k_cache,
@@ -667,9 +672,12 @@ int32_t gncx_matvec_preq(const uint8_t* base, size_t off, int32_t type, const vo
     if (ensure_init() != kOk) return g_status;
     const uint8_t* b = xl(base);
     if (check_dev(b, "base") || check_dev(act, "act") || check_dev(out_vec, "out_vec")) return g_status;
-    if (type == kBF16) return finish(kErrInvalidArg);
-    return finish(gemv_launch(b + off, type, nullptr, static_cast<const ActBlock*>(act), in_dim, out_dim, out_vec,
-                              0.0f, g_rt.d_err, stream()));
+    if (type == kBF16 || in_dim <= 0 || (in_dim & 255)) return finish(kErrInvalidArg);
+    uint8_t* staged = workspace(staged_act_bytes(in_dim));
+    if (!staged) return g_status;
+    int32_t st = act_stage_launch(static_cast<const ActBlock*>(act), in_dim, staged, stream());
+    if (st == kOk) st = gemv_launch(b + off, type, nullptr, staged, in_dim, out_dim, out_vec, 0.0f, g_rt.d_err, stream());
+    return finish(st);
 }
 
 int32_t gncx_dequantize_rows(const uint8_t* base, size_t off, int32_t type, int32_t rows, int32_t n, float* out) {

@@ -179,11 +179,12 @@ struct Engine {
     float *rope_c = nullptr, *rope_s = nullptr;
     // decode buffers
     float *hidden = nullptr, *proj = nullptr, *qkv = nullptr, *gu = nullptr, *logits = nullptr, *normed = nullptr;
-    ActBlock *act_d = nullptr, *act_q = nullptr, *act_f = nullptr;
+    uint8_t *act_d = nullptr, *act_q = nullptr, *act_f = nullptr;  // staged activation vectors
     float* part = nullptr;
     int max_splits = 0;
     bool exact = false;      // exact serial softmax in attention
     float* scores = nullptr; // [n_heads][max_splits * chunk] (decode, exact mode)
+    int* attn_counters = nullptr;  // [kPrefillGroup][n_kv], zero between attention launches
     int graph_exact = -1;
     DecodeState* st = nullptr;
     DecodeState* st_host = nullptr;  // pinned staging
@@ -222,7 +223,7 @@ static constexpr int kPrefillGroup = 256;  // prompt positions per attention lau
         if ((x) != cudaSuccess) return kErrCuda;          \
     } while (0)
 
-static int gemv(Engine* e, const uint8_t* w, int t, const ActBlock* act, const float* x, int in, int out, float* y,
+static int gemv(Engine* e, const uint8_t* w, int t, const uint8_t* act, const float* x, int in, int out, float* y,
                 float cap = 0.0f) {
     return gemv_launch(w, t, t == kBF16 ? x : nullptr, t == kBF16 ? nullptr : act, in, out, y, cap, e->d_err,
                        e->stream);
@@ -237,8 +238,8 @@ static int decode_step(Engine* e, bool sample, double penalty) {
     CK(dequant_launch(e->tok_embd, e->embd_type, 1, D, e->embd_scale, &e->st->token, e->hidden, s));
     for (int l = 0; l < e->n_layers; ++l) {
         const LayerW& w = e->L[l];
-        CK(add_norm_quant_launch(e->hidden, l == 0 ? nullptr : e->proj, w.attn_norm, 1, D, e->eps, e->act_d, e->normed,
-                                 s));
+        CK(add_norm_quant_launch(e->hidden, l == 0 ? nullptr : e->proj, w.attn_norm, 1, D, e->eps,
+                                 ActOut{nullptr, e->act_d}, e->normed, s));
         if (w.qkv_fused) {
             CK(gemv(e, w.wq, w.tq, e->act_d, e->normed, D, qkv_w, e->qkv));
         } else {
@@ -265,26 +266,28 @@ static int decode_step(Engine* e, bool sample, double penalty) {
         a.chunk = kDecodeChunk;
         a.max_splits = e->max_splits;
         a.part = e->part;
-        a.out = nullptr;
-        a.out_stride = QD;
-        a.act_out = e->act_q;
+        a.out = e->exact ? e->qkv : nullptr;  // exact mode: the output replaces q
+        a.out_stride = qkv_w;
+        a.counters = nullptr;  // one query: a separate merge kernel is faster than the last-CTA merge
+        a.act_out = ActOut{nullptr, e->act_q};
         a.err = e->d_err;
         a.exact = e->exact ? 1 : 0;
         a.scores = e->scores;
         a.score_cap = e->max_splits * kDecodeChunk;
         CK(attention_run(a, 1, s));
         CK(gemv(e, w.wo, w.to, e->act_q, nullptr, QD, D, e->proj));
-        CK(add_norm_quant_launch(e->hidden, e->proj, w.ffn_norm, 1, D, e->eps, e->act_d, e->normed, s));
+        CK(add_norm_quant_launch(e->hidden, e->proj, w.ffn_norm, 1, D, e->eps, ActOut{nullptr, e->act_d}, e->normed,
+                                 s));
         if (w.gu_fused) {
             CK(gemv(e, w.wg, w.tg, e->act_d, e->normed, D, 2 * F, e->gu));
         } else {
             CK(gemv(e, w.wg, w.tg, e->act_d, e->normed, D, F, e->gu));
             CK(gemv(e, w.wu, w.tu, e->act_d, e->normed, D, F, e->gu + F));
         }
-        CK(glu_quant_launch(e->gu, e->gu + F, 2 * F, F, 1, e->arch == 2, e->act_f, s));
+        CK(glu_quant_launch(e->gu, e->gu + F, 2 * F, F, 1, e->arch == 2, ActOut{nullptr, e->act_f}, s));
         CK(gemv(e, w.wd, w.td, e->act_f, nullptr, F, D, e->proj));
     }
-    CK(add_norm_quant_launch(e->hidden, e->proj, e->out_norm, 1, D, e->eps, e->act_d, e->normed, s));
+    CK(add_norm_quant_launch(e->hidden, e->proj, e->out_norm, 1, D, e->eps, ActOut{nullptr, e->act_d}, e->normed, s));
     CK(gemv(e, e->tok_embd, e->embd_type, e->act_d, e->normed, D, e->vocab, e->logits, e->softcap));
     if (sample) CK(argmax_state_launch(e->logits, e->vocab, e->st, penalty, e->out_ids, 1, e->am_scratch, s));
     return kOk;
@@ -300,7 +303,7 @@ static int ensure_prefill(Engine* e, int B) {
     const size_t D = e->dim, QKV = e->q_dim + 2 * e->kv_dim, F = e->ffn;
     const int grp = B < kPrefillGroup ? B : kPrefillGroup;
     const size_t splits = (size_t)(B + kDecodeChunk - 1) / kDecodeChunk;
-    e->pf_part_floats = (size_t)grp * e->nh * splits * (e->hd + 2);
+    e->pf_part_floats = (size_t)grp * e->nh * splits * attn_record_floats(e->hd);
     if (cudaMalloc(&e->pf_h, (size_t)B * D * 4) || cudaMalloc(&e->pf_p, (size_t)B * D * 4) ||
         cudaMalloc(&e->pf_qkv, (size_t)B * QKV * 4) || cudaMalloc(&e->pf_gu, (size_t)B * 2 * F * 4) ||
         cudaMalloc(&e->pf_part, e->pf_part_floats * 4) ||
@@ -327,7 +330,8 @@ static int prefill_batch(Engine* e, int B) {
     CK(dequant_launch(e->tok_embd, e->embd_type, B, D, e->embd_scale, e->ids_dev, e->pf_h, s));
     for (int l = 0; l < e->n_layers; ++l) {
         const LayerW& w = e->L[l];
-        CK(add_norm_quant_launch(e->pf_h, l == 0 ? nullptr : e->pf_p, w.attn_norm, B, D, e->eps, e->pf_act, nullptr, s));
+        CK(add_norm_quant_launch(e->pf_h, l == 0 ? nullptr : e->pf_p, w.attn_norm, B, D, e->eps,
+                                 ActOut{e->pf_act, nullptr}, nullptr, s));
         if (w.qkv_fused) {
             CK(matbatch_launch(w.wq, w.tq, nullptr, e->pf_act, B, D, qkv_w, e->pf_qkv, e->d_err, s, qkv_w));
         } else {
@@ -356,31 +360,33 @@ static int prefill_batch(Engine* e, int B) {
             a.chunk = kDecodeChunk;
             a.max_splits = (z0 + nz + kDecodeChunk - 1) / kDecodeChunk;
             a.part = e->pf_part;
-            a.out = nullptr;
-            a.out_stride = QD;
-            a.act_out = e->pf_actq + (size_t)z0 * (QD / 32);
+            a.out = e->exact ? e->pf_qkv + (size_t)z0 * qkv_w : nullptr;
+            a.out_stride = qkv_w;
+            a.counters = e->attn_counters;
+            a.act_out = ActOut{e->pf_actq + (size_t)z0 * (QD / 32), nullptr};
             a.err = e->d_err;
             a.exact = e->exact ? 1 : 0;
             a.scores = e->pf_scores;
             a.score_cap = (int)e->pf_score_cap;
-            if ((size_t)nz * e->nh * a.max_splits * (e->hd + 2) > e->pf_part_floats) return kErrCapacity;
+            if ((size_t)nz * e->nh * a.max_splits * attn_record_floats(e->hd) > e->pf_part_floats) return kErrCapacity;
             CK(attention_run(a, nz, s));
         }
         CK(matbatch_launch(w.wo, w.to, nullptr, e->pf_actq, B, QD, D, e->pf_p, e->d_err, s));
-        CK(add_norm_quant_launch(e->pf_h, e->pf_p, w.ffn_norm, B, D, e->eps, e->pf_act, nullptr, s));
+        CK(add_norm_quant_launch(e->pf_h, e->pf_p, w.ffn_norm, B, D, e->eps, ActOut{e->pf_act, nullptr}, nullptr, s));
         if (w.gu_fused) {
             CK(matbatch_launch(w.wg, w.tg, nullptr, e->pf_act, B, D, 2 * F, e->pf_gu, e->d_err, s, 2 * F));
         } else {
             CK(matbatch_launch(w.wg, w.tg, nullptr, e->pf_act, B, D, F, e->pf_gu, e->d_err, s, 2 * F));
             CK(matbatch_launch(w.wu, w.tu, nullptr, e->pf_act, B, D, F, e->pf_gu + F, e->d_err, s, 2 * F));
         }
-        CK(glu_quant_launch(e->pf_gu, e->pf_gu + F, 2 * F, F, B, e->arch == 2, e->pf_actf, s));
+        CK(glu_quant_launch(e->pf_gu, e->pf_gu + F, 2 * F, F, B, e->arch == 2, ActOut{e->pf_actf, nullptr}, s));
         CK(matbatch_launch(w.wd, w.td, nullptr, e->pf_actf, B, F, D, e->pf_p, e->d_err, s));
     }
     // last position: residual, final norm, LM head (:1185-1205)
     const size_t last = (size_t)(B - 1) * D;
     CU(cudaMemcpyAsync(e->hidden, e->pf_h + last, (size_t)D * 4, cudaMemcpyDeviceToDevice, s));
-    CK(add_norm_quant_launch(e->hidden, e->pf_p + last, e->out_norm, 1, D, e->eps, e->act_d, e->normed, s));
+    CK(add_norm_quant_launch(e->hidden, e->pf_p + last, e->out_norm, 1, D, e->eps, ActOut{nullptr, e->act_d},
+                             e->normed, s));
     CK(gemv(e, e->tok_embd, e->embd_type, e->act_d, e->normed, D, e->vocab, e->logits, e->softcap));
     return kOk;
 }
@@ -569,11 +575,13 @@ static int engine_load(Engine* e, const char* path, int max_seq, std::string& er
     CU(cudaMalloc(&e->qkv, (size_t)(e->q_dim + 2 * e->kv_dim) * 4));
     CU(cudaMalloc(&e->gu, 2 * F * 4));
     CU(cudaMalloc(&e->logits, (size_t)e->vocab * 4));
-    CU(cudaMalloc(&e->act_d, (D / 32) * sizeof(ActBlock)));
-    CU(cudaMalloc(&e->act_q, (size_t)(e->q_dim / 32) * sizeof(ActBlock)));
-    CU(cudaMalloc(&e->act_f, (F / 32) * sizeof(ActBlock)));
-    CU(cudaMalloc(&e->part, (size_t)e->nh * e->max_splits * (e->hd + 2) * 4));
+    CU(cudaMalloc(&e->act_d, staged_act_bytes(D)));
+    CU(cudaMalloc(&e->act_q, staged_act_bytes(e->q_dim)));
+    CU(cudaMalloc(&e->act_f, staged_act_bytes(F)));
+    CU(cudaMalloc(&e->part, (size_t)e->nh * e->max_splits * attn_record_floats(e->hd) * 4));
     CU(cudaMalloc(&e->scores, (size_t)e->nh * e->max_splits * kDecodeChunk * 4));
+    CU(cudaMalloc(&e->attn_counters, (size_t)kPrefillGroup * e->nkv * sizeof(int)));
+    CU(cudaMemset(e->attn_counters, 0, (size_t)kPrefillGroup * e->nkv * sizeof(int)));
     CU(cudaMalloc(&e->st, sizeof(DecodeState)));
     CU(cudaMallocHost(&e->st_host, sizeof(DecodeState)));
     CU(cudaMalloc(&e->am_scratch, argmax_state_scratch_bytes()));
@@ -590,7 +598,7 @@ static void engine_free(Engine* e) {
     if (!e) return;
     if (e->stream) cudaStreamSynchronize(e->stream);
     if (e->graph) cudaGraphExecDestroy(e->graph);
-    void* bufs[] = {e->scores, e->pf_scores, e->arena, e->kv, e->rope_c, e->rope_s, e->hidden, e->normed, e->proj, e->qkv, e->gu, e->logits,
+    void* bufs[] = {e->scores, e->attn_counters, e->pf_scores, e->arena, e->kv, e->rope_c, e->rope_s, e->hidden, e->normed, e->proj, e->qkv, e->gu, e->logits,
                     e->act_d, e->act_q, e->act_f, e->part, e->st, e->am_scratch, e->d_err, e->out_ids, e->ids_dev,
                     e->pf_h, e->pf_p, e->pf_qkv, e->pf_gu, e->pf_part, e->pf_act, e->pf_actq, e->pf_actf};
     for (void* b : bufs)

@@ -13,6 +13,7 @@
 #include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 #include "norm.cuh"
 
 namespace gncx {
@@ -20,12 +21,12 @@ namespace gncx {
 static int status() { return cudaPeekAtLastError() == cudaSuccess ? kOk : kErrCuda; }
 
 // ---------------------------------------------------------------- add + norm + quantize
-// One CTA per row: hidden[r] += residual[r] (if given, written back), then
-// y = rmsnorm(hidden[r]) * w, re-quantized to act[r][dim/32] (and optionally
-// stored as fp32 in normed).
+// Prefill form, one CTA per row: hidden[r] += residual[r] (if given, written
+// back), then y = rmsnorm(hidden[r]) * w, re-quantized to act blocks (and
+// optionally stored as fp32 in normed).
 __global__ void __launch_bounds__(256) add_norm_quant_kernel(float* hidden, const float* residual,
                                                              const float* __restrict__ w, int dim, float eps,
-                                                             ActBlock* act, float* normed) {
+                                                             ActOut act, float* normed) {
     extern __shared__ float xs[];
     const size_t base = (size_t)blockIdx.x * dim;
     for (int i = threadIdx.x; i < dim; i += blockDim.x) {
@@ -44,16 +45,129 @@ __global__ void __launch_bounds__(256) add_norm_quant_kernel(float* hidden, cons
         const int i = b * 32 + lane;
         const float v = fmul(fmul(xs[i], inv), w[i]);
         if (normed) normed[base + i] = v;
-        warp_quantize_store(v, act + (size_t)blockIdx.x * nb + b, lane);
+        act_out_store(act, v, dim, blockIdx.x, b, lane);
+    }
+}
+
+// Decode form (one row, staged output, one CTA of kRowThreads): the norm gains
+// are fetched before the dependency wait; each thread owns 8 consecutive
+// inputs per pass, writes their squares lane-major for the four serial chains,
+// and after the chains quantizes its 8 outputs (four threads per 32-input
+// block).  The next kernel may launch (and prefetch its weights) meanwhile.
+constexpr int kRowThreads = 512;
+constexpr int kRowPasses = 2;  // dim <= kRowPasses * 8 * kRowThreads
+
+__global__ void __launch_bounds__(kRowThreads) add_norm_quant_row_kernel(float* hidden, const float* residual,
+                                                                         const float* __restrict__ w, int dim,
+                                                                         float eps, uint8_t* staged, float* normed) {
+    extern __shared__ __align__(16) float sq[];  // [4][dim/4]
+    const int tid = threadIdx.x;
+    const int n4 = dim >> 2;
+    float g[kRowPasses][8];
+#pragma unroll
+    for (int ps = 0; ps < kRowPasses; ++ps) {
+        const int base = (ps * kRowThreads + tid) * 8;
+        if (base < dim) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(w + base));
+            const float4 b = __ldg(reinterpret_cast<const float4*>(w + base + 4));
+            g[ps][0] = a.x; g[ps][1] = a.y; g[ps][2] = a.z; g[ps][3] = a.w;
+            g[ps][4] = b.x; g[ps][5] = b.y; g[ps][6] = b.z; g[ps][7] = b.w;
+        }
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    float x[kRowPasses][8];
+#pragma unroll
+    for (int ps = 0; ps < kRowPasses; ++ps) {
+        const int base = (ps * kRowThreads + tid) * 8;
+        if (base < dim) {
+            float4* h4 = reinterpret_cast<float4*>(hidden + base);
+            float4 a = h4[0], b = h4[1];
+            if (residual) {
+                const float4* r4 = reinterpret_cast<const float4*>(residual + base);
+                const float4 ra = r4[0], rb = r4[1];
+                a = make_float4(fadd(a.x, ra.x), fadd(a.y, ra.y), fadd(a.z, ra.z), fadd(a.w, ra.w));
+                b = make_float4(fadd(b.x, rb.x), fadd(b.y, rb.y), fadd(b.z, rb.z), fadd(b.w, rb.w));
+                h4[0] = a;
+                h4[1] = b;
+            }
+            x[ps][0] = a.x; x[ps][1] = a.y; x[ps][2] = a.z; x[ps][3] = a.w;
+            x[ps][4] = b.x; x[ps][5] = b.y; x[ps][6] = b.z; x[ps][7] = b.w;
+            // inputs base+j and base+4+j belong to chain j at k = base/4 and base/4 + 1
+            const int k = base >> 2;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                *reinterpret_cast<float2*>(sq + (size_t)j * n4 + k) =
+                    make_float2(fmul(x[ps][j], x[ps][j]), fmul(x[ps][4 + j], x[ps][4 + j]));
+        }
+    }
+    __syncthreads();
+    const float inv = rms_inv_sq(sq, n4, eps);
+    const int q4 = tid & 3;
+    float4* rec = reinterpret_cast<float4*>(staged + dim);
+#pragma unroll
+    for (int ps = 0; ps < kRowPasses; ++ps) {
+        const int base = (ps * kRowThreads + tid) * 8;
+        if (ps * kRowThreads * 8 >= dim) break;  // uniform across the CTA
+        const bool ok = base < dim;
+        float v[8];
+        float amax = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            v[e] = ok ? fmul(fmul(x[ps][e], inv), g[ps][e]) : 0.0f;
+            amax = fmaxf(amax, fabsf(v[e]));
+        }
+        if (ok && normed) {
+            reinterpret_cast<float4*>(normed + base)[0] = make_float4(v[0], v[1], v[2], v[3]);
+            reinterpret_cast<float4*>(normed + base)[1] = make_float4(v[4], v[5], v[6], v[7]);
+        }
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        uint32_t w0 = 0, w1 = 0;
+        int part = 0;
+        float d = 0.0f;
+        if (amax != 0.0f) {
+            const float qi = fdiv(127.0f, amax);
+            d = fdiv(amax, 127.0f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int qv = __float2int_rn(fmul(v[e], qi));
+                part += qv;
+                if (e < 4) w0 |= ((uint32_t)qv & 0xFFu) << (8 * e);
+                else w1 |= ((uint32_t)qv & 0xFFu) << (8 * (e - 4));
+            }
+        }
+        const int pair = part + __shfl_xor_sync(0xffffffffu, part, 1);  // quarters 0+1 or 2+3
+        const int other = __shfl_xor_sync(0xffffffffu, pair, 2);
+        if (ok) {
+            const int b = base >> 5;
+            *reinterpret_cast<uint2*>(staged + act_chunk_pos(b >> 3, 2 * (b & 7) + (q4 >> 1)) + 8 * (q4 & 1)) =
+                make_uint2(w0, w1);
+            if (q4 == 0)
+                rec[act_rec_pos(b)] = make_float4(d, __int_as_float(pair), __int_as_float(other),
+                                                  __int_as_float(pair + other));
+        }
     }
 }
 
 int add_norm_quant_launch(float* hidden, const float* residual, const float* w, int32_t rows, int32_t dim, float eps,
-                          ActBlock* act, float* normed, cudaStream_t st) {
-    if (!hidden || !w || !act || rows < 0 || dim <= 0 || (dim & 31)) return kErrInvalidArg;
+                          ActOut act, float* normed, cudaStream_t st) {
+    if (!hidden || !w || (!act.blocks && !act.staged) || rows < 0 || dim <= 0 || (dim & 31)) return kErrInvalidArg;
+    if (act.staged && (rows != 1 || (dim & 255) || ((uintptr_t)act.staged & 15))) return kErrInvalidArg;
     if (rows == 0) return kOk;
     const size_t smem = (size_t)dim * 4;
     if (smem > 200 * 1024) return kErrCapacity;
+    const bool vec = ((uintptr_t)hidden & 15) == 0 && ((uintptr_t)residual & 15) == 0 && ((uintptr_t)w & 15) == 0 &&
+                     ((uintptr_t)normed & 15) == 0;
+    if (act.staged && vec && dim <= kRowPasses * 8 * kRowThreads) {
+        if (smem > 48 * 1024 && cudaFuncSetAttribute(add_norm_quant_row_kernel,
+                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return kErrCuda;
+        return launch_k(add_norm_quant_row_kernel, dim3(1), dim3(kRowThreads), smem, st, hidden, residual, w, dim,
+                        eps, act.staged, normed) == cudaSuccess
+                   ? kOk
+                   : kErrCuda;
+    }
     if (smem > 48 * 1024)
         cudaFuncSetAttribute(add_norm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     add_norm_quant_kernel<<<rows, 256, smem, st>>>(hidden, residual, w, dim, eps, act, normed);
@@ -117,7 +231,9 @@ int qkv_post_launch(float* qkv, int32_t row_stride, int32_t rows, int32_t nh, in
 // ---------------------------------------------------------------- GLU + quantize
 // One warp per 32-output block: out = glu(gate, up), re-quantized for ffn_down.
 __global__ void glu_quant_kernel(const float* __restrict__ g, const float* __restrict__ u, int stride, int ffn,
-                                 int rows, int gelu, ActBlock* act) {
+                                 int rows, int gelu, ActOut act) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int nbf = ffn >> 5;
     const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -126,17 +242,20 @@ __global__ void glu_quant_kernel(const float* __restrict__ g, const float* __res
     const int b = (int)(gw % nbf);
     const size_t i = (size_t)r * stride + (size_t)b * 32 + lane;
     const float v = gelu ? geglu1(g[i], u[i]) : swiglu1(g[i], u[i]);
-    warp_quantize_store(v, act + (size_t)r * nbf + b, lane);
+    act_out_store(act, v, ffn, (size_t)r, b, lane);
 }
 
 int glu_quant_launch(const float* g, const float* u, int32_t stride, int32_t ffn, int32_t rows, bool gelu,
-                     ActBlock* act, cudaStream_t st) {
-    if (!g || !u || !act || ffn <= 0 || (ffn & 31) || rows < 0) return kErrInvalidArg;
+                     ActOut act, cudaStream_t st) {
+    if (!g || !u || (!act.blocks && !act.staged) || ffn <= 0 || (ffn & 31) || rows < 0) return kErrInvalidArg;
+    if (act.staged && (rows != 1 || (ffn & 255) || ((uintptr_t)act.staged & 15))) return kErrInvalidArg;
     if (rows == 0) return kOk;
     const int64_t warps = (int64_t)rows * (ffn >> 5);
     const int64_t blocks = (warps + 7) / 8;
-    glu_quant_kernel<<<(unsigned)blocks, 256, 0, st>>>(g, u, stride, ffn, rows, gelu ? 1 : 0, act);
-    return status();
+    return launch_k(glu_quant_kernel, dim3((unsigned)blocks), dim3(256), 0, st, g, u, stride, ffn, rows,
+                    gelu ? 1 : 0, act) == cudaSuccess
+               ? kOk
+               : kErrCuda;
 }
 
 // ---------------------------------------------------------------- argmax -> decode state

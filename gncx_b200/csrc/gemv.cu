@@ -8,31 +8,34 @@
 //     memory stages with cp.async.bulk (TMA) completing on mbarriers.  Each row
 //     segment is copied as its 16-byte-aligned superset, so any base/row
 //     alignment works (an aligned 16-byte chunk never crosses a page);
-//   * eight compute warps re-quantize x to int8 per 32 inputs once per CTA
-//     (or load blocks another kernel quantized), then each lane computes one
-//     256-input unit of one row with dp4a integer dots and the reference's
+//   * the compute warps re-quantize x to int8 per 32 inputs once per CTA, or
+//     bulk-copy a vector the producing kernel already quantized in the same
+//     shared-memory layout ("staged" act); each lane then computes one or two
+//     256-input units of one row with dp4a integer dots and the reference's
 //     exactly-rounded fp32 scale arithmetic;
-//   * the eight lanes of a row add their unit terms to the row accumulator in
-//     unit order with a shuffle chain, which reproduces the reference's serial
-//     per-row accumulation bit for bit.
+//   * the lanes of a row park their unit terms in shared memory and the row's
+//     first lane adds them to the row accumulator in unit order, which
+//     reproduces the reference's serial per-row accumulation bit for bit.
 // HBM traffic is the weight bytes once plus the (L2-resident) activation.
 #include <cuda_runtime.h>
 #include <stdlib.h>
 #include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 #include "tma.cuh"
 #include "units.cuh"
 
 namespace gncx {
 
 constexpr int kMaxUnitsPerLane = 2;
+constexpr size_t kGemvSmemCap = 200 * 1024;
 
 struct GemvArgs {
     const uint8_t* w;
     size_t rb;              // bytes per row
     const float* x;         // fp32 activations (PREQ == false)
-    const ActBlock* act;    // pre-quantized activations (PREQ == true)
+    const uint8_t* act;     // staged activations (PREQ == true): staged_act_bytes(in_dim)
     float* y;
     int in_dim, out_dim;
     int upr;                // units (256 inputs) per row
@@ -48,8 +51,10 @@ struct GemvArgs {
 struct GemvSmem {
     uint64_t* full;
     uint64_t* empty;
+    uint64_t* act_bar;
     int8_t* qs;
     float4* rec;
+    float* red;      // [CW][64 * E] unit terms awaiting the serial row sum
     uint8_t* stage0;
 };
 
@@ -58,26 +63,30 @@ __host__ __device__ inline size_t gemv_act_bytes(int in_dim) {
     return (size_t)in_dim + (size_t)nb * 16;
 }
 
-__host__ __device__ inline size_t gemv_smem_bytes(int in_dim, int stage_bytes, int stages) {
+__host__ __device__ inline size_t gemv_red_bytes(int cw, int e) { return (size_t)cw * 64 * e * 4; }
+
+__host__ __device__ inline size_t gemv_smem_bytes(int in_dim, int stage_bytes, int stages, size_t red_bytes) {
     size_t off = 128;  // barriers
     off += (gemv_act_bytes(in_dim) + 127) & ~(size_t)127;
+    off += red_bytes;
     off += (size_t)stages * stage_bytes;
     return off;
 }
 
-__device__ inline GemvSmem carve(uint8_t* base, int in_dim, int stages) {
+__device__ inline GemvSmem carve(uint8_t* base, int in_dim, int stages, size_t red_bytes) {
     GemvSmem s;
     s.full = reinterpret_cast<uint64_t*>(base);
     s.empty = s.full + stages;
+    s.act_bar = s.empty + stages;
     uint8_t* p = base + 128;
     s.qs = reinterpret_cast<int8_t*>(p);
     s.rec = reinterpret_cast<float4*>(p + in_dim);
-    s.stage0 = base + 128 + ((gemv_act_bytes(in_dim) + 127) & ~(size_t)127);
+    p += (gemv_act_bytes(in_dim) + 127) & ~(size_t)127;
+    s.red = reinterpret_cast<float*>(p);
+    s.stage0 = p + red_bytes;
     return s;
 }
 
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 // One pipeline stage = one tile of `rows` consecutive whole rows, which are
 // contiguous in memory and arrive with a single bulk copy (its 16-byte-aligned
@@ -90,7 +99,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) gemv_kernel(const GemvArgs a
     constexpr int UB = Fmt<T>::UB, NW = Fmt<T>::NW, E = Fmt<T>::E;
     constexpr int CT = CW * 32;
     extern __shared__ __align__(128) uint8_t smem[];
-    const GemvSmem sm = carve(smem, args.in_dim, args.stages);
+    const GemvSmem sm = carve(smem, args.in_dim, args.stages, gemv_red_bytes(CW, E));
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int S = args.stages;
@@ -102,6 +111,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) gemv_kernel(const GemvArgs a
             mbar_init(&sm.full[i], 1);
             mbar_init(&sm.empty[i], CW);
         }
+        mbar_init(sm.act_bar, 1);
         abort_flag = 0;
         fence_barrier_init();
     }
@@ -139,16 +149,30 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) gemv_kernel(const GemvArgs a
 
     // ---------------- compute warps ----------------
     pdl_wait();  // x / act and y belong to the preceding kernel's world from here on
-    if (PREQ) stage_act_blocks(args.act, args.in_dim, sm.qs, sm.rec, tid, CT);
-    else stage_act_fp32(args.x, args.in_dim, sm.qs, sm.rec, tid, CT);
+    if (PREQ) {
+        // the staged vector is already in the shared-memory layout: one bulk copy
+        if (tid == 0) {
+            const uint32_t bytes = (uint32_t)gemv_act_bytes(args.in_dim);
+            mbar_arrive_expect_tx(sm.act_bar, bytes);
+            bulk_g2s(sm.qs, args.act, bytes, sm.act_bar);
+        }
+        if (!mbar_wait(sm.act_bar, 0)) {
+            record_error(args.err, kErrTimeout);
+            atomicExch(&abort_flag, 1);
+        }
+    } else {
+        stage_act_fp32(args.x, args.in_dim, sm.qs, sm.rec, tid, CT);
+    }
     asm volatile("bar.sync 1, %0;" ::"r"(CT) : "memory");
     const ActView av{sm.qs, sm.rec};
 
     const int lpr = args.lpr;
     const int rloc = tid / lpr;          // row within tile
     const int j = tid - rloc * lpr;      // lane within the row group
-    const int gbase = lane - j;          // first lane of this row's group
     const int upr = args.upr;
+    const int n_terms = upr * E;                           // terms per row
+    float* const red_w = sm.red + (size_t)warp * 64 * E;   // this warp's rows
+    const int rbase = (lane / lpr) * n_terms;
     const float inv_cap = args.softcap > 0.0f ? fdiv(1.0f, args.softcap) : 0.0f;
 
     int item = 0;
@@ -180,20 +204,36 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) gemv_kernel(const GemvArgs a
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[s]);
-        // Serial chain over the row's units in unit order (unit u = k*lpr + owner).
-        float acc = 0.0f;
+        // Park the terms (row-major, unit order), then the row's first lane adds
+        // them serially: unit u = k*lpr + j, terms e = 0..E-1 within a unit.
 #pragma unroll
         for (int k = 0; k < kMaxUnitsPerLane; ++k) {
-            const int nj = min(lpr, upr - k * lpr);
-            for (int o = 0; o < nj; ++o) {
-                if (j == o) {
+            const int u = j + k * lpr;
+            if (u < upr) {
+                float* dst = red_w + rbase + u * E;
+                if constexpr (E % 4 == 0) {
 #pragma unroll
-                    for (int e = 0; e < E; ++e) acc = fadd(acc, t[k][e]);
+                    for (int e = 0; e < E; e += 4)
+                        *reinterpret_cast<float4*>(dst + e) = make_float4(t[k][e], t[k][e + 1], t[k][e + 2], t[k][e + 3]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < E; ++e) dst[e] = t[k][e];
                 }
-                acc = __shfl_sync(0xffffffffu, acc, gbase + o);
             }
         }
+        __syncwarp();
         if (row_ok && j == 0) {
+            float acc = 0.0f;
+            const float* rp = red_w + rbase;
+            if ((n_terms & 3) == 0) {
+#pragma unroll 4
+                for (int i = 0; i < n_terms; i += 4) {
+                    const float4 v4 = *reinterpret_cast<const float4*>(rp + i);
+                    acc = fadd(fadd(fadd(fadd(acc, v4.x), v4.y), v4.z), v4.w);
+                }
+            } else {
+                for (int i = 0; i < n_terms; ++i) acc = fadd(acc, rp[i]);
+            }
             float v = acc;
             if (args.softcap > 0.0f) v = fmul(tanh_cr(fmul(v, inv_cap)), args.softcap);
             args.y[row0 + rloc] = v;
@@ -228,6 +268,7 @@ __global__ void gemv_bf16_kernel(const uint8_t* __restrict__ w, size_t rb, const
 
 static bool g_pdl = false;
 void gemv_set_pdl(bool on) { g_pdl = on; }
+bool pdl_enabled() { return g_pdl; }
 
 // Tuning overrides (GNCX_GEMV_WARPS = 8|16, GNCX_GEMV_STAGES = 2..4); read once.
 static int env_int(const char* name, int dflt) {
@@ -283,7 +324,7 @@ static int launch_cw(const GemvArgs& a, int cw, bool aligned, bool preq, size_t 
                    : launch_fmt<T, 4>(a, aligned, preq, smem, grid, st);
 }
 
-int gemv_launch(const uint8_t* w, int32_t type, const float* x, const ActBlock* act, int32_t in_dim,
+int gemv_launch(const uint8_t* w, int32_t type, const float* x, const uint8_t* act, int32_t in_dim,
                 int32_t out_dim, float* y, float softcap, int32_t* err, cudaStream_t st) {
     if (!w || !y || (!x && !act) || in_dim <= 0 || out_dim < 0) return kErrInvalidArg;
     if (out_dim == 0) return kOk;
@@ -297,12 +338,13 @@ int gemv_launch(const uint8_t* w, int32_t type, const float* x, const ActBlock* 
     }
     if (type != kQ4_0 && type != kQ8_0 && type != kQ4_K && type != kQ6_K) return kErrInvalidArg;
     if (in_dim % 256 != 0) return kErrInvalidArg;
-    int ub = 0;
+    if (act && ((uintptr_t)act & 15)) return kErrInvalidArg;  // bulk-copied
+    int ub = 0, terms = 1;
     switch (type) {
-        case kQ4_0: ub = Fmt<kQ4_0>::UB; break;
-        case kQ8_0: ub = Fmt<kQ8_0>::UB; break;
-        case kQ4_K: ub = Fmt<kQ4_K>::UB; break;
-        default: ub = Fmt<kQ6_K>::UB; break;
+        case kQ4_0: ub = Fmt<kQ4_0>::UB; terms = Fmt<kQ4_0>::E; break;
+        case kQ8_0: ub = Fmt<kQ8_0>::UB; terms = Fmt<kQ8_0>::E; break;
+        case kQ4_K: ub = Fmt<kQ4_K>::UB; terms = Fmt<kQ4_K>::E; break;
+        default: ub = Fmt<kQ6_K>::UB; terms = Fmt<kQ6_K>::E; break;
     }
     GemvArgs a{};
     a.w = w;
@@ -320,7 +362,9 @@ int gemv_launch(const uint8_t* w, int32_t type, const float* x, const ActBlock* 
     a.lpr = lpr;
     a.softcap = softcap;
     a.err = err;
-    const size_t budget = (size_t)dev.max_smem_optin;
+    // Leave room beside each CTA for the small kernels that run between GEMVs,
+    // so the next GEMV's CTAs become resident (and prefetch) while they run.
+    const size_t budget = (size_t)dev.max_smem_optin < kGemvSmemCap ? (size_t)dev.max_smem_optin : kGemvSmemCap;
     static const int force_cw = env_int("GNCX_GEMV_WARPS", 0);
     static const int max_stages = env_int("GNCX_GEMV_STAGES", 4);
     // 8 compute warps unless that leaves SMs idle (then 4) or does not fit.
@@ -332,13 +376,14 @@ int gemv_launch(const uint8_t* w, int32_t type, const float* x, const ActBlock* 
         a.rows = cw * 32 / lpr;
         a.stage_bytes = (int)((((size_t)a.rows * a.rb + 15) & ~(size_t)15) + 32);
         stages = max_stages < 2 ? 2 : (max_stages > 4 ? 4 : max_stages);
-        while (stages > 2 && gemv_smem_bytes(in_dim, a.stage_bytes, stages) > budget) --stages;
-        if (gemv_smem_bytes(in_dim, a.stage_bytes, stages) <= budget || cw == 4) break;
+        while (stages > 2 && gemv_smem_bytes(in_dim, a.stage_bytes, stages, gemv_red_bytes(cw, terms)) > budget)
+            --stages;
+        if (gemv_smem_bytes(in_dim, a.stage_bytes, stages, gemv_red_bytes(cw, terms)) <= budget || cw == 4) break;
     }
-    if (gemv_smem_bytes(in_dim, a.stage_bytes, stages) > budget) return kErrCapacity;
+    const size_t smem = gemv_smem_bytes(in_dim, a.stage_bytes, stages, gemv_red_bytes(cw, terms));
+    if (smem > budget) return kErrCapacity;
     a.stages = stages;
     a.n_tiles = (out_dim + a.rows - 1) / a.rows;
-    const size_t smem = gemv_smem_bytes(in_dim, a.stage_bytes, stages);
     const int grid = 0;  // chosen from the occupancy of the instantiation
     const bool aligned = ((uintptr_t)w % 16 == 0) && (a.rb % 16 == 0) && (ub % 16 == 0);
     const bool preq = act != nullptr;

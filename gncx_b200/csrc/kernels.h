@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
+#include "act.cuh"
 #include "common.cuh"
 
 namespace gncx {
@@ -19,17 +20,23 @@ struct DeviceInfo {
 const DeviceInfo& device_info();
 
 // ---- GEMV / prefill ----
-int gemv_launch(const uint8_t* w, int32_t type, const float* x, const ActBlock* act, int32_t in_dim,
+// `act` (16-byte aligned), when given, is a staged activation vector
+// (staged_act_bytes(in_dim) bytes, written by act_stage_launch or a fused
+// producer kernel); otherwise x is re-quantized inside the kernel.
+int gemv_launch(const uint8_t* w, int32_t type, const float* x, const uint8_t* act, int32_t in_dim,
                 int32_t out_dim, float* y, float softcap, int32_t* err, cudaStream_t st);
-// Programmatic dependent launch for the GEMV: its weight stream may start
-// before the preceding kernel on the stream completes (weights must not be
-// written by that kernel).  Off by default.
+// Programmatic dependent launch for the GEMV and the fused decode kernels:
+// a kernel may start (prefetching weights) before the preceding kernel on the
+// stream completes; weights must not be written by that kernel.  Off by default.
 void gemv_set_pdl(bool on);
+bool pdl_enabled();
 // yb[t * ldy + o] (ldy = out_dim when 0)
 int matbatch_launch(const uint8_t* w, int32_t type, const float* xb, const ActBlock* act, int32_t batch,
                     int32_t in_dim, int32_t out_dim, float* yb, int32_t* err, cudaStream_t st, int32_t ldy = 0);
 // x[rows][in_dim] -> ActBlock[rows][in_dim/32]
 int act_quantize_launch(const float* x, int32_t rows, int32_t in_dim, ActBlock* out, cudaStream_t st);
+// ActBlock[in_dim/32] -> staged vector (staged_act_bytes(in_dim) bytes)
+int act_stage_launch(const ActBlock* blocks, int32_t in_dim, uint8_t* staged, cudaStream_t st);
 // Dequantize `rows` rows of `n` weights (row stride = row_bytes(type, n)) to fp32.
 int dequant_launch(const uint8_t* w, int32_t type, int32_t rows, int32_t n, float scale, const int32_t* row_ids,
                    float* out, cudaStream_t st);
@@ -57,7 +64,9 @@ int softcap_launch(float* x, int64_t n, float cap, cudaStream_t st);
 
 // ---- attention ----
 // General form: n_tok queries; query z sits at position (pos_dev ? *pos_dev : pos0) + z
-// and attends to its window; records [z][head][max_splits] of (hd + 2) floats.
+// and attends to its window; records [z][head][max_splits] of attn_record_floats(hd)
+// floats: {max, sum of exp, -, -, o[hd]} (16-byte aligned rows).
+__host__ __device__ inline int attn_record_floats(int hd) { return hd + 4; }
 struct AttnArgs {
     const float* q;        // query z at q + z * q_stride
     int q_stride;
@@ -75,14 +84,17 @@ struct AttnArgs {
     float* part;
     float* out;            // may be null
     int out_stride;
-    ActBlock* act_out;     // may be null: re-quantized output [z][n_heads*hd/32]
+    ActOut act_out;        // optional re-quantized output: blocks [z][n_heads*hd/32], or staged (one query)
     int32_t* err;
     // exact mode: scores go to `scores` [z][head][score_cap] and the softmax sum
     // and the probability-weighted V sum are formed serially in position order,
     // as the reference does (bit-exact up to the host libm's expf rounding).
     int exact;
     float* scores;
-    int score_cap;
+    int score_cap;         // floats per (query, head) score row; a multiple of 4
+    // optional [n_tok][n_kv] arrival counters, zero between launches: the last
+    // CTA of each (query, KV head) merges the split records (no combine kernel)
+    int* counters;
 };
 int attention_run(const AttnArgs& a, int32_t n_tok, cudaStream_t st);
 int attention_geometry_chunk(int32_t len, int32_t n_kv, int sm_count);
@@ -91,10 +103,12 @@ struct AttnScratch {
     int32_t capacity;   // records available
 };
 // exact_scores: null for the split-KV softmax, else n_heads * (window rounded up
-// to 64) floats for the exact serial softmax.
+// to 64) floats for the exact serial softmax.  counters: optional zeroed
+// arrival counters (n_heads * head_dim / 32 of them) that let a single-query
+// launch spread each KV head over several clusters.
 int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t n_heads, int32_t n_kv,
                      int32_t head_dim, float scale, int32_t window, float* out, const AttnScratch& scratch,
-                     int32_t* err, cudaStream_t st, float* exact_scores = nullptr);
+                     int32_t* err, cudaStream_t st, float* exact_scores = nullptr, int* counters = nullptr);
 int32_t attention_scratch_records(int32_t pos, int32_t n_heads, int32_t window);
 
 // ---- sampling ----
@@ -116,14 +130,15 @@ struct DecodeState {
     int32_t pad;
     int32_t ring[kRecentWindow];  // last kRecentWindow tokens (any order)
 };
+// act.staged (rows == 1) or act.blocks [rows][dim/32]
 int add_norm_quant_launch(float* hidden, const float* residual, const float* w, int32_t rows, int32_t dim, float eps,
-                          ActBlock* act, float* normed, cudaStream_t st);
+                          ActOut act, float* normed, cudaStream_t st);
 int qkv_post_launch(float* qkv, int32_t row_stride, int32_t rows, int32_t nh, int32_t nkv, int32_t hd,
                     const float* q_norm, const float* k_norm, bool do_norm, float eps, const float* cos_tab,
                     const float* sin_tab, int32_t pos0, const int32_t* pos_dev, float* kc, float* vc,
                     int64_t kv_pos_stride, int64_t kv_head_stride, cudaStream_t st);
 int glu_quant_launch(const float* g, const float* u, int32_t stride, int32_t ffn, int32_t rows, bool gelu,
-                     ActBlock* act, cudaStream_t st);
+                     ActOut act, cudaStream_t st);
 size_t argmax_state_scratch_bytes();
 int argmax_state_launch(const float* logits, int32_t vocab, DecodeState* st, double penalty, int32_t* out_ids,
                         int advance_pos, void* scratch, cudaStream_t s);

@@ -74,4 +74,33 @@ __device__ __forceinline__ float rms_inv(const float* xs, int n, float eps) {
     return s_inv;
 }
 
+// The same factor from precomputed squares stored lane-major: sq[j * n4 + k]
+// = x[4k+j]^2 (n = 4 * n4, n4 a multiple of 4, sq 16-byte aligned).  Lanes 0-3
+// of warp 0 run the four chains with vector loads well ahead of the adds.
+__device__ __forceinline__ float rms_inv_sq(const float* sq, int n4, float eps) {
+    __shared__ float s_inv;
+    const int tid = threadIdx.x;
+    if (tid < 32) {
+        float acc = 0.0f;
+        if (tid < 4) {
+            const float4* p = reinterpret_cast<const float4*>(sq + (size_t)tid * n4);
+#pragma unroll 8
+            for (int i = 0; i < (n4 >> 2); ++i) {
+                const float4 v = p[i];
+                acc = fadd(fadd(fadd(fadd(acc, v.x), v.y), v.z), v.w);
+            }
+        }
+        const float a1 = __shfl_sync(0xffffffffu, acc, 1);
+        const float a2 = __shfl_sync(0xffffffffu, acc, 2);
+        const float a3 = __shfl_sync(0xffffffffu, acc, 3);
+        if (tid == 0) {
+            const double s = __dadd_rn(__dadd_rn(__dadd_rn((double)acc, (double)a1), (double)a2), (double)a3);
+            const float ms = __double2float_rn(__ddiv_rn(s, (double)(4 * n4)));
+            s_inv = fdiv(1.0f, __fsqrt_rn(fadd(ms, eps)));
+        }
+    }
+    __syncthreads();
+    return s_inv;
+}
+
 }  // namespace gncx

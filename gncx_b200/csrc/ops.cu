@@ -42,6 +42,18 @@ int act_quantize_launch(const float* x, int32_t rows, int32_t in_dim, ActBlock* 
     return launch_status();
 }
 
+__global__ void act_stage_kernel(const ActBlock* __restrict__ blocks, int in_dim, uint8_t* __restrict__ staged) {
+    stage_act_blocks(blocks, in_dim, reinterpret_cast<int8_t*>(staged), reinterpret_cast<float4*>(staged + in_dim),
+                     blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
+}
+
+int act_stage_launch(const ActBlock* blocks, int32_t in_dim, uint8_t* staged, cudaStream_t st) {
+    if (!blocks || !staged || in_dim <= 0 || (in_dim & 255) || ((uintptr_t)staged & 15)) return kErrInvalidArg;
+    const int nb = in_dim >> 5;
+    act_stage_kernel<<<(nb + 127) / 128, 128, 0, st>>>(blocks, in_dim, staged);
+    return launch_status();
+}
+
 // ---------------- dequantization / embedding rows ----------------
 // Element e of a row, following the reference fetch routines (:693-780) with
 // scale factor `scale` applied to the block scale first (scale 1.0 is exact).

@@ -308,6 +308,31 @@ def test_attention_config(gpu, oracle, ctx, window):
     assert np.array_equal(host(kc)[(ctx - 1) * nkv * hd:], kc_ref[(ctx - 1) * nkv * hd:])
 
 
+@pytest.mark.parametrize("nh,nkv,hd", [(4, 2, 64), (8, 1, 128), (16, 8, 64), (32, 8, 128)])
+@pytest.mark.parametrize("exact", [0, 1])
+def test_attention_lengths(gpu, oracle, nh, nkv, hd, exact):
+    """Every context length up to 70 and the chunk edges around 128 / 1024,
+    with and without a sliding window, in both softmax modes."""
+    scale = float(np.float32(1.0 / np.sqrt(hd)))
+    gpu.gncx_set_exact_attention(exact)
+    try:
+        for ctx in list(range(1, 71)) + [127, 128, 129, 1023, 1024, 1025]:
+            kc_np = synth.random_activations(ctx * nkv * hd, seed=ctx)
+            vc_np = synth.random_activations(ctx * nkv * hd, seed=ctx + 7)
+            q = synth.random_activations(nh * hd, seed=ctx + 3)
+            kc, vc = dev(kc_np), dev(vc_np)
+            for window in (0, 17):
+                ref, _, _ = oracle.attention(q, None, None, kc_np, vc_np, ctx - 1, nh, nkv, hd, scale, window, 0)
+                y = out(nh * hd)
+                gpu.gncx_mqa_attention_step_ext(P(dev(q)), None, None, P(kc), P(vc), ctx - 1, nh, nkv, hd, scale,
+                                                window, 0, P(y))
+                core.check(gpu)
+                err = np.max(np.abs(host(y) - ref)) / np.max(np.abs(ref))
+                assert err <= ATTN_TOL, (ctx, window, err)
+    finally:
+        gpu.gncx_set_exact_attention(0)
+
+
 # ---------------------------------------------------------------- sampling
 def test_sample_greedy(gpu, oracle):
     rng = np.random.default_rng(0)
