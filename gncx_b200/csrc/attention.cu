@@ -9,11 +9,9 @@
 // shared memory (16-byte cp.async copies into rows padded by 4 floats, so that
 // eight threads reading eight different rows hit eight different bank groups),
 // serves every query head of the group from it, and writes a partial record
-// (chunk max, sum of exp, unnormalised output).  The records of a (query, KV
-// head) are merged either by the last of its CTAs to finish (a per-(query, KV
-// head) arrival counter; the merge also re-quantizes the output for the next
-// GEMV) or by a separate combine kernel.  In decode each K/V byte crosses HBM
-// once.  The position may live in device memory so a captured CUDA graph
+// (chunk max, sum of exp, unnormalised output).  A combine kernel merges the
+// records of each (query, head) and can re-quantize the result for the next
+// GEMV.  In decode each K/V byte crosses HBM once.  The position may live in device memory so a captured CUDA graph
 // replays every token; CTAs past the window exit at once.
 //
 // Scores are bit-identical to the reference's: its q.k is two 4-lane SSE
@@ -51,19 +49,17 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Floats of the K/V staging area, which the merge reuses for its weights.
-// (also the scratch of the position-group reduction: kAttnThreads * 8 floats)
-__host__ __device__ inline size_t attn_kv_floats(int G, int hd, int chunk, int max_splits) {
+// Floats of the K/V staging area, which the position-group reduction of the
+// PV step reuses as scratch (kAttnThreads * 8 floats).
+__host__ __device__ inline size_t attn_kv_floats(int hd, int chunk) {
     size_t n = (size_t)2 * chunk * (hd + kRowPad);
-    const size_t merge = (size_t)2 * G * max_splits;
-    if (merge > n) n = merge;
     if ((size_t)kAttnThreads * 8 > n) n = (size_t)kAttnThreads * 8;
     return (n + 3) & ~(size_t)3;  // keeps the q rows that follow 16-byte aligned
 }
 
-static size_t attn_smem_bytes(int G, int hd, int chunk, int max_splits) {
+static size_t attn_smem_bytes(int G, int hd, int chunk) {
     const int G4 = (G + 3) & ~3;
-    return attn_kv_floats(G, hd, chunk, max_splits) * 4 + (size_t)G * attn_q_stride(hd) * 4 +
+    return attn_kv_floats(hd, chunk) * 4 + (size_t)G * attn_q_stride(hd) * 4 +
            (size_t)G * (chunk + kScorePad) * 4 + (size_t)chunk * G4 * 4 + (size_t)2 * G * 4;
 }
 
@@ -209,7 +205,6 @@ __device__ __forceinline__ void pv_reduce(const float (&acc)[kPvHeads], int ng, 
 template <bool VEC, bool SCORES_ONLY>
 __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnArgs a) {
     extern __shared__ __align__(16) uint8_t smraw[];
-    __shared__ int s_last;
     const int z = blockIdx.z;
     int t0, len;
     attn_window(a, z, t0, len);
@@ -223,11 +218,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
     const int kvh = blockIdx.y;
     const int cn = min(chunk, len - c0);
     const int rs = hd + kRowPad;
-    const int n_split = (len + chunk - 1) / chunk;
     float* ks = reinterpret_cast<float*>(smraw);                                  // [chunk][rs]
     float* vs = ks + (size_t)chunk * rs;                                           // [chunk][rs]
     const int qrs = attn_q_stride(hd), sld = chunk + kScorePad;
-    float* qs = ks + attn_kv_floats(G, hd, chunk, a.max_splits);                   // [G][qrs]
+    float* qs = ks + attn_kv_floats(hd, chunk);                                    // [G][qrs]
     float* sc = qs + (size_t)G * qrs;                                              // [G][sld]
     float* es = sc + (size_t)G * sld;                                              // [chunk][G4]
     float* red = es + (size_t)chunk * G4;                                          // [G][2]
@@ -317,20 +311,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
             if (dd == 0) { rec[0] = red[2 * (g0 + i)]; rec[1] = red[2 * (g0 + i) + 1]; }
         });
     }
-    if (!a.counters) return;
-
-    // ---- the last CTA of this (query, KV head) to finish merges its records ----
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = atomicAdd(&a.counters[(size_t)z * a.n_kv + kvh], 1) == n_split - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    attn_merge(a, z, kvh * G, G, n_split, ks, ks + (size_t)G * a.max_splits, red);
-    if (tid == 0) a.counters[(size_t)z * a.n_kv + kvh] = 0;  // ready for the next launch
 }
 
-// Merge the split records of one (query, head) when no arrival counters are given.
+// Merge the split records of one (query, head).
 __global__ void attn_combine_kernel(const AttnArgs a) {
     extern __shared__ float wsm[];  // [max_splits] weights, then [max_splits] sums
     __shared__ float s_inv[1];
@@ -504,7 +487,7 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
         return kErrInvalidArg;
     const DeviceInfo& dev = device_info();
     const int G = a.n_heads / a.n_kv;
-    const size_t smem = attn_smem_bytes(G, a.hd, a.chunk, a.max_splits);
+    const size_t smem = attn_smem_bytes(G, a.hd, a.chunk);
     if (smem > (size_t)dev.max_smem_optin) return kErrCapacity;
     const bool vec = ((uintptr_t)a.kc % 16 == 0) && ((uintptr_t)a.vc % 16 == 0) && (a.kv_pos_stride % 4 == 0) &&
                      (a.kv_head_stride % 4 == 0);
@@ -531,7 +514,6 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
     }
     e = vec ? launch_partial<true, false>(a, grid, smem, st) : launch_partial<false, false>(a, grid, smem, st);
     if (e != cudaSuccess) return kErrCuda;
-    if (a.counters) return kOk;  // merged by the last CTA of each (query, KV head)
     const size_t csm = (size_t)a.max_splits * 8;
     if (csm > 48 * 1024 &&
         cudaFuncSetAttribute(attn_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csm) != cudaSuccess)
@@ -548,7 +530,7 @@ int32_t attention_scratch_records(int32_t pos, int32_t n_heads, int32_t window) 
 
 int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t n_heads, int32_t n_kv,
                      int32_t head_dim, float scale, int32_t window, float* out, const AttnScratch& scratch,
-                     int32_t* err, cudaStream_t st, float* exact_scores, int* counters) {
+                     int32_t* err, cudaStream_t st, float* exact_scores) {
     if (!q || !kc || !vc || !out || pos < 0 || n_heads <= 0 || n_kv <= 0 || head_dim <= 0) return kErrInvalidArg;
     const int32_t t0 = window > 0 ? (pos - window + 1 > 0 ? pos - window + 1 : 0) : 0;
     const int32_t len = pos + 1 - t0;
@@ -577,7 +559,6 @@ int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t 
     a.exact = exact_scores != nullptr;
     a.scores = exact_scores;
     a.score_cap = a.max_splits * a.chunk;
-    a.counters = counters;
     return attention_run(a, 1, st);
 }
 

@@ -35,10 +35,8 @@ struct Runtime {
     int32_t* h_err = nullptr;  // pinned
     uint8_t* ws = nullptr;
     size_t ws_bytes = 0;
-    int* attn_counters = nullptr;  // kAttnCounters arrival counters, zero between launches
     std::vector<Mapping> maps;
 };
-static constexpr int kAttnCounters = 8192;
 
 static Runtime g_rt;
 static std::mutex g_maps_mu;
@@ -89,14 +87,12 @@ static int32_t ensure_init() {
         g_rt.device = dev;
         if ((e = cudaStreamCreateWithFlags(&g_rt.own, cudaStreamNonBlocking)) != cudaSuccess ||
             (e = cudaMalloc(&g_rt.d_err, sizeof(int32_t))) != cudaSuccess ||
-            (e = cudaMallocHost(&g_rt.h_err, sizeof(int32_t))) != cudaSuccess ||
-            (e = cudaMalloc(&g_rt.attn_counters, kAttnCounters * sizeof(int))) != cudaSuccess) {
+            (e = cudaMallocHost(&g_rt.h_err, sizeof(int32_t))) != cudaSuccess) {
             set_error(kErrCuda, cuda_msg(e));
             g_rt.device = -1;
             return kErrCuda;
         }
         cudaMemset(g_rt.d_err, 0, sizeof(int32_t));
-        cudaMemset(g_rt.attn_counters, 0, kAttnCounters * sizeof(int));
         g_rt.stream = g_rt.own;
         device_info();
     }
@@ -635,9 +631,8 @@ void gncx_mqa_attention_step_ext(const float* q_vec, const float* k_vec, const f
     if (!ws) return;
     float* part = reinterpret_cast<float*>(ws);
     float* scores = g_exact_attention ? reinterpret_cast<float*>(ws + part_bytes) : nullptr;
-    int* counters = (int64_t)n_heads * hd / 32 <= kAttnCounters ? g_rt.attn_counters : nullptr;
     finish(attention_launch(q, kc, vc, pos, n_heads, n_kv, hd, attn_scale, window, out, AttnScratch{part, recs},
-                            g_rt.d_err, stream(), scores, counters));
+                            g_rt.d_err, stream(), scores));
 }
 
 void gncx_mqa_attention_step(const float* q_vec, const float* k_vec, const float* v_vec, float* k_cache,

@@ -184,7 +184,6 @@ struct Engine {
     int max_splits = 0;
     bool exact = false;      // exact serial softmax in attention
     float* scores = nullptr; // [n_heads][max_splits * chunk] (decode, exact mode)
-    int* attn_counters = nullptr;  // [kPrefillGroup][n_kv], zero between attention launches
     int graph_exact = -1;
     DecodeState* st = nullptr;
     DecodeState* st_host = nullptr;  // pinned staging
@@ -268,7 +267,6 @@ static int decode_step(Engine* e, bool sample, double penalty) {
         a.part = e->part;
         a.out = e->exact ? e->qkv : nullptr;  // exact mode: the output replaces q
         a.out_stride = qkv_w;
-        a.counters = nullptr;  // one query: a separate merge kernel is faster than the last-CTA merge
         a.act_out = ActOut{nullptr, e->act_q};
         a.err = e->d_err;
         a.exact = e->exact ? 1 : 0;
@@ -362,7 +360,6 @@ static int prefill_batch(Engine* e, int B) {
             a.part = e->pf_part;
             a.out = e->exact ? e->pf_qkv + (size_t)z0 * qkv_w : nullptr;
             a.out_stride = qkv_w;
-            a.counters = e->attn_counters;
             a.act_out = ActOut{e->pf_actq + (size_t)z0 * (QD / 32), nullptr};
             a.err = e->d_err;
             a.exact = e->exact ? 1 : 0;
@@ -580,8 +577,6 @@ static int engine_load(Engine* e, const char* path, int max_seq, std::string& er
     CU(cudaMalloc(&e->act_f, staged_act_bytes(F)));
     CU(cudaMalloc(&e->part, (size_t)e->nh * e->max_splits * attn_record_floats(e->hd) * 4));
     CU(cudaMalloc(&e->scores, (size_t)e->nh * e->max_splits * kDecodeChunk * 4));
-    CU(cudaMalloc(&e->attn_counters, (size_t)kPrefillGroup * e->nkv * sizeof(int)));
-    CU(cudaMemset(e->attn_counters, 0, (size_t)kPrefillGroup * e->nkv * sizeof(int)));
     CU(cudaMalloc(&e->st, sizeof(DecodeState)));
     CU(cudaMallocHost(&e->st_host, sizeof(DecodeState)));
     CU(cudaMalloc(&e->am_scratch, argmax_state_scratch_bytes()));
@@ -598,7 +593,7 @@ static void engine_free(Engine* e) {
     if (!e) return;
     if (e->stream) cudaStreamSynchronize(e->stream);
     if (e->graph) cudaGraphExecDestroy(e->graph);
-    void* bufs[] = {e->scores, e->attn_counters, e->pf_scores, e->arena, e->kv, e->rope_c, e->rope_s, e->hidden, e->normed, e->proj, e->qkv, e->gu, e->logits,
+    void* bufs[] = {e->scores, e->pf_scores, e->arena, e->kv, e->rope_c, e->rope_s, e->hidden, e->normed, e->proj, e->qkv, e->gu, e->logits,
                     e->act_d, e->act_q, e->act_f, e->part, e->st, e->am_scratch, e->d_err, e->out_ids, e->ids_dev,
                     e->pf_h, e->pf_p, e->pf_qkv, e->pf_gu, e->pf_part, e->pf_act, e->pf_actq, e->pf_actf};
     for (void* b : bufs)

@@ -92,9 +92,6 @@ struct AttnArgs {
     int exact;
     float* scores;
     int score_cap;         // floats per (query, head) score row; a multiple of 4
-    // optional [n_tok][n_kv] arrival counters, zero between launches: the last
-    // CTA of each (query, KV head) merges the split records (no combine kernel)
-    int* counters;
 };
 int attention_run(const AttnArgs& a, int32_t n_tok, cudaStream_t st);
 int attention_geometry_chunk(int32_t len, int32_t n_kv, int sm_count);
@@ -103,12 +100,10 @@ struct AttnScratch {
     int32_t capacity;   // records available
 };
 // exact_scores: null for the split-KV softmax, else n_heads * (window rounded up
-// to 64) floats for the exact serial softmax.  counters: optional zeroed
-// arrival counters (n_heads * head_dim / 32 of them) that let a single-query
-// launch spread each KV head over several clusters.
+// to 64) floats for the exact serial softmax.
 int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t n_heads, int32_t n_kv,
                      int32_t head_dim, float scale, int32_t window, float* out, const AttnScratch& scratch,
-                     int32_t* err, cudaStream_t st, float* exact_scores = nullptr, int* counters = nullptr);
+                     int32_t* err, cudaStream_t st, float* exact_scores = nullptr);
 int32_t attention_scratch_records(int32_t pos, int32_t n_heads, int32_t window);
 
 // ---- sampling ----
