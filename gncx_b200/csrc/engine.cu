@@ -28,6 +28,7 @@
 #include <vector>
 
 #include "kernels.h"
+#include <nvtx3/nvToolsExt.h>
 
 namespace gncx {
 
@@ -730,15 +731,23 @@ int32_t gncx_engine_generate(void* h, const int32_t* prompt, int32_t n_prompt, i
     if (n_prompt >= e->max_seq) return 0;
     if (max_new > e->max_seq - n_prompt) max_new = e->max_seq - n_prompt;
     if (max_new == 0) return 0;
+    nvtxRangePushA("gncx_prefill");
     int st = gncx_engine_prefill(h, prompt, n_prompt, nullptr);
+    nvtxRangePop();
     if (st != kOk) return -st;
     if ((st = set_state(e, 0, n_prompt, prompt, n_prompt, eos, max_new)) != kOk) return -st;
     if ((st = argmax_state_launch(e->logits, e->vocab, e->st, penalty, e->out_ids, 0, e->am_scratch, e->stream)) != kOk)
         return -st;
     if ((st = build_graph(e, penalty)) != kOk) return -st;
     if (cudaEventRecord(e->ev[2], e->stream) != cudaSuccess) return -kErrCuda;
-    for (int i = 1; i < max_new; ++i)
-        if (cudaGraphLaunch(e->graph, e->stream) != cudaSuccess) return -kErrCuda;
+    nvtxRangePushA("gncx_decode");  // profiler ranges (no cost without a tool attached)
+    for (int i = 1; i < max_new; ++i) {
+        if (cudaGraphLaunch(e->graph, e->stream) != cudaSuccess) {
+            nvtxRangePop();
+            return -kErrCuda;
+        }
+    }
+    nvtxRangePop();
     if (cudaEventRecord(e->ev[3], e->stream) != cudaSuccess) return -kErrCuda;
     DecodeState& hs = *e->st_host;
     if (cudaMemcpyAsync(&hs, e->st, sizeof(DecodeState), cudaMemcpyDeviceToHost, e->stream) != cudaSuccess)

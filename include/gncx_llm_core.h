@@ -181,6 +181,37 @@ int32_t gncx_dequantize_rows(const uint8_t* base, size_t offset, int32_t ggml_ty
 int32_t gncx_sample_greedy(const float* logits, int32_t vocab, const int32_t* recent, int32_t n_recent,
                            double repeat_penalty);
 
+/* ------------------------------------------------------------------------ */
+/* Model engine: the reference orchestrator's decode loop on the GPU         */
+/* ------------------------------------------------------------------------ */
+/* A restatement of GNCXStreamer (lua/gncx_streamer.lua) for callers without
+ * LuaJIT: the GGUF's quantized blocks are uploaded in their native layout,
+ * forward_token (:759-965) runs as fused kernels, and every greedy decode
+ * step of generate (:1276-1311) is one CUDA graph launch driven by state in
+ * device memory.  Token ids in, token ids / logits out (no tokenizer).
+ * Statuses are GNCX_* codes; gncx_engine_error() describes the last one. */
+void* gncx_engine_create(const char* gguf_path, int32_t max_seq_len); /* NULL on failure (reason on stderr) */
+void gncx_engine_destroy(void* engine);
+/* out[12] = n_layers, dim, n_heads, n_kv_heads, head_dim, ffn_dim, vocab, max_seq, eos, arch, embd_type, qk_norm */
+int32_t gncx_engine_hparams(void* engine, int32_t* out);
+/* 1: exact serial softmax in attention (the reference's order); 0 (default): split-KV softmax */
+int32_t gncx_engine_set_exact(void* engine, int32_t on);
+const char* gncx_engine_error(void* engine);
+void* gncx_engine_stream(void* engine);                 /* the engine's CUDA stream */
+/* Logits of token `id` at position `pos` (KV cache entries below pos must be filled);
+ * logits_out: host array of vocab floats, or NULL. */
+int32_t gncx_engine_forward_token(void* engine, int32_t id, int32_t pos, float* logits_out);
+/* Runs the prompt from position 0 (batched prefill); logits of the last position. */
+int32_t gncx_engine_prefill(void* engine, const int32_t* ids, int32_t n, float* logits_out);
+const float* gncx_engine_logits(void* engine);          /* device logits of the last forward / prefill */
+/* Prefill, then penalized greedy decode of up to max_new tokens (stops at eos);
+ * writes the generated ids to out_ids (host) and returns their count, or -status. */
+int32_t gncx_engine_generate(void* engine, const int32_t* prompt, int32_t n_prompt, int32_t max_new,
+                             double repeat_penalty, int32_t eos, int32_t* out_ids);
+/* Device time (ms) of the last prefill and decode loop, and the decode step count. */
+int32_t gncx_engine_timing(void* engine, double* prefill_ms, double* decode_ms, int32_t* decode_steps);
+
+
 #ifdef __cplusplus
 }
 #endif
