@@ -105,6 +105,8 @@ _SIGS = {
     "gncx_matvec_preq": (c_int32, [P, c_size_t, c_int32, P, c_int32, c_int32, P]),
     "gncx_dequantize_rows": (c_int32, [P, c_size_t, c_int32, c_int32, c_int32, P]),
     "gncx_sample_greedy": (c_int32, [P, c_int32, POINTER(c_int32), c_int32, c_double]),
+    "gncx_mqa_attention_step_noalloc": (c_int32, [P, P, P, P, P, c_int32, c_int32, c_int32, c_int32, c_float,
+                                                  c_int32, c_int32, P, P]),
     # model engine
     "gncx_engine_create": (c_void_p, [c_char_p, c_int32]),
     "gncx_engine_destroy": (None, [c_void_p]),

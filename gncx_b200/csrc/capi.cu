@@ -51,6 +51,9 @@ static void set_error(int32_t code, const char* what) {
 
 static const char* cuda_msg(cudaError_t e) { return cudaGetErrorString(e); }
 
+// Status of an entry point defined in another file of the library.
+void record_api_error(int32_t code, const char* message) { set_error(code, message); }
+
 static DeviceInfo g_info[64];
 
 const DeviceInfo& device_info() {

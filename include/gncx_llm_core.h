@@ -181,6 +181,24 @@ int32_t gncx_dequantize_rows(const uint8_t* base, size_t offset, int32_t ggml_ty
 int32_t gncx_sample_greedy(const float* logits, int32_t vocab, const int32_t* recent, int32_t n_recent,
                            double repeat_penalty);
 
+/* Decode attention that allocates nothing (no counterpart in the reference).
+ * Same arguments and result as gncx_mqa_attention_step_ext with the split-KV
+ * softmax, plus the CUDA stream to run on (NULL = legacy default stream);
+ * pointers must be device-accessible (no mapped-file translation), and the
+ * call is stream-ordered (it does not wait).  Its scratch is a fixed 4 MiB
+ * array per device, held until exit: n_heads * ceil(window / chunk) *
+ * (head_dim + 4) * 4 bytes must fit (chunk = 16..64 positions; e.g. 32 heads
+ * of 128 fit a window of ~15,800 positions), else GNCX_ERR_CAPACITY with a
+ * message in gncx_last_error_message().  The first call on a device does a
+ * one-time set-up (looks up the array's address) and should come before any
+ * stream capture.  All calls on a device share the array, so calls whose GPU
+ * work overlaps race and must be serialised by the caller.  Returns a status. */
+int32_t gncx_mqa_attention_step_noalloc(const float* q_vec, const float* k_vec, const float* v_vec,
+                                        float* k_cache_layer, float* v_cache_layer, int32_t pos, int32_t n_heads,
+                                        int32_t n_kv_heads, int32_t head_dim, float attn_scale,
+                                        int32_t sliding_window, int32_t write_kv, float* out_attn_vec,
+                                        void* cuda_stream);
+
 /* ------------------------------------------------------------------------ */
 /* Model engine: the reference orchestrator's decode loop on the GPU         */
 /* ------------------------------------------------------------------------ */
