@@ -31,6 +31,7 @@
 #include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace gncx {
 
@@ -71,6 +72,14 @@ __device__ __forceinline__ void attn_window(const AttnArgs& a, int z, int& t0, i
 
 constexpr int kMergeBatch = 32;  // split records loaded per round trip in a merge
 
+// L2 load that the compiler keeps after every preceding memory barrier (a
+// dependency wait, a fence): __ldcg is a pure asm the compiler may hoist.
+__device__ __forceinline__ float ld_l2(const float* p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Merge the n split records of heads h0 .. h0+G-1 of query z:
 // out = (sum_s o_s * e^(m_s-M)) / (sum_s l_s * e^(m_s-M) + 1e-12), serial in s.
 // `wsm` / `lsm` hold G*n floats each, `s_inv` G floats; called by whole CTAs.
@@ -81,8 +90,8 @@ __device__ void attn_merge(const AttnArgs& a, int z, int h0, int G, int n, float
     for (int i = tid; i < G * n; i += nthr) {
         const int g = i / n, s = i - g * n;
         const float* rec = a.part + (((size_t)z * a.n_heads + h0 + g) * a.max_splits + s) * R;
-        wsm[i] = __ldcg(rec);
-        lsm[i] = __ldcg(rec + 1);
+        wsm[i] = ld_l2(rec);
+        lsm[i] = ld_l2(rec + 1);
     }
     __syncthreads();
     for (int g = warp; g < G; g += nthr >> 5) {
@@ -107,7 +116,7 @@ __device__ void attn_merge(const AttnArgs& a, int z, int h0, int G, int n, float
         for (int s0 = 0; s0 < n; s0 += kMergeBatch) {
             float v[kMergeBatch];  // a batch of records in flight at once
 #pragma unroll
-            for (int b = 0; b < kMergeBatch; ++b) v[b] = s0 + b < n ? __ldcg(rec + (size_t)(s0 + b) * R) : 0.0f;
+            for (int b = 0; b < kMergeBatch; ++b) v[b] = s0 + b < n ? ld_l2(rec + (size_t)(s0 + b) * R) : 0.0f;
 #pragma unroll
             for (int b = 0; b < kMergeBatch; ++b)
                 if (s0 + b < n) o = fadd(o, fmul(v[b], w[s0 + b]));
@@ -189,6 +198,7 @@ __device__ __forceinline__ void pv_reduce(const float (&acc)[kPvHeads], int ng, 
             for (int i = 0; i < ng; ++i) out(i, d, acc[i]);
         return;
     }
+    __syncthreads();  // scr may overlap the V rows other threads are still reading
     if (active)
         for (int i = 0; i < ng; ++i) scr[((size_t)pg * kPvHeads + i) * hd + d] = acc[i];
     __syncthreads();
@@ -230,34 +240,36 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
     const size_t row0 = (size_t)(t0 + c0) * a.kv_pos_stride + (size_t)kvh * a.kv_head_stride;
     const size_t ps = (size_t)a.kv_pos_stride;
 
-    // ---- stage K (copy group 0) and V (group 1) ----
-    if (VEC) {
-        // thread -> one 16-byte piece c of rows p0, p0 + step, ...
-        const int cpr = hd >> 2, step = kAttnThreads / cpr;
-        const int c = tid % cpr, p0 = tid / cpr;
-        const bool on = tid < step * cpr;
-        if (on)
-            for (int p = p0; p < cn; p += step) cp_async16(ks + (size_t)p * rs + 4 * c, a.kc + row0 + p * ps + 4 * c);
-        cp_async_commit();
-        if (!SCORES_ONLY) {
-            if (on)
-                for (int p = p0; p < cn; p += step)
-                    cp_async16(vs + (size_t)p * rs + 4 * c, a.vc + row0 + p * ps + 4 * c);
+    pdl_launch_dependents();
+    // ---- stage K and V: rows written before the preceding kernel first (they
+    // may stream in while it finishes), the rest after the dependency wait ----
+    const int n_old = a.prefetch_old ? max(0, min(cn, (t0 + len - 1) - (t0 + c0))) : 0;
+    auto stage_rows = [&](int pa, int pb) {
+        if (VEC) {
+            // thread -> one 16-byte piece c of rows pa + p0, pa + p0 + step, ...
+            const int cpr = hd >> 2, step = kAttnThreads / cpr;
+            const int c = tid % cpr, p0 = tid / cpr;
+            if (tid < step * cpr) {
+                for (int p = pa + p0; p < pb; p += step) {
+                    cp_async16(ks + (size_t)p * rs + 4 * c, a.kc + row0 + p * ps + 4 * c);
+                    if (!SCORES_ONLY) cp_async16(vs + (size_t)p * rs + 4 * c, a.vc + row0 + p * ps + 4 * c);
+                }
+            }
             cp_async_commit();
+        } else {
+            for (int i = tid; i < (pb - pa) * hd; i += kAttnThreads) {
+                const int p = pa + i / hd, d = i % hd;
+                ks[(size_t)p * rs + d] = a.kc[row0 + p * ps + d];
+                if (!SCORES_ONLY) vs[(size_t)p * rs + d] = a.vc[row0 + p * ps + d];
+            }
         }
-    } else {
-        for (int i = tid; i < cn * hd; i += kAttnThreads) {
-            const int p = i / hd, d = i - p * hd;
-            ks[(size_t)p * rs + d] = a.kc[row0 + p * ps + d];
-            if (!SCORES_ONLY) vs[(size_t)p * rs + d] = a.vc[row0 + p * ps + d];
-        }
-    }
+    };
+    if (n_old > 0) stage_rows(0, n_old);
+    pdl_wait();
+    if (n_old < cn) stage_rows(n_old, cn);
     const float* qz = a.q + (size_t)z * a.q_stride + (size_t)kvh * G * hd;
     for (int i = tid; i < G * hd; i += kAttnThreads) qs[(size_t)(i / hd) * qrs + i % hd] = qz[i];
-    if (VEC) {
-        if (SCORES_ONLY) cp_async_wait<0>();
-        else cp_async_wait<1>();
-    }
+    if (VEC) cp_async_wait<0>();
     __syncthreads();
 
     // ---- scores (the reference's eight chains per dot) ----
@@ -290,7 +302,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
         if (lane == 0) { red[2 * g] = mx; red[2 * g + 1] = sum; }
     }
     for (int i = tid; i < cn * (G4 - G); i += kAttnThreads) es[(size_t)(i / (G4 - G)) * G4 + G + i % (G4 - G)] = 0.0f;
-    if (VEC) cp_async_wait<0>();
     __syncthreads();
 
     // ---- o[g][d] = sum_p e[p][g] * v[p][d] ----
@@ -317,6 +328,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
 __global__ void attn_combine_kernel(const AttnArgs a) {
     extern __shared__ float wsm[];  // [max_splits] weights, then [max_splits] sums
     __shared__ float s_inv[1];
+    pdl_launch_dependents();
+    pdl_wait();
     const int h = blockIdx.x, z = blockIdx.y;
     int t0, len;
     attn_window(a, z, t0, len);
@@ -331,6 +344,8 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
 // scores are replaced by p_t = e_t * inv.  One CTA per (head, query).
 constexpr int kExactThreads = 256;
 __global__ void __launch_bounds__(kExactThreads) attn_exact_softmax_kernel(const AttnArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int h = blockIdx.x, z = blockIdx.y;
     int t0, len;
     attn_window(a, z, t0, len);
@@ -374,6 +389,8 @@ constexpr int kExactTile = 64;
 constexpr int kExactHeads = kExactThreads / kExactSlice;  // 8
 template <bool VEC>
 __global__ void __launch_bounds__(kExactThreads) attn_exact_pv_kernel(const AttnArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ __align__(16) float vt[2][kExactTile][kExactSlice];
     __shared__ __align__(16) float pt[2][kExactHeads][kExactTile];
     const int slices = (a.hd + kExactSlice - 1) / kExactSlice;
@@ -447,6 +464,8 @@ __global__ void __launch_bounds__(kExactThreads) attn_exact_pv_kernel(const Attn
 
 // Re-quantize exact-mode outputs for the next GEMV (one warp per 32 outputs).
 __global__ void attn_exact_quant_kernel(const AttnArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int z = blockIdx.y;
     const int dim = a.n_heads * a.hd;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -471,8 +490,7 @@ static cudaError_t launch_partial(const AttnArgs& a, dim3 grid, size_t smem, cud
         if (e != cudaSuccess) return e;
         set_bytes = smem;
     }
-    attn_partial_kernel<VEC, SCORES_ONLY><<<grid, kAttnThreads, smem, st>>>(a);
-    return cudaPeekAtLastError();
+    return launch_k(attn_partial_kernel<VEC, SCORES_ONLY>, grid, dim3(kAttnThreads), smem, st, a);
 }
 
 int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
@@ -498,19 +516,21 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
         if (!a.out) return kErrInvalidArg;
         e = vec ? launch_partial<true, true>(a, grid, smem, st) : launch_partial<false, true>(a, grid, smem, st);
         if (e != cudaSuccess) return kErrCuda;
-        attn_exact_softmax_kernel<<<dim3(a.n_heads, n_tok), kExactThreads, 0, st>>>(a);
+        if (launch_k(attn_exact_softmax_kernel, dim3(a.n_heads, n_tok), dim3(kExactThreads), 0, st, a) != cudaSuccess)
+            return kErrCuda;
         const int slices = (a.hd + kExactSlice - 1) / kExactSlice;
         const int hgroups = (G + kExactHeads - 1) / kExactHeads;
         const dim3 pv_grid(a.n_kv * hgroups * slices, n_tok);
-        if (vec && ((uintptr_t)a.scores & 15) == 0)
-            attn_exact_pv_kernel<true><<<pv_grid, kExactThreads, 0, st>>>(a);
-        else
-            attn_exact_pv_kernel<false><<<pv_grid, kExactThreads, 0, st>>>(a);
+        e = (vec && ((uintptr_t)a.scores & 15) == 0)
+                ? launch_k(attn_exact_pv_kernel<true>, pv_grid, dim3(kExactThreads), 0, st, a)
+                : launch_k(attn_exact_pv_kernel<false>, pv_grid, dim3(kExactThreads), 0, st, a);
+        if (e != cudaSuccess) return kErrCuda;
         if (act) {
             const int dim = a.n_heads * a.hd;
-            attn_exact_quant_kernel<<<dim3((dim + 255) / 256, n_tok), 256, 0, st>>>(a);
+            if (launch_k(attn_exact_quant_kernel, dim3((dim + 255) / 256, n_tok), dim3(256), 0, st, a) != cudaSuccess)
+                return kErrCuda;
         }
-        return cudaPeekAtLastError() == cudaSuccess ? kOk : kErrCuda;
+        return kOk;
     }
     e = vec ? launch_partial<true, false>(a, grid, smem, st) : launch_partial<false, false>(a, grid, smem, st);
     if (e != cudaSuccess) return kErrCuda;
@@ -518,8 +538,8 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
     if (csm > 48 * 1024 &&
         cudaFuncSetAttribute(attn_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csm) != cudaSuccess)
         return kErrCuda;
-    attn_combine_kernel<<<dim3(a.n_heads, n_tok), 128, csm, st>>>(a);
-    return cudaPeekAtLastError() == cudaSuccess ? kOk : kErrCuda;
+    return launch_k(attn_combine_kernel, dim3(a.n_heads, n_tok), dim3(128), csm, st, a) == cudaSuccess ? kOk
+                                                                                                    : kErrCuda;
 }
 
 int32_t attention_scratch_records(int32_t pos, int32_t n_heads, int32_t window) {
@@ -559,6 +579,7 @@ int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t 
     a.exact = exact_scores != nullptr;
     a.scores = exact_scores;
     a.score_cap = a.max_splits * a.chunk;
+    a.prefetch_old = 0;  // a caller's kernel just before may have written any row
     return attention_run(a, 1, st);
 }
 

@@ -268,6 +268,7 @@ static int decode_step(Engine* e, bool sample, double penalty) {
         a.part = e->part;
         a.out = e->exact ? e->qkv : nullptr;  // exact mode: the output replaces q
         a.out_stride = qkv_w;
+        a.prefetch_old = 1;  // cache rows below pos come from earlier tokens
         a.act_out = ActOut{nullptr, e->act_q};
         a.err = e->d_err;
         a.exact = e->exact ? 1 : 0;

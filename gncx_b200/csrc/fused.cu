@@ -182,6 +182,8 @@ __global__ void qkv_post_kernel(float* qkv, int row_stride, int nh, int nkv, int
                                 const float* __restrict__ stab, int pos0, const int* pos_dev, float* kc, float* vc,
                                 int64_t kps, int64_t khs) {
     extern __shared__ float xs[];
+    pdl_launch_dependents();
+    pdl_wait();
     const int x = blockIdx.x, r = blockIdx.y;
     const int pos = (pos_dev ? *pos_dev : pos0) + r;
     float* row = qkv + (size_t)r * row_stride;
@@ -222,10 +224,11 @@ int qkv_post_launch(float* qkv, int32_t row_stride, int32_t rows, int32_t nh, in
                     int64_t kv_pos_stride, int64_t kv_head_stride, cudaStream_t st) {
     if (!qkv || !cos_tab || !sin_tab || !kc || !vc || rows <= 0 || hd <= 0 || (hd & 1)) return kErrInvalidArg;
     const int threads = hd >= 256 ? 256 : (hd >= 128 ? 128 : 64);
-    qkv_post_kernel<<<dim3(nh + 2 * nkv, rows), threads, (size_t)hd * 4, st>>>(
-        qkv, row_stride, nh, nkv, hd, q_norm, k_norm, do_norm ? 1 : 0, eps, cos_tab, sin_tab, pos0, pos_dev, kc, vc,
-        kv_pos_stride, kv_head_stride);
-    return status();
+    return launch_k(qkv_post_kernel, dim3(nh + 2 * nkv, rows), dim3(threads), (size_t)hd * 4, st, qkv, row_stride,
+                    nh, nkv, hd, q_norm, k_norm, do_norm ? 1 : 0, eps, cos_tab, sin_tab, pos0, pos_dev, kc, vc,
+                    kv_pos_stride, kv_head_stride) == cudaSuccess
+               ? kOk
+               : kErrCuda;
 }
 
 // ---------------------------------------------------------------- GLU + quantize

@@ -92,6 +92,10 @@ struct AttnArgs {
     int exact;
     float* scores;
     int score_cap;         // floats per (query, head) score row; a multiple of 4
+    // 1: K/V rows below the query's own position were written before the
+    // preceding kernel ran (single-query decode), so a CTA may load them before
+    // its dependency wait under programmatic dependent launch.  0: load nothing early.
+    int prefetch_old;
 };
 int attention_run(const AttnArgs& a, int32_t n_tok, cudaStream_t st);
 int attention_geometry_chunk(int32_t len, int32_t n_kv, int sm_count);
