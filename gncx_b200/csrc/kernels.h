@@ -33,6 +33,10 @@ bool pdl_enabled();
 // yb[t * ldy + o] (ldy = out_dim when 0)
 int matbatch_launch(const uint8_t* w, int32_t type, const float* xb, const ActBlock* act, int32_t batch,
                     int32_t in_dim, int32_t out_dim, float* yb, int32_t* err, cudaStream_t st, int32_t ldy = 0);
+// The same on the tensor cores (tcgen05 kind::i8) for Q4_0 / Q8_0 / Q4_K;
+// kErrInvalidArg when the format, shape or alignment has no such path.
+int matbatch_tc_launch(const uint8_t* w, int32_t type, const ActBlock* act, int32_t batch, int32_t in_dim,
+                       int32_t out_dim, float* yb, int32_t* err, cudaStream_t st, int32_t ldy);
 // x[rows][in_dim] -> ActBlock[rows][in_dim/32]
 int act_quantize_launch(const float* x, int32_t rows, int32_t in_dim, ActBlock* out, cudaStream_t st);
 // ActBlock[in_dim/32] -> staged vector (staged_act_bytes(in_dim) bytes)

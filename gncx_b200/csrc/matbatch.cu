@@ -9,6 +9,7 @@
 // 256-input unit of weights and activations per step in shared memory; each
 // weight unit is unpacked once into registers and reused for four tokens.
 #include <cuda_runtime.h>
+#include <stdlib.h>
 #include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
@@ -137,6 +138,15 @@ int matbatch_launch(const uint8_t* w, int32_t type, const float* xb, const ActBl
         return cudaPeekAtLastError() == cudaSuccess ? kOk : kErrCuda;
     }
     if (!act || in_dim % 256) return kErrInvalidArg;
+    // Q4_0 / Q8_0 / Q4_K on the tensor cores (matbatch_tc.cu) unless disabled
+    static const bool use_tc = [] {
+        const char* v = getenv("GNCX_MATBATCH_TC");
+        return !(v && v[0] == '0');
+    }();
+    if (use_tc) {
+        const int r = matbatch_tc_launch(w, type, act, batch, in_dim, out_dim, yb, err, st, ldy);
+        if (r != kErrInvalidArg) return r;
+    }
     const size_t rb = row_bytes(type, in_dim);
     dim3 grid((out_dim + kMbRows - 1) / kMbRows, (batch + kMbToks - 1) / kMbToks);
     if (grid.y > 65535) return kErrCapacity;
