@@ -337,6 +337,163 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
     attn_merge(a, z, h, 1, n, wsm, wsm + a.max_splits, s_inv);
 }
 
+// ---- causal prefill: one CTA per (chunk, KV head, tile of queries) ----
+// Many queries share each K/V chunk, so a CTA stages the chunk once and
+// serves a tile of 64 (query, head) rows of the KV head's group: scores as a
+// 64 x 64 register-blocked product (4 x 4 per thread), a per-row softmax over
+// the positions each query may see (position <= its own), and the PV product,
+// written as the same split records the combine kernel merges.  Split-KV
+// softmax mode only; window 0; chunk of 64 positions.
+constexpr int kPfRows = 64;  // (query, head) rows per CTA
+constexpr int kPfChunk = 64;
+
+static size_t attn_prefill_smem_bytes(int hd) {
+    const int rs = hd + kRowPad;
+    return ((size_t)3 * kPfRows * rs + (size_t)2 * kPfRows * (kPfChunk + 4) + 2 * kPfRows) * 4;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads, 1) attn_prefill_kernel(const AttnArgs a) {
+    extern __shared__ __align__(16) float psm[];
+    constexpr int RS = HD + kRowPad;
+    constexpr int SL = kPfChunk + 4;
+    const int G = a.n_heads / a.n_kv;
+    const int QT = kPfRows / G;  // queries per tile
+    const int split = blockIdx.x, kvh = blockIdx.y;
+    const int z0 = blockIdx.z * QT;
+    const int c0 = split * kPfChunk;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int pos_first = (a.pos_dev ? *a.pos_dev : a.pos0) + z0;  // query z sits at position pos0 + z
+    // the tile's last valid query sees the most positions (score_cap carries n_tok here)
+    const int z_last = min(z0 + QT, a.score_cap) - 1;
+    const int pos_last = pos_first + (z_last - z0);
+    if (c0 > pos_last) return;  // uniform: no query of the tile sees this chunk
+    const int cn = min(kPfChunk, pos_last + 1 - c0);
+    float* ks = psm;                                  // [64][RS]
+    float* vs = ks + kPfRows * RS;                    // [64][RS]
+    float* qs = vs + kPfRows * RS;                    // [64 rows][RS]
+    float* sc = qs + kPfRows * RS;                    // [64 rows][SL]
+    float* es = sc + kPfRows * SL;                    // [64 positions][SL] (row index fastest)
+    float* red = es + kPfRows * SL;                   // [64 rows][2]
+    const size_t ps = (size_t)a.kv_pos_stride;
+    const size_t row0 = (size_t)c0 * ps + (size_t)kvh * a.kv_head_stride;
+    // ---- stage K/V rows [c0, c0+cn) and the tile's q rows ----
+    {
+        constexpr int CPR = HD / 4, STEP = kAttnThreads / CPR;
+        const int c = tid % CPR, p0 = tid / CPR;
+        for (int p = p0; p < cn; p += STEP) {
+            cp_async16(ks + p * RS + 4 * c, a.kc + row0 + p * ps + 4 * c);
+            cp_async16(vs + p * RS + 4 * c, a.vc + row0 + p * ps + 4 * c);
+        }
+        cp_async_commit();
+        for (int i = tid; i < kPfRows * (HD / 4); i += kAttnThreads) {
+            const int qr = i / (HD / 4), cc = i % (HD / 4);
+            const int zl = qr / G, g = qr % G;
+            const int z = z0 + zl;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (z <= z_last)
+                v = *reinterpret_cast<const float4*>(a.q + (size_t)z * a.q_stride + (size_t)(kvh * G + g) * HD + 4 * cc);
+            *reinterpret_cast<float4*>(qs + qr * RS + 4 * cc) = v;
+        }
+        cp_async_wait<0>();
+        __syncthreads();
+    }
+    // ---- scores: thread (i, j) owns rows 4i..4i+3 x positions 4j..4j+3 ----
+    {
+        const int i = tid >> 4, j = tid & 15;
+        float acc[4][4];
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+#pragma unroll
+            for (int y = 0; y < 4; ++y) acc[x][y] = 0.0f;
+#pragma unroll 2
+        for (int m = 0; m < HD / 8; ++m) {
+            float4 q0[4], q1[4], k0[4], k1[4];
+#pragma unroll
+            for (int x = 0; x < 4; ++x) {
+                q0[x] = *reinterpret_cast<const float4*>(qs + (4 * i + x) * RS + 8 * m);
+                q1[x] = *reinterpret_cast<const float4*>(qs + (4 * i + x) * RS + 8 * m + 4);
+                k0[x] = *reinterpret_cast<const float4*>(ks + (4 * j + x) * RS + 8 * m);
+                k1[x] = *reinterpret_cast<const float4*>(ks + (4 * j + x) * RS + 8 * m + 4);
+            }
+#pragma unroll
+            for (int x = 0; x < 4; ++x)
+#pragma unroll
+                for (int y = 0; y < 4; ++y) {
+                    float t = acc[x][y];
+                    t = fmaf(q0[x].x, k0[y].x, t); t = fmaf(q0[x].y, k0[y].y, t);
+                    t = fmaf(q0[x].z, k0[y].z, t); t = fmaf(q0[x].w, k0[y].w, t);
+                    t = fmaf(q1[x].x, k1[y].x, t); t = fmaf(q1[x].y, k1[y].y, t);
+                    t = fmaf(q1[x].z, k1[y].z, t); t = fmaf(q1[x].w, k1[y].w, t);
+                    acc[x][y] = t;
+                }
+        }
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+            const int qr = 4 * i + x;
+            const int pos_q = pos_first + qr / G;
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+                const int p = 4 * j + y;
+                sc[qr * SL + p] = (p < cn && c0 + p <= pos_q) ? acc[x][y] * a.scale : -INFINITY;
+            }
+        }
+    }
+    __syncthreads();
+    // ---- softmax per row (a warp per row, 8 rows per warp) ----
+    for (int qr = warp; qr < kPfRows; qr += kAttnThreads / 32) {
+        const float s0 = sc[qr * SL + lane], s1 = sc[qr * SL + lane + 32];
+        float mx = fmaxf(s0, s1);
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const bool live = mx != -INFINITY;
+        const float e0 = live ? exp_cr(fsub(s0, mx)) : 0.0f, e1 = live ? exp_cr(fsub(s1, mx)) : 0.0f;
+        es[lane * SL + qr] = e0;
+        es[(lane + 32) * SL + qr] = e1;
+        float sum = e0 + e1;
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) { red[2 * qr] = mx; red[2 * qr + 1] = sum; }
+    }
+    __syncthreads();
+    // ---- PV: thread (i, j) owns rows 4i..4i+3 x columns (HD/16)*j .. ----
+    {
+        constexpr int DJ = HD / 16;  // columns per thread: 8 (HD 128) or 4 (HD 64)
+        const int i = tid >> 4, j = tid & 15;
+        float acc[4][DJ];
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+#pragma unroll
+            for (int y = 0; y < DJ; ++y) acc[x][y] = 0.0f;
+        for (int p = 0; p < cn; ++p) {
+            const float4 e = *reinterpret_cast<const float4*>(es + p * SL + 4 * i);
+            float v[DJ];
+#pragma unroll
+            for (int y = 0; y < DJ; y += 4) {
+                const float4 t = *reinterpret_cast<const float4*>(vs + p * RS + DJ * j + y);
+                v[y] = t.x; v[y + 1] = t.y; v[y + 2] = t.z; v[y + 3] = t.w;
+            }
+            const float ex[4] = {e.x, e.y, e.z, e.w};
+#pragma unroll
+            for (int x = 0; x < 4; ++x)
+#pragma unroll
+                for (int y = 0; y < DJ; ++y) acc[x][y] = fmaf(ex[x], v[y], acc[x][y]);
+        }
+        const size_t R = attn_record_floats(HD);
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+            const int qr = 4 * i + x;
+            const int zl = qr / G, g = qr % G;
+            const int z = z0 + zl;
+            if (z > z_last || c0 > pos_first + zl) continue;  // this query does not see the chunk
+            float* rec = a.part + (((size_t)z * a.n_heads + kvh * G + g) * a.max_splits + split) * R;
+#pragma unroll
+            for (int y = 0; y < DJ; ++y) rec[4 + DJ * j + y] = acc[x][y];
+            if (j == 0) { rec[0] = red[2 * qr]; rec[1] = red[2 * qr + 1]; }
+        }
+    }
+}
+
 // ---- exact mode (:1960-1987) ----
 // Softmax in the reference's order: max over the window (its running max
 // starts at -1e30), e_t = exp(s_t - max) (correctly rounded here; the reference
@@ -532,7 +689,36 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
         }
         return kOk;
     }
-    e = vec ? launch_partial<true, false>(a, grid, smem, st) : launch_partial<false, false>(a, grid, smem, st);
+    const int Gq = a.n_heads / a.n_kv;
+    if (n_tok > 1 && vec && a.window == 0 && a.chunk == kPfChunk && (a.hd == 128 || a.hd == 64) &&
+        kPfRows % Gq == 0 && Gq <= kPfRows && attn_prefill_smem_bytes(a.hd) <= (size_t)dev.max_smem_optin) {
+        // query-tiled causal prefill; score_cap carries the query count
+        AttnArgs b = a;
+        b.score_cap = n_tok;
+        const int qt = kPfRows / Gq;
+        const dim3 pgrid(a.max_splits, a.n_kv, (n_tok + qt - 1) / qt);
+        const size_t psm = attn_prefill_smem_bytes(a.hd);
+        static size_t set128 = 0, set64 = 0;
+        if (a.hd == 128) {
+            if (psm > set128) {
+                if (cudaFuncSetAttribute(attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)psm) != cudaSuccess)
+                    return kErrCuda;
+                set128 = psm;
+            }
+            e = launch_k(attn_prefill_kernel<128>, pgrid, dim3(kAttnThreads), psm, st, b);
+        } else {
+            if (psm > set64) {
+                if (cudaFuncSetAttribute(attn_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)psm) != cudaSuccess)
+                    return kErrCuda;
+                set64 = psm;
+            }
+            e = launch_k(attn_prefill_kernel<64>, pgrid, dim3(kAttnThreads), psm, st, b);
+        }
+    } else {
+        e = vec ? launch_partial<true, false>(a, grid, smem, st) : launch_partial<false, false>(a, grid, smem, st);
+    }
     if (e != cudaSuccess) return kErrCuda;
     const size_t csm = (size_t)a.max_splits * 8;
     if (csm > 48 * 1024 &&

@@ -18,8 +18,11 @@
 //     per-block scales; they also stage the tokens' int8 quants and scales;
 //   * MMA warp: one thread issues the 8 block MMAs of a unit into one half of
 //     TMEM (8 x 32 columns) and commits them to mbarriers;
-//   * epilogue warps (4): warp w reads TMEM lanes 32w..32w+31 (its rows),
-//     one 32-column block at a time, and accumulates the block terms.
+//   * epilogue warps (8): warp w reads TMEM lanes 32(w%4).. (its rows) and
+//     16 of the 32 token columns, one block at a time, and accumulates the
+//     block terms.
+// The loaders fetch the next unit's weight bytes while unpacking the current
+// one and copy token quants with cp.async.
 // Units alternate between the two stages and the two TMEM halves, so the
 // tensor cores, the loaders and the epilogue overlap.  Every wait is bounded;
 // on a timeout the kernel records an error, skips the remaining work and
@@ -36,7 +39,7 @@ namespace gncx {
 constexpr int kTcM = 128;        // weight rows per tile
 constexpr int kTcN = 32;         // tokens per tile
 constexpr int kTcCols = 512;     // TMEM columns: 2 halves x 8 blocks x kTcN
-constexpr int kTcEpiWarps = 4;
+constexpr int kTcEpiWarps = 8;   // two per TMEM lane quadrant, 16 tokens each
 constexpr int kTcLoadWarps = 4;
 constexpr int kTcThreads = (kTcEpiWarps + kTcLoadWarps + 1) * 32;
 constexpr int kTcMmaWarp = kTcEpiWarps + kTcLoadWarps;
@@ -45,7 +48,7 @@ constexpr int kTcMmaWarp = kTcEpiWarps + kTcLoadWarps;
 constexpr int kTcA = 16 * 16 * 128;     // 16 K-chunks x 16 row groups x (8 rows x 16 B)
 constexpr int kTcB = 16 * 4 * 128;      // 16 K-chunks x 4 token groups x (8 tokens x 16 B)
 constexpr int kTcWS = 8 * kTcM * 8;     // per block, per row: float2
-constexpr int kTcAS = 8 * kTcN * 8;     // per block, per token: float2 {d_a, sum q}
+constexpr int kTcAS = 8 * kTcN * 8;     // per block and token {d_a, sum q} (Q4_K: per chunk {lo, hi} pairs)
 constexpr int kTcStage = kTcA + kTcB + kTcWS + kTcAS;
 constexpr int kTcSmem = 2 * kTcStage + 128;
 // More than half of an SM's shared memory, so one CTA per SM owns all of TMEM.
@@ -165,12 +168,29 @@ template <> struct TcFmt<kQ4_0> { static constexpr int UB = 144; };
 template <> struct TcFmt<kQ8_0> { static constexpr int UB = 272; };
 template <> struct TcFmt<kQ4_K> { static constexpr int UB = 144; };
 
+__device__ __forceinline__ void cp_async16_tc(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+
+// 16 consecutive TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+
 template <int T>
 __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_t* __restrict__ w, size_t rb,
                                                                     const ActBlock* __restrict__ act, int batch,
                                                                     int in_dim, int out_dim, float* __restrict__ y,
                                                                     int ldy, int32_t* err) {
     constexpr int UB = TcFmt<T>::UB;
+    constexpr int NQ = UB / 16;           // 16-byte pieces of a row's unit
+    constexpr int NE = kTcEpiWarps * 32;  // epilogue threads
+    constexpr int NL = kTcLoadWarps * 32; // loader threads
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kTcStage);
     uint64_t* empty = full + 2;
@@ -187,10 +207,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
 
     if (tid == 0) {
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&full[i], kTcLoadWarps * 32);
-            mbar_init(&empty[i], 1 + kTcEpiWarps * 32);
+            mbar_init(&full[i], NL);
+            mbar_init(&empty[i], 1 + NE);
             mbar_init(&accf[i], 1);
-            mbar_init(&acce[i], kTcEpiWarps * 32);
+            mbar_init(&acce[i], NE);
         }
         mbar_init(done, 1);
         abort_flag = 0;
@@ -210,59 +230,86 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
     auto stage_a = [&](int s) { return smem + s * kTcStage; };
     auto stage_b = [&](int s) { return smem + s * kTcStage + kTcA; };
     auto stage_ws = [&](int s) { return reinterpret_cast<float2*>(smem + s * kTcStage + kTcA + kTcB); };
-    auto stage_as = [&](int s) { return reinterpret_cast<float2*>(smem + s * kTcStage + kTcA + kTcB + kTcWS); };
+    auto stage_as = [&](int s) { return smem + s * kTcStage + kTcA + kTcB + kTcWS; };
     auto fail = [&]() {
         record_error(err, kErrTimeout);
         atomicExch(&abort_flag, 1);
     };
 
     if (warp >= kTcEpiWarps && warp < kTcMmaWarp) {
-        // ---------------- loaders ----------------
-        const int r = tid - kTcEpiWarps * 32;  // 0..127: weight row within the tile
+        // ---------------- loaders: thread r owns weight row r of the tile ----------------
+        const int r = tid - NE;
         const int grow = row0 + r;
+        const bool row_ok = grow < out_dim;
+        const uint4* wrow = reinterpret_cast<const uint4*>(w + (size_t)(row_ok ? grow : 0) * rb);
+        uint32_t q[4 * NQ + 1];
+        auto fetch = [&](int u) {  // the next unit's raw bytes, in flight while this one is unpacked
+#pragma unroll
+            for (int i = 0; i < NQ; ++i) {
+                const uint4 v = row_ok ? __ldg(wrow + (size_t)u * NQ + i) : make_uint4(0, 0, 0, 0);
+                q[4 * i] = v.x; q[4 * i + 1] = v.y; q[4 * i + 2] = v.z; q[4 * i + 3] = v.w;
+            }
+            q[4 * NQ] = 0u;
+        };
+        fetch(0);
         for (int u = 0; u < upr; ++u) {
             const int s = u & 1;
             if (u >= 2 && !mbar_wait(&empty[s], ((u >> 1) - 1) & 1)) fail();
             if (*(volatile int*)&abort_flag) break;
-            uint8_t* at = stage_a(s);
-            float2* ws = stage_ws(s);
-            if (grow < out_dim) {
-                uint32_t q[UB / 4 + 1];
-                const uint4* src = reinterpret_cast<const uint4*>(w + (size_t)grow * rb + (size_t)u * UB);
-#pragma unroll
-                for (int i = 0; i < UB / 16; ++i) {
-                    const uint4 v = __ldg(src + i);
-                    q[4 * i] = v.x; q[4 * i + 1] = v.y; q[4 * i + 2] = v.z; q[4 * i + 3] = v.w;
-                }
-                q[UB / 4] = 0u;
-                tc_unpack<T>(q, at, r, ws);
-            } else {
-                for (int kc = 0; kc < 16; ++kc) *reinterpret_cast<uint4*>(at + tile_off(r, kc, 2048)) = make_uint4(0, 0, 0, 0);
-                for (int j = 0; j < 8; ++j) ws[j * kTcM + r] = make_float2(0.0f, 0.0f);
-            }
-            // tokens: 32 x 16 K-chunks of quants, 32 x 8 block scalars
+            // tokens' quants straight into the B tile (asynchronous), then their scalars
             uint8_t* bt = stage_b(s);
-            for (int p = r; p < kTcN * 16; p += kTcLoadWarps * 32) {
+            for (int p = r; p < kTcN * 16; p += NL) {
                 const int t = p >> 4, kc = p & 15;
                 const int tok = tok0 + t;
-                uint4 v = make_uint4(0, 0, 0, 0);
+                uint8_t* dst = bt + tile_off(t, kc, 512);
                 if (tok < batch)
-                    v = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(act + (size_t)tok * nb + u * 8 +
-                                                                                       (kc >> 1)) +
-                                                        16 + 16 * (kc & 1));
-                *reinterpret_cast<uint4*>(bt + tile_off(t, kc, 512)) = v;
+                    cp_async16_tc(dst, reinterpret_cast<const uint8_t*>(act + (size_t)tok * nb + u * 8 + (kc >> 1)) +
+                                           16 + 16 * (kc & 1));
+                else
+                    *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
             }
-            float2* as = stage_as(s);
-            for (int p = r; p < kTcN * 8; p += kTcLoadWarps * 32) {
+            asm volatile("cp.async.commit_group;" ::: "memory");
+            uint4 hdr[(kTcN * 8 + NL - 1) / NL];
+#pragma unroll
+            for (int k = 0; k < (kTcN * 8 + NL - 1) / NL; ++k) {
+                const int p = r + k * NL;
                 const int b = p / kTcN, t = p % kTcN;
-                const int tok = tok0 + t;
-                float2 v = make_float2(0.0f, 0.0f);
-                if (tok < batch) {
-                    const uint4 h = *reinterpret_cast<const uint4*>(act + (size_t)tok * nb + u * 8 + b);
-                    v = make_float2(__uint_as_float(h.x), i2f((int)h.y + (int)h.z));
-                }
-                as[b * kTcN + t] = v;
+                hdr[k] = (p < kTcN * 8 && tok0 + t < batch)
+                             ? *reinterpret_cast<const uint4*>(act + (size_t)(tok0 + t) * nb + u * 8 + b)
+                             : make_uint4(0, 0, 0, 0);
             }
+            constexpr bool kAhead = NQ <= 9;  // a second copy of a Q8_0 unit does not fit in registers
+            uint32_t cur[kAhead ? 4 * NQ + 1 : 1];
+            if constexpr (kAhead) {
+#pragma unroll
+                for (int i = 0; i < 4 * NQ + 1; ++i) cur[i] = q[i];
+                if (u + 1 < upr) fetch(u + 1);
+            }
+            if (row_ok) {
+                tc_unpack<T>(kAhead ? cur : q, stage_a(s), r, stage_ws(s));
+            } else {
+                for (int kc = 0; kc < 16; ++kc)
+                    *reinterpret_cast<uint4*>(stage_a(s) + tile_off(r, kc, 2048)) = make_uint4(0, 0, 0, 0);
+                for (int j = 0; j < 8; ++j) stage_ws(s)[j * kTcM + r] = make_float2(0.0f, 0.0f);
+            }
+            if constexpr (!kAhead) {
+                if (u + 1 < upr) fetch(u + 1);
+            }
+            uint8_t* as = stage_as(s);
+#pragma unroll
+            for (int k = 0; k < (kTcN * 8 + NL - 1) / NL; ++k) {
+                const int p = r + k * NL;
+                if (p < kTcN * 8) {
+                    const int b = p / kTcN, t = p % kTcN;
+                    const float ad = __uint_as_float(hdr[k].x), sq = i2f((int)hdr[k].y + (int)hdr[k].z);
+                    if constexpr (T == kQ4_K)  // per 64-input chunk and token: {d_lo, S_lo, d_hi, S_hi}
+                        *reinterpret_cast<float2*>(as + (((b >> 1) * kTcN + t) * 16 + (b & 1) * 8)) =
+                            make_float2(ad, sq);
+                    else
+                        *reinterpret_cast<float2*>(as + (b * kTcN + t) * 8) = make_float2(ad, sq);
+                }
+            }
+            asm volatile("cp.async.wait_all;" ::: "memory");
             fence_async_smem();  // the tensor cores read these tiles through the async proxy
             mbar_arrive(&full[s]);
         }
@@ -293,12 +340,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
         }
         __syncwarp();
     } else {
-        // ---------------- epilogue: rows 32*warp .. +31 ----------------
-        const int r = warp * 32 + lane;
-        const uint32_t tlane = tmem + ((uint32_t)(warp * 32) << 16);
-        float acc[kTcN];
+        // ---- epilogue: warp w reads TMEM lanes 32*(w%4).. (its rows), tokens 16*(w/4) .. +15 ----
+        constexpr int TN = kTcN / (kTcEpiWarps / 4);  // tokens per thread
+        const int quad = warp & 3, half = warp >> 2;
+        const int r = quad * 32 + lane;
+        const int t0 = half * TN;
+        const uint32_t tlane = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)t0;
+        float acc[TN];
 #pragma unroll
-        for (int t = 0; t < kTcN; ++t) acc[t] = 0.0f;
+        for (int t = 0; t < TN; ++t) acc[t] = 0.0f;
         for (int u = 0; u < upr; ++u) {
             const int s = u & 1, hb = u & 1;
             // accf: this unit's dots are in TMEM; full: the stage's scales are
@@ -308,35 +358,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
             if (*(volatile int*)&abort_flag) break;
             tc_fence_after();
             const float2* ws = stage_ws(s);
-            const float2* as = stage_as(s);
+            const uint8_t* as = stage_as(s);
             if constexpr (T == kQ4_K) {
                 // per 64-input chunk c: st = (0 + lo) + hi, a half skipped when its act scale is 0 (:1546-1618)
 #pragma unroll 1
                 for (int c = 0; c < 4; ++c) {
-                    int dl[32], dh[32];
-                    tmem_ld32(tlane + (uint32_t)((hb * 8 + 2 * c) * kTcN), dl);
-                    tmem_ld32(tlane + (uint32_t)((hb * 8 + 2 * c + 1) * kTcN), dh);
+                    int dl[TN], dh[TN];
+                    tmem_ld16(tlane + (uint32_t)((hb * 8 + 2 * c) * kTcN), dl);
+                    tmem_ld16(tlane + (uint32_t)((hb * 8 + 2 * c + 1) * kTcN), dh);
                     tmem_wait_ld();
                     const float2 w1 = ws[(2 * c) * kTcM + r], w2 = ws[(2 * c + 1) * kTcM + r];
+                    const float4* a4 = reinterpret_cast<const float4*>(as) + c * kTcN + t0;
 #pragma unroll
-                    for (int t = 0; t < kTcN; ++t) {
-                        const float2 al = as[(2 * c) * kTcN + t], ah = as[(2 * c + 1) * kTcN + t];
+                    for (int t = 0; t < TN; ++t) {
+                        const float4 a = a4[t];  // {d_lo, S_lo, d_hi, S_hi}
                         float st = 0.0f;
-                        if (al.x != 0.0f) st = fadd(st, fmul(al.x, fsub(fmul(w1.x, i2f(dl[t])), fmul(w1.y, al.y))));
-                        if (ah.x != 0.0f) st = fadd(st, fmul(ah.x, fsub(fmul(w2.x, i2f(dh[t])), fmul(w2.y, ah.y))));
+                        if (a.x != 0.0f) st = fadd(st, fmul(a.x, fsub(fmul(w1.x, i2f(dl[t])), fmul(w1.y, a.y))));
+                        if (a.z != 0.0f) st = fadd(st, fmul(a.z, fsub(fmul(w2.x, i2f(dh[t])), fmul(w2.y, a.w))));
                         acc[t] = fadd(acc[t], st);
                     }
                 }
             } else {
 #pragma unroll 1
                 for (int b = 0; b < 8; ++b) {
-                    int dv[32];
-                    tmem_ld32(tlane + (uint32_t)((hb * 8 + b) * kTcN), dv);
+                    int dv[TN];
+                    tmem_ld16(tlane + (uint32_t)((hb * 8 + b) * kTcN), dv);
                     tmem_wait_ld();
                     const float wd = ws[b * kTcM + r].x;
+                    const float2* a2 = reinterpret_cast<const float2*>(as) + b * kTcN + t0;
 #pragma unroll
-                    for (int t = 0; t < kTcN; ++t) {
-                        const float2 a = as[b * kTcN + t];
+                    for (int t = 0; t < TN; ++t) {
+                        const float2 a = a2[t];
                         float term;
                         if constexpr (T == kQ4_0) {
                             // (float)(dot - 8*sum_q) * (d_w * d_a), 0 when d_a == 0
@@ -356,8 +408,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
         const int grow = row0 + r;
         if (grow < out_dim && !*(volatile int*)&abort_flag) {
 #pragma unroll
-            for (int t = 0; t < kTcN; ++t)
-                if (tok0 + t < batch) y[(size_t)(tok0 + t) * ldy + grow] = acc[t];
+            for (int t = 0; t < TN; ++t)
+                if (tok0 + t0 + t < batch) y[(size_t)(tok0 + t0 + t) * ldy + grow] = acc[t];
         }
     }
     tc_fence_before();
