@@ -400,7 +400,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_prefill_kernel(const Att
         cp_async_wait<0>();
         __syncthreads();
     }
-    // ---- scores: thread (i, j) owns rows 4i..4i+3 x positions 4j..4j+3 ----
+    // ---- scores: thread (i, j) owns rows 4i..4i+3 x positions j, j+16, j+32, j+48
+    // (consecutive threads read consecutive padded K rows: no bank conflicts) ----
     {
         const int i = tid >> 4, j = tid & 15;
         float acc[4][4];
@@ -415,8 +416,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_prefill_kernel(const Att
             for (int x = 0; x < 4; ++x) {
                 q0[x] = *reinterpret_cast<const float4*>(qs + (4 * i + x) * RS + 8 * m);
                 q1[x] = *reinterpret_cast<const float4*>(qs + (4 * i + x) * RS + 8 * m + 4);
-                k0[x] = *reinterpret_cast<const float4*>(ks + (4 * j + x) * RS + 8 * m);
-                k1[x] = *reinterpret_cast<const float4*>(ks + (4 * j + x) * RS + 8 * m + 4);
+                k0[x] = *reinterpret_cast<const float4*>(ks + (j + 16 * x) * RS + 8 * m);
+                k1[x] = *reinterpret_cast<const float4*>(ks + (j + 16 * x) * RS + 8 * m + 4);
             }
 #pragma unroll
             for (int x = 0; x < 4; ++x)
@@ -436,7 +437,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_prefill_kernel(const Att
             const int pos_q = pos_first + qr / G;
 #pragma unroll
             for (int y = 0; y < 4; ++y) {
-                const int p = 4 * j + y;
+                const int p = j + 16 * y;
                 sc[qr * SL + p] = (p < cn && c0 + p <= pos_q) ? acc[x][y] * a.scale : -INFINITY;
             }
         }
