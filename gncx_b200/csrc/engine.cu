@@ -13,7 +13,12 @@
 //     argmax -- is one captured CUDA graph launch with no host round trip;
 //   * the KV cache is fp32 like the reference's, laid out head-major
 //     [n_kv][max_seq][head_dim] so a run of positions of one head is contiguous
-//     (one bulk copy per attention chunk).
+//     (one bulk copy per attention chunk);
+//   * tensor parallel (one process per GPU): every linear layer and the
+//     attention heads are split by output rows, so each output element is
+//     computed whole on one GPU in the 1-GPU order and the token stream is the
+//     same; the ranks all-gather (tp.cu) the attention output, the
+//     attn_output and ffn_down results, the GLU output and the logits.
 #include <cuda_runtime.h>
 #include <fcntl.h>
 #include <math.h>
@@ -170,6 +175,11 @@ struct Engine {
     float eps = 1e-6f, rope_base = 10000.0f, softcap = 0.0f, attn_scale = 0.0f, embd_scale = 1.0f;
     int eos = -1;
     bool qk_norm = false;
+    // this rank's share under tensor parallelism (the whole model when tp.size == 1)
+    TpComm tp;
+    int nh_l = 0, nkv_l = 0, qd_l = 0, kvd_l = 0, ffn_l = 0, dim_l = 0, voc0 = 0, voc_l = 0;
+    size_t x_q = 0, x_p = 0, x_f = 0, x_l = 0;  // gather buffers (byte offsets in the exchange region)
+    int x_rows = 0;                              // rows each gather buffer holds
     const uint8_t* tok_embd = nullptr;
     int embd_type = 0;
     const float* out_norm = nullptr;
@@ -180,6 +190,7 @@ struct Engine {
     float *rope_c = nullptr, *rope_s = nullptr;
     // decode buffers
     float *hidden = nullptr, *proj = nullptr, *qkv = nullptr, *gu = nullptr, *logits = nullptr, *normed = nullptr;
+    float* logits_own = nullptr;  // logits buffer of a 1-GPU engine (tp: the gather buffer)
     uint8_t *act_d = nullptr, *act_q = nullptr, *act_f = nullptr;  // staged activation vectors
     float* part = nullptr;
     int max_splits = 0;
@@ -212,6 +223,7 @@ struct Engine {
 
 static constexpr int kDecodeChunk = 64;    // positions per attention split in decode
 static constexpr int kPrefillGroup = 256;  // prompt positions per attention launch in prefill
+static constexpr int kTpMaxRows = 4096;    // prompt rows a tensor-parallel prefill gathers at once
 
 #define CK(x)                                             \
     do {                                                  \
@@ -229,26 +241,51 @@ static int gemv(Engine* e, const uint8_t* w, int t, const uint8_t* act, const fl
                        e->stream);
 }
 
+static int gather(Engine* e, size_t buf, int rows, int row_floats, int off, int len);
+
+// LM head over this rank's vocabulary rows of the staged act_d, then (tensor
+// parallel) the all-gather that gives every rank all logits.
+static int lm_head(Engine* e) {
+    const uint8_t* w = e->tok_embd + (size_t)e->voc0 * row_bytes(e->embd_type, e->dim);
+    CK(gemv(e, w, e->embd_type, e->act_d, e->normed, e->dim, e->voc_l, e->logits + e->voc0, e->softcap));
+    return gather(e, e->x_l, 1, e->vocab, e->voc0, e->voc_l);
+}
+
+// GEMV whose input is an fp32 vector (re-quantized inside the GEMV).
+static int gemv_x(Engine* e, const uint8_t* w, int t, const float* x, int in, int out, float* y, float cap = 0.0f) {
+    return gemv_launch(w, t, x, nullptr, in, out, y, cap, e->d_err, e->stream);
+}
+
+static int gather(Engine* e, size_t buf, int rows, int row_floats, int off, int len) {
+    return tp_gather_launch(e->tp, buf, rows, row_floats, off, len, e->d_err, e->stream);
+}
+
 // One decode step: forward(st->token at st->pos) and, if `sample`, the
 // penalized argmax that appends the next token and advances the position.
 static int decode_step(Engine* e, bool sample, double penalty) {
     cudaStream_t s = e->stream;
-    const int D = e->dim, QD = e->q_dim, KVD = e->kv_dim, F = e->ffn;
-    const int qkv_w = QD + 2 * KVD;
+    const int D = e->dim, QD = e->q_dim, F = e->ffn;
+    const int qd = e->qd_l, kvd = e->kvd_l, fl = e->ffn_l, dl = e->dim_l;
+    const int qkv_w = qd + 2 * kvd;
+    const bool tp = e->tp.size > 1;
+    const int rk = e->tp.rank;
+    float* gq = tp ? tp_buffer(e->tp, e->x_q) : nullptr;  // attention output (gathered)
+    float* gp = tp ? tp_buffer(e->tp, e->x_p) : e->proj;  // attn_output / ffn_down result
+    float* gf = tp ? tp_buffer(e->tp, e->x_f) : nullptr;  // GLU output (gathered)
     CK(dequant_launch(e->tok_embd, e->embd_type, 1, D, e->embd_scale, &e->st->token, e->hidden, s));
     for (int l = 0; l < e->n_layers; ++l) {
         const LayerW& w = e->L[l];
-        CK(add_norm_quant_launch(e->hidden, l == 0 ? nullptr : e->proj, w.attn_norm, 1, D, e->eps,
+        CK(add_norm_quant_launch(e->hidden, l == 0 ? nullptr : gp, w.attn_norm, 1, D, e->eps,
                                  ActOut{nullptr, e->act_d}, e->normed, s));
         if (w.qkv_fused) {
             CK(gemv(e, w.wq, w.tq, e->act_d, e->normed, D, qkv_w, e->qkv));
         } else {
-            CK(gemv(e, w.wq, w.tq, e->act_d, e->normed, D, QD, e->qkv));
-            CK(gemv(e, w.wk, w.tk, e->act_d, e->normed, D, KVD, e->qkv + QD));
-            CK(gemv(e, w.wv, w.tv, e->act_d, e->normed, D, KVD, e->qkv + QD + KVD));
+            CK(gemv(e, w.wq, w.tq, e->act_d, e->normed, D, qd, e->qkv));
+            CK(gemv(e, w.wk, w.tk, e->act_d, e->normed, D, kvd, e->qkv + qd));
+            CK(gemv(e, w.wv, w.tv, e->act_d, e->normed, D, kvd, e->qkv + qd + kvd));
         }
-        CK(qkv_post_launch(e->qkv, qkv_w, 1, e->nh, e->nkv, e->hd, w.q_norm, w.k_norm, e->qk_norm, e->eps, e->rope_c,
-                           e->rope_s, 0, &e->st->pos, w.kc, w.vc, e->hd, (int64_t)e->max_seq * e->hd, s));
+        CK(qkv_post_launch(e->qkv, qkv_w, 1, e->nh_l, e->nkv_l, e->hd, w.q_norm, w.k_norm, e->qk_norm, e->eps,
+                           e->rope_c, e->rope_s, 0, &e->st->pos, w.kc, w.vc, e->hd, (int64_t)e->max_seq * e->hd, s));
         AttnArgs a{};
         a.q = e->qkv;
         a.q_stride = qkv_w;
@@ -258,59 +295,79 @@ static int decode_step(Engine* e, bool sample, double penalty) {
         a.kv_head_stride = e->max_seq * e->hd;
         a.pos0 = 0;
         a.pos_dev = &e->st->pos;
-        a.n_heads = e->nh;
-        a.n_kv = e->nkv;
+        a.n_heads = e->nh_l;
+        a.n_kv = e->nkv_l;
         a.hd = e->hd;
         a.scale = e->attn_scale;
         a.window = 0;
         a.chunk = kDecodeChunk;
         a.max_splits = e->max_splits;
         a.part = e->part;
-        a.out = e->exact ? e->qkv : nullptr;  // exact mode: the output replaces q
-        a.out_stride = qkv_w;
+        if (tp) {
+            a.out = gq + (size_t)rk * qd;  // this rank's heads of the gathered vector
+            a.out_stride = QD;
+            a.act_out = ActOut{nullptr, nullptr};
+        } else {
+            a.out = e->exact ? e->qkv : nullptr;  // exact mode: the output replaces q
+            a.out_stride = qkv_w;
+            a.act_out = ActOut{nullptr, e->act_q};
+        }
         a.prefetch_old = 1;  // cache rows below pos come from earlier tokens
-        a.act_out = ActOut{nullptr, e->act_q};
         a.err = e->d_err;
         a.exact = e->exact ? 1 : 0;
         a.scores = e->scores;
         a.score_cap = e->max_splits * kDecodeChunk;
         CK(attention_run(a, 1, s));
-        CK(gemv(e, w.wo, w.to, e->act_q, nullptr, QD, D, e->proj));
-        CK(add_norm_quant_launch(e->hidden, e->proj, w.ffn_norm, 1, D, e->eps, ActOut{nullptr, e->act_d}, e->normed,
-                                 s));
-        if (w.gu_fused) {
-            CK(gemv(e, w.wg, w.tg, e->act_d, e->normed, D, 2 * F, e->gu));
+        if (tp) {
+            CK(gather(e, e->x_q, 1, QD, rk * qd, qd));
+            CK(gemv_x(e, w.wo, w.to, gq, QD, dl, gp + (size_t)rk * dl));
+            CK(gather(e, e->x_p, 1, D, rk * dl, dl));
         } else {
-            CK(gemv(e, w.wg, w.tg, e->act_d, e->normed, D, F, e->gu));
-            CK(gemv(e, w.wu, w.tu, e->act_d, e->normed, D, F, e->gu + F));
+            CK(gemv(e, w.wo, w.to, e->act_q, nullptr, QD, D, e->proj));
         }
-        CK(glu_quant_launch(e->gu, e->gu + F, 2 * F, F, 1, e->arch == 2, ActOut{nullptr, e->act_f}, s));
-        CK(gemv(e, w.wd, w.td, e->act_f, nullptr, F, D, e->proj));
+        CK(add_norm_quant_launch(e->hidden, gp, w.ffn_norm, 1, D, e->eps, ActOut{nullptr, e->act_d}, e->normed, s));
+        if (w.gu_fused) {
+            CK(gemv(e, w.wg, w.tg, e->act_d, e->normed, D, 2 * fl, e->gu));
+        } else {
+            CK(gemv(e, w.wg, w.tg, e->act_d, e->normed, D, fl, e->gu));
+            CK(gemv(e, w.wu, w.tu, e->act_d, e->normed, D, fl, e->gu + fl));
+        }
+        if (tp) {
+            CK(glu_quant_launch(e->gu, e->gu + fl, 2 * fl, fl, 1, e->arch == 2, ActOut{nullptr, nullptr}, s,
+                                gf + (size_t)rk * fl, F));
+            CK(gather(e, e->x_f, 1, F, rk * fl, fl));
+            CK(gemv_x(e, w.wd, w.td, gf, F, dl, gp + (size_t)rk * dl));
+            CK(gather(e, e->x_p, 1, D, rk * dl, dl));
+        } else {
+            CK(glu_quant_launch(e->gu, e->gu + F, 2 * F, F, 1, e->arch == 2, ActOut{nullptr, e->act_f}, s));
+            CK(gemv(e, w.wd, w.td, e->act_f, nullptr, F, D, e->proj));
+        }
     }
-    CK(add_norm_quant_launch(e->hidden, e->proj, e->out_norm, 1, D, e->eps, ActOut{nullptr, e->act_d}, e->normed, s));
-    CK(gemv(e, e->tok_embd, e->embd_type, e->act_d, e->normed, D, e->vocab, e->logits, e->softcap));
+    CK(add_norm_quant_launch(e->hidden, gp, e->out_norm, 1, D, e->eps, ActOut{nullptr, e->act_d}, e->normed, s));
+    CK(lm_head(e));
     if (sample) CK(argmax_state_launch(e->logits, e->vocab, e->st, penalty, e->out_ids, 1, e->am_scratch, s));
     return kOk;
 }
 
 static int ensure_prefill(Engine* e, int B) {
     if (B <= e->pf_cap) return kOk;
+    if (e->tp.size > 1 && B > e->x_rows) return kErrCapacity;  // the gather buffers hold x_rows rows
     cudaStreamSynchronize(e->stream);
     cudaFree(e->pf_h); cudaFree(e->pf_p); cudaFree(e->pf_qkv); cudaFree(e->pf_gu); cudaFree(e->pf_part);
     cudaFree(e->pf_act); cudaFree(e->pf_actq); cudaFree(e->pf_actf); cudaFree(e->pf_scores);
     e->pf_scores = nullptr;
     e->pf_cap = 0;
-    const size_t D = e->dim, QKV = e->q_dim + 2 * e->kv_dim, F = e->ffn;
+    const size_t D = e->dim, QKV = e->qd_l + 2 * e->kvd_l, FL = e->ffn_l;
     const int grp = B < kPrefillGroup ? B : kPrefillGroup;
     const size_t splits = (size_t)(B + kDecodeChunk - 1) / kDecodeChunk;
-    e->pf_part_floats = (size_t)grp * e->nh * splits * attn_record_floats(e->hd);
+    e->pf_part_floats = (size_t)grp * e->nh_l * splits * attn_record_floats(e->hd);
     if (cudaMalloc(&e->pf_h, (size_t)B * D * 4) || cudaMalloc(&e->pf_p, (size_t)B * D * 4) ||
-        cudaMalloc(&e->pf_qkv, (size_t)B * QKV * 4) || cudaMalloc(&e->pf_gu, (size_t)B * 2 * F * 4) ||
+        cudaMalloc(&e->pf_qkv, (size_t)B * QKV * 4) || cudaMalloc(&e->pf_gu, (size_t)B * 2 * FL * 4) ||
         cudaMalloc(&e->pf_part, e->pf_part_floats * 4) ||
         cudaMalloc(&e->pf_act, (size_t)B * (D / 32) * sizeof(ActBlock)) ||
         cudaMalloc(&e->pf_actq, (size_t)B * (e->q_dim / 32) * sizeof(ActBlock)) ||
-        cudaMalloc(&e->pf_actf, (size_t)B * (F / 32) * sizeof(ActBlock)) ||
-        cudaMalloc(&e->pf_scores, (size_t)grp * e->nh * splits * kDecodeChunk * 4)) {
+        cudaMalloc(&e->pf_actf, (size_t)B * (e->ffn / 32) * sizeof(ActBlock)) ||
+        cudaMalloc(&e->pf_scores, (size_t)grp * e->nh_l * splits * kDecodeChunk * 4)) {
         cudaGetLastError();
         return kErrOutOfMemory;
     }
@@ -324,23 +381,29 @@ static int ensure_prefill(Engine* e, int B) {
 // the positions <= its own, exactly what the reference's per-token loop does).
 static int prefill_batch(Engine* e, int B) {
     cudaStream_t s = e->stream;
-    const int D = e->dim, QD = e->q_dim, KVD = e->kv_dim, F = e->ffn;
-    const int qkv_w = QD + 2 * KVD;
+    const int D = e->dim, QD = e->q_dim, F = e->ffn;
+    const int qd = e->qd_l, kvd = e->kvd_l, fl = e->ffn_l, dl = e->dim_l;
+    const int qkv_w = qd + 2 * kvd;
+    const bool tp = e->tp.size > 1;
+    const int rk = e->tp.rank;
     CK(ensure_prefill(e, B));
+    float* gq = tp ? tp_buffer(e->tp, e->x_q) : nullptr;
+    float* gp = tp ? tp_buffer(e->tp, e->x_p) : e->pf_p;
+    float* gf = tp ? tp_buffer(e->tp, e->x_f) : nullptr;
     CK(dequant_launch(e->tok_embd, e->embd_type, B, D, e->embd_scale, e->ids_dev, e->pf_h, s));
     for (int l = 0; l < e->n_layers; ++l) {
         const LayerW& w = e->L[l];
-        CK(add_norm_quant_launch(e->pf_h, l == 0 ? nullptr : e->pf_p, w.attn_norm, B, D, e->eps,
+        CK(add_norm_quant_launch(e->pf_h, l == 0 ? nullptr : gp, w.attn_norm, B, D, e->eps,
                                  ActOut{e->pf_act, nullptr}, nullptr, s));
         if (w.qkv_fused) {
             CK(matbatch_launch(w.wq, w.tq, nullptr, e->pf_act, B, D, qkv_w, e->pf_qkv, e->d_err, s, qkv_w));
         } else {
-            CK(matbatch_launch(w.wq, w.tq, nullptr, e->pf_act, B, D, QD, e->pf_qkv, e->d_err, s, qkv_w));
-            CK(matbatch_launch(w.wk, w.tk, nullptr, e->pf_act, B, D, KVD, e->pf_qkv + QD, e->d_err, s, qkv_w));
-            CK(matbatch_launch(w.wv, w.tv, nullptr, e->pf_act, B, D, KVD, e->pf_qkv + QD + KVD, e->d_err, s, qkv_w));
+            CK(matbatch_launch(w.wq, w.tq, nullptr, e->pf_act, B, D, qd, e->pf_qkv, e->d_err, s, qkv_w));
+            CK(matbatch_launch(w.wk, w.tk, nullptr, e->pf_act, B, D, kvd, e->pf_qkv + qd, e->d_err, s, qkv_w));
+            CK(matbatch_launch(w.wv, w.tv, nullptr, e->pf_act, B, D, kvd, e->pf_qkv + qd + kvd, e->d_err, s, qkv_w));
         }
-        CK(qkv_post_launch(e->pf_qkv, qkv_w, B, e->nh, e->nkv, e->hd, w.q_norm, w.k_norm, e->qk_norm, e->eps, e->rope_c,
-                           e->rope_s, 0, nullptr, w.kc, w.vc, e->hd, (int64_t)e->max_seq * e->hd, s));
+        CK(qkv_post_launch(e->pf_qkv, qkv_w, B, e->nh_l, e->nkv_l, e->hd, w.q_norm, w.k_norm, e->qk_norm, e->eps,
+                           e->rope_c, e->rope_s, 0, nullptr, w.kc, w.vc, e->hd, (int64_t)e->max_seq * e->hd, s));
         for (int z0 = 0; z0 < B; z0 += kPrefillGroup) {
             const int nz = B - z0 < kPrefillGroup ? B - z0 : kPrefillGroup;
             AttnArgs a{};
@@ -352,42 +415,64 @@ static int prefill_batch(Engine* e, int B) {
             a.kv_head_stride = e->max_seq * e->hd;
             a.pos0 = z0;
             a.pos_dev = nullptr;
-            a.n_heads = e->nh;
-            a.n_kv = e->nkv;
+            a.n_heads = e->nh_l;
+            a.n_kv = e->nkv_l;
             a.hd = e->hd;
             a.scale = e->attn_scale;
             a.window = 0;
             a.chunk = kDecodeChunk;
             a.max_splits = (z0 + nz + kDecodeChunk - 1) / kDecodeChunk;
             a.part = e->pf_part;
-            a.out = e->exact ? e->pf_qkv + (size_t)z0 * qkv_w : nullptr;
-            a.out_stride = qkv_w;
-            a.act_out = ActOut{e->pf_actq + (size_t)z0 * (QD / 32), nullptr};
+            if (tp) {
+                a.out = gq + (size_t)z0 * QD + (size_t)rk * qd;
+                a.out_stride = QD;
+                a.act_out = ActOut{nullptr, nullptr};
+            } else {
+                a.out = e->exact ? e->pf_qkv + (size_t)z0 * qkv_w : nullptr;
+                a.out_stride = qkv_w;
+                a.act_out = ActOut{e->pf_actq + (size_t)z0 * (QD / 32), nullptr};
+            }
             a.err = e->d_err;
             a.exact = e->exact ? 1 : 0;
             a.scores = e->pf_scores;
             a.score_cap = (int)e->pf_score_cap;
-            if ((size_t)nz * e->nh * a.max_splits * attn_record_floats(e->hd) > e->pf_part_floats) return kErrCapacity;
+            if ((size_t)nz * e->nh_l * a.max_splits * attn_record_floats(e->hd) > e->pf_part_floats)
+                return kErrCapacity;
             CK(attention_run(a, nz, s));
         }
-        CK(matbatch_launch(w.wo, w.to, nullptr, e->pf_actq, B, QD, D, e->pf_p, e->d_err, s));
-        CK(add_norm_quant_launch(e->pf_h, e->pf_p, w.ffn_norm, B, D, e->eps, ActOut{e->pf_act, nullptr}, nullptr, s));
-        if (w.gu_fused) {
-            CK(matbatch_launch(w.wg, w.tg, nullptr, e->pf_act, B, D, 2 * F, e->pf_gu, e->d_err, s, 2 * F));
+        if (tp) {
+            CK(gather(e, e->x_q, B, QD, rk * qd, qd));
+            CK(act_quantize_launch(gq, B, QD, e->pf_actq, s));
+            CK(matbatch_launch(w.wo, w.to, nullptr, e->pf_actq, B, QD, dl, gp + (size_t)rk * dl, e->d_err, s, D));
+            CK(gather(e, e->x_p, B, D, rk * dl, dl));
         } else {
-            CK(matbatch_launch(w.wg, w.tg, nullptr, e->pf_act, B, D, F, e->pf_gu, e->d_err, s, 2 * F));
-            CK(matbatch_launch(w.wu, w.tu, nullptr, e->pf_act, B, D, F, e->pf_gu + F, e->d_err, s, 2 * F));
+            CK(matbatch_launch(w.wo, w.to, nullptr, e->pf_actq, B, QD, D, e->pf_p, e->d_err, s));
         }
-        CK(glu_quant_launch(e->pf_gu, e->pf_gu + F, 2 * F, F, B, e->arch == 2, ActOut{e->pf_actf, nullptr}, s));
-        CK(matbatch_launch(w.wd, w.td, nullptr, e->pf_actf, B, F, D, e->pf_p, e->d_err, s));
+        CK(add_norm_quant_launch(e->pf_h, gp, w.ffn_norm, B, D, e->eps, ActOut{e->pf_act, nullptr}, nullptr, s));
+        if (w.gu_fused) {
+            CK(matbatch_launch(w.wg, w.tg, nullptr, e->pf_act, B, D, 2 * fl, e->pf_gu, e->d_err, s, 2 * fl));
+        } else {
+            CK(matbatch_launch(w.wg, w.tg, nullptr, e->pf_act, B, D, fl, e->pf_gu, e->d_err, s, 2 * fl));
+            CK(matbatch_launch(w.wu, w.tu, nullptr, e->pf_act, B, D, fl, e->pf_gu + fl, e->d_err, s, 2 * fl));
+        }
+        if (tp) {
+            CK(glu_quant_launch(e->pf_gu, e->pf_gu + fl, 2 * fl, fl, B, e->arch == 2, ActOut{nullptr, nullptr}, s,
+                                gf + (size_t)rk * fl, F));
+            CK(gather(e, e->x_f, B, F, rk * fl, fl));
+            CK(act_quantize_launch(gf, B, F, e->pf_actf, s));
+            CK(matbatch_launch(w.wd, w.td, nullptr, e->pf_actf, B, F, dl, gp + (size_t)rk * dl, e->d_err, s, D));
+            CK(gather(e, e->x_p, B, D, rk * dl, dl));
+        } else {
+            CK(glu_quant_launch(e->pf_gu, e->pf_gu + F, 2 * F, F, B, e->arch == 2, ActOut{e->pf_actf, nullptr}, s));
+            CK(matbatch_launch(w.wd, w.td, nullptr, e->pf_actf, B, F, D, e->pf_p, e->d_err, s));
+        }
     }
     // last position: residual, final norm, LM head (:1185-1205)
     const size_t last = (size_t)(B - 1) * D;
     CU(cudaMemcpyAsync(e->hidden, e->pf_h + last, (size_t)D * 4, cudaMemcpyDeviceToDevice, s));
-    CK(add_norm_quant_launch(e->hidden, e->pf_p + last, e->out_norm, 1, D, e->eps, ActOut{nullptr, e->act_d},
-                             e->normed, s));
-    CK(gemv(e, e->tok_embd, e->embd_type, e->act_d, e->normed, D, e->vocab, e->logits, e->softcap));
-    return kOk;
+    CK(add_norm_quant_launch(e->hidden, gp + last, e->out_norm, 1, D, e->eps, ActOut{nullptr, e->act_d}, e->normed,
+                             s));
+    return lm_head(e);
 }
 
 static int upload_ids(Engine* e, const int32_t* ids, int n) {
@@ -433,8 +518,17 @@ static int check_device_error(Engine* e) {
 
 static const LayerW* layer_or_null(const Engine* e, int l) { return l < (int)e->L.size() ? &e->L[l] : nullptr; }
 
-// Load: read hyper-parameters, lay tensors out in one device arena, upload.
-static int engine_load(Engine* e, const char* path, int max_seq, std::string& err) {
+// Rows [r0, r1) of `n` split over `tp` ranks in pieces of `unit` rows (the last
+// rank takes what remains).
+static void split_rows(int n, int tp, int rank, int unit, int& r0, int& r1) {
+    const int per = ((n + tp - 1) / tp + unit - 1) / unit * unit;
+    r0 = rank * per < n ? rank * per : n;
+    r1 = r0 + per < n ? r0 + per : n;
+}
+
+// Load: read hyper-parameters, lay this rank's share of the tensors out in one
+// device arena, upload.
+static int engine_load(Engine* e, const char* path, int max_seq, int tp_rank, int tp_size, std::string& err) {
     Gguf g;
     if (!gguf_open(path, g, err)) return kErrInvalidArg;
     const std::string arch = g.str.count("general.architecture") ? g.str["general.architecture"] : "qwen3";
@@ -466,18 +560,48 @@ static int engine_load(Engine* e, const char* path, int max_seq, std::string& er
         err = "shapes not supported (dims must be multiples of 256, head_dim a multiple of 32 up to 256)";
         return kErrInvalidArg;
     }
+    // ---- this rank's share (tensor parallel: heads, ffn rows, model rows, vocabulary rows)
+    const int tp = tp_size;
+    if (tp < 1 || tp > kTpMaxRanks || tp_rank < 0 || tp_rank >= tp) { err = "bad tensor-parallel rank/size"; return kErrInvalidArg; }
+    if (e->nkv % tp || e->dim % (4 * tp) || e->ffn % (32 * tp)) {
+        err = "tensor parallel size must divide the KV heads, hidden/4 and ffn/32";
+        return kErrInvalidArg;
+    }
+    e->nh_l = e->nh / tp;
+    e->nkv_l = e->nkv / tp;
+    e->qd_l = e->nh_l * e->hd;
+    e->kvd_l = e->nkv_l * e->hd;
+    e->ffn_l = e->ffn / tp;
+    e->dim_l = e->dim / tp;
+    {
+        int v0, v1;
+        split_rows(e->vocab, tp, tp_rank, 4, v0, v1);
+        e->voc0 = v0;
+        e->voc_l = v1 - v0;
+        if (e->voc_l <= 0) { err = "vocabulary too small for the tensor parallel size"; return kErrInvalidArg; }
+    }
     // ---- arena layout
     auto T = [&](const std::string& n) -> const GgufTensor* { auto it = g.tensors.find(n); return it == g.tensors.end() ? nullptr : &it->second; };
-    struct Item { const GgufTensor* t; size_t off; };
+    struct Item { uint64_t src; size_t bytes; size_t off; };
     std::vector<Item> items;
     size_t off = 0;
     auto place = [&](const GgufTensor* t, bool follow) -> size_t {
         if (!follow) off = (off + 255) & ~(size_t)255;
         const size_t o = off;
-        items.push_back({t, o});
+        items.push_back({t->abs_off, t->nbytes, o});
         off += t->nbytes;
         return o;
     };
+    // rows [r0, r1) of a [in, out] weight (rows are contiguous, out of them)
+    auto place_rows = [&](const GgufTensor* t, int r0, int r1, bool follow) -> size_t {
+        if (!follow) off = (off + 255) & ~(size_t)255;
+        const size_t rb = row_bytes(t->type, (int64_t)t->dims[0]);
+        const size_t o = off;
+        items.push_back({t->abs_off + (uint64_t)r0 * rb, (size_t)(r1 - r0) * rb, o});
+        off += (size_t)(r1 - r0) * rb;
+        return o;
+    };
+    const int rk = tp_rank;
     struct Offs { size_t an, fn, qn, kn, q, k, v, o, gt, up, dn; bool has_qn, has_kn, qkv_f, gu_f; int tq, tk, tv, to, tg, tu, td; };
     std::vector<Offs> lo(e->n_layers);
     const char* lin[] = {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"};
@@ -485,9 +609,15 @@ static int engine_load(Engine* e, const char* path, int max_seq, std::string& er
         const std::string p = "blk." + std::to_string(l) + ".";
         const GgufTensor* an = T(p + "attn_norm.weight"), *fn = T(p + "ffn_norm.weight");
         const GgufTensor* lt[7];
+        const uint64_t want_out[7] = {(uint64_t)e->q_dim, (uint64_t)e->kv_dim, (uint64_t)e->kv_dim, (uint64_t)e->dim,
+                                      (uint64_t)e->ffn, (uint64_t)e->ffn, (uint64_t)e->dim};
         for (int i = 0; i < 7; ++i) {
             lt[i] = T(p + lin[i] + ".weight");
             if (!lt[i]) { err = "missing tensor " + p + lin[i] + ".weight"; return kErrInvalidArg; }
+            if (lt[i]->dims.size() != 2 || lt[i]->dims[1] != want_out[i]) {
+                err = "unexpected shape of " + p + lin[i] + ".weight";
+                return kErrInvalidArg;
+            }
             const int ty = lt[i]->type;
             if (ty != kQ4_0 && ty != kQ8_0 && ty != kQ4_K && ty != kQ6_K) { err = "unsupported weight type in " + p + lin[i]; return kErrInvalidArg; }
         }
@@ -501,14 +631,14 @@ static int engine_load(Engine* e, const char* path, int max_seq, std::string& er
         O.qn = O.has_qn ? place(qn, false) : 0;
         O.kn = O.has_kn ? place(kn, false) : 0;
         O.qkv_f = lt[0]->type == lt[1]->type && lt[1]->type == lt[2]->type;
-        O.q = place(lt[0], false);
-        O.k = place(lt[1], O.qkv_f);
-        O.v = place(lt[2], O.qkv_f);
-        O.o = place(lt[3], false);
+        O.q = place_rows(lt[0], rk * e->qd_l, (rk + 1) * e->qd_l, false);
+        O.k = place_rows(lt[1], rk * e->kvd_l, (rk + 1) * e->kvd_l, O.qkv_f);
+        O.v = place_rows(lt[2], rk * e->kvd_l, (rk + 1) * e->kvd_l, O.qkv_f);
+        O.o = place_rows(lt[3], rk * e->dim_l, (rk + 1) * e->dim_l, false);
         O.gu_f = lt[4]->type == lt[5]->type;
-        O.gt = place(lt[4], false);
-        O.up = place(lt[5], O.gu_f);
-        O.dn = place(lt[6], false);
+        O.gt = place_rows(lt[4], rk * e->ffn_l, (rk + 1) * e->ffn_l, false);
+        O.up = place_rows(lt[5], rk * e->ffn_l, (rk + 1) * e->ffn_l, O.gu_f);
+        O.dn = place_rows(lt[6], rk * e->dim_l, (rk + 1) * e->dim_l, false);
         O.tq = lt[0]->type; O.tk = lt[1]->type; O.tv = lt[2]->type; O.to = lt[3]->type;
         O.tg = lt[4]->type; O.tu = lt[5]->type; O.td = lt[6]->type;
     }
@@ -525,12 +655,12 @@ static int engine_load(Engine* e, const char* path, int max_seq, std::string& er
     e->arena_bytes = (off + 255) & ~(size_t)255;
     CU(cudaMalloc(&e->arena, e->arena_bytes));
     for (const Item& it : items)
-        CU(cudaMemcpyAsync(e->arena + it.off, g.base + it.t->abs_off, it.t->nbytes, cudaMemcpyHostToDevice, e->stream));
+        CU(cudaMemcpyAsync(e->arena + it.off, g.base + it.src, it.bytes, cudaMemcpyHostToDevice, e->stream));
     CU(cudaStreamSynchronize(e->stream));
     e->tok_embd = e->arena + emb_off;
     e->out_norm = reinterpret_cast<const float*>(e->arena + on_off);
     // ---- KV cache
-    const size_t kv_layer = (size_t)max_seq * e->kv_dim;
+    const size_t kv_layer = (size_t)max_seq * e->kvd_l;  // this rank's KV heads
     CU(cudaMalloc(&e->kv, kv_layer * 2 * e->n_layers * 4));
     CU(cudaMemsetAsync(e->kv, 0, kv_layer * 2 * e->n_layers * 4, e->stream));
     e->L.resize(e->n_layers);
@@ -571,14 +701,30 @@ static int engine_load(Engine* e, const char* path, int max_seq, std::string& er
     CU(cudaMalloc(&e->hidden, D * 4));
     CU(cudaMalloc(&e->normed, D * 4));
     CU(cudaMalloc(&e->proj, D * 4));
-    CU(cudaMalloc(&e->qkv, (size_t)(e->q_dim + 2 * e->kv_dim) * 4));
-    CU(cudaMalloc(&e->gu, 2 * F * 4));
-    CU(cudaMalloc(&e->logits, (size_t)e->vocab * 4));
+    CU(cudaMalloc(&e->qkv, (size_t)(e->qd_l + 2 * e->kvd_l) * 4));
+    CU(cudaMalloc(&e->gu, 2 * (size_t)e->ffn_l * 4));
+    // ---- exchange region (tensor parallel): gather buffers for up to x_rows prompt rows
+    {
+        e->x_rows = max_seq < kTpMaxRows ? max_seq : kTpMaxRows;
+        const size_t R = tp > 1 ? (size_t)e->x_rows : 0;
+        e->x_q = 0;
+        e->x_p = e->x_q + R * e->q_dim * 4;
+        e->x_f = e->x_p + R * D * 4;
+        e->x_l = e->x_f + R * F * 4;
+        const int st = tp_alloc(e->tp, tp_rank, tp, tp > 1 ? e->x_l + (size_t)e->vocab * 4 : 0);
+        if (st != kOk) return st;
+    }
+    if (tp > 1) {
+        e->logits = tp_buffer(e->tp, e->x_l);
+    } else {
+        CU(cudaMalloc(&e->logits_own, (size_t)e->vocab * 4));
+        e->logits = e->logits_own;
+    }
     CU(cudaMalloc(&e->act_d, staged_act_bytes(D)));
     CU(cudaMalloc(&e->act_q, staged_act_bytes(e->q_dim)));
     CU(cudaMalloc(&e->act_f, staged_act_bytes(F)));
-    CU(cudaMalloc(&e->part, (size_t)e->nh * e->max_splits * attn_record_floats(e->hd) * 4));
-    CU(cudaMalloc(&e->scores, (size_t)e->nh * e->max_splits * kDecodeChunk * 4));
+    CU(cudaMalloc(&e->part, (size_t)e->nh_l * e->max_splits * attn_record_floats(e->hd) * 4));
+    CU(cudaMalloc(&e->scores, (size_t)e->nh_l * e->max_splits * kDecodeChunk * 4));
     CU(cudaMalloc(&e->st, sizeof(DecodeState)));
     CU(cudaMallocHost(&e->st_host, sizeof(DecodeState)));
     CU(cudaMalloc(&e->am_scratch, argmax_state_scratch_bytes()));
@@ -595,11 +741,12 @@ static void engine_free(Engine* e) {
     if (!e) return;
     if (e->stream) cudaStreamSynchronize(e->stream);
     if (e->graph) cudaGraphExecDestroy(e->graph);
-    void* bufs[] = {e->scores, e->pf_scores, e->arena, e->kv, e->rope_c, e->rope_s, e->hidden, e->normed, e->proj, e->qkv, e->gu, e->logits,
+    void* bufs[] = {e->scores, e->pf_scores, e->arena, e->kv, e->rope_c, e->rope_s, e->hidden, e->normed, e->proj, e->qkv, e->gu, e->logits_own,
                     e->act_d, e->act_q, e->act_f, e->part, e->st, e->am_scratch, e->d_err, e->out_ids, e->ids_dev,
                     e->pf_h, e->pf_p, e->pf_qkv, e->pf_gu, e->pf_part, e->pf_act, e->pf_actq, e->pf_actf};
     for (void* b : bufs)
         if (b) cudaFree(b);
+    tp_free(e->tp);
     if (e->st_host) cudaFreeHost(e->st_host);
     for (auto& ev : e->ev)
         if (ev) cudaEventDestroy(ev);
@@ -640,7 +787,7 @@ using namespace gncx;
 // ---------------------------------------------------------------- C ABI
 extern "C" {
 
-void* gncx_engine_create(const char* gguf_path, int32_t max_seq_len) {
+void* gncx_engine_create_tp(const char* gguf_path, int32_t max_seq_len, int32_t tp_rank, int32_t tp_size) {
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
         cudaGetLastError();
@@ -653,12 +800,32 @@ void* gncx_engine_create(const char* gguf_path, int32_t max_seq_len) {
     }
     std::string err;
     gemv_set_pdl(true);  // engine weights are never written while decoding
-    if (engine_load(e, gguf_path, max_seq_len > 0 ? max_seq_len : 4096, err) != kOk) {
+    if (engine_load(e, gguf_path, max_seq_len > 0 ? max_seq_len : 4096, tp_rank, tp_size, err) != kOk) {
         fprintf(stderr, "gncx_engine_create: %s\n", err.empty() ? "CUDA error" : err.c_str());
         engine_free(e);
         return nullptr;
     }
     return e;
+}
+
+// This rank's exchange-region handle (GNCX_TP_HANDLE_BYTES bytes) for the other ranks.
+int32_t gncx_engine_tp_handle(void* h, void* out) {
+    Engine* e = static_cast<Engine*>(h);
+    if (!e || !out) return kErrInvalidArg;
+    if (e->tp.size == 1) return kOk;
+    return tp_handle(e->tp, out);
+}
+
+// Map every rank's exchange region (handles in rank order); collective in effect:
+// every rank calls it before the first prefill / forward.
+int32_t gncx_engine_tp_connect(void* h, const void* handles) {
+    Engine* e = static_cast<Engine*>(h);
+    if (!e || !handles) return kErrInvalidArg;
+    return tp_connect(e->tp, handles);
+}
+
+void* gncx_engine_create(const char* gguf_path, int32_t max_seq_len) {
+    return gncx_engine_create_tp(gguf_path, max_seq_len, 0, 1);
 }
 
 void gncx_engine_destroy(void* h) { engine_free(static_cast<Engine*>(h)); }
@@ -689,7 +856,7 @@ void* gncx_engine_stream(void* h) { return h ? static_cast<Engine*>(h)->stream :
 // lua/gncx_streamer.lua:759-965: logits of token `id` at position `pos` (host copy if logits_out).
 int32_t gncx_engine_forward_token(void* h, int32_t id, int32_t pos, float* logits_out) {
     Engine* e = static_cast<Engine*>(h);
-    if (!e || id < 0 || id >= e->vocab || pos < 0 || pos >= e->max_seq) return kErrInvalidArg;
+    if (!e || id < 0 || id >= e->vocab || pos < 0 || pos >= e->max_seq || !e->tp.connected) return kErrInvalidArg;
     CK(set_state(e, id, pos, nullptr, 0, -1, 0));
     CK(decode_step(e, false, 1.0));
     if (logits_out) CU(cudaMemcpyAsync(logits_out, e->logits, (size_t)e->vocab * 4, cudaMemcpyDeviceToHost, e->stream));
@@ -699,7 +866,7 @@ int32_t gncx_engine_forward_token(void* h, int32_t id, int32_t pos, float* logit
 // lua/gncx_streamer.lua:968-1208: runs the prompt from position 0, fills the KV cache.
 int32_t gncx_engine_prefill(void* h, const int32_t* ids, int32_t n, float* logits_out) {
     Engine* e = static_cast<Engine*>(h);
-    if (!e || !ids || n <= 0 || n > e->max_seq) return kErrInvalidArg;
+    if (!e || !ids || n <= 0 || n > e->max_seq || !e->tp.connected) return kErrInvalidArg;
     for (int i = 0; i < n; ++i)
         if (ids[i] < 0 || ids[i] >= e->vocab) return kErrInvalidArg;
     CU(cudaEventRecord(e->ev[0], e->stream));

@@ -234,7 +234,7 @@ int qkv_post_launch(float* qkv, int32_t row_stride, int32_t rows, int32_t nh, in
 // ---------------------------------------------------------------- GLU + quantize
 // One warp per 32-output block: out = glu(gate, up), re-quantized for ffn_down.
 __global__ void glu_quant_kernel(const float* __restrict__ g, const float* __restrict__ u, int stride, int ffn,
-                                 int rows, int gelu, ActOut act) {
+                                 int rows, int gelu, ActOut act, float* out, int out_stride) {
     pdl_launch_dependents();
     pdl_wait();
     const int lane = threadIdx.x & 31;
@@ -245,18 +245,19 @@ __global__ void glu_quant_kernel(const float* __restrict__ g, const float* __res
     const int b = (int)(gw % nbf);
     const size_t i = (size_t)r * stride + (size_t)b * 32 + lane;
     const float v = gelu ? geglu1(g[i], u[i]) : swiglu1(g[i], u[i]);
-    act_out_store(act, v, ffn, (size_t)r, b, lane);
+    if (out) out[(size_t)r * out_stride + (size_t)b * 32 + lane] = v;
+    if (act.blocks || act.staged) act_out_store(act, v, ffn, (size_t)r, b, lane);
 }
 
 int glu_quant_launch(const float* g, const float* u, int32_t stride, int32_t ffn, int32_t rows, bool gelu,
-                     ActOut act, cudaStream_t st) {
-    if (!g || !u || (!act.blocks && !act.staged) || ffn <= 0 || (ffn & 31) || rows < 0) return kErrInvalidArg;
+                     ActOut act, cudaStream_t st, float* out, int32_t out_stride) {
+    if (!g || !u || (!act.blocks && !act.staged && !out) || ffn <= 0 || (ffn & 31) || rows < 0) return kErrInvalidArg;
     if (act.staged && (rows != 1 || (ffn & 255) || ((uintptr_t)act.staged & 15))) return kErrInvalidArg;
     if (rows == 0) return kOk;
     const int64_t warps = (int64_t)rows * (ffn >> 5);
     const int64_t blocks = (warps + 7) / 8;
     return launch_k(glu_quant_kernel, dim3((unsigned)blocks), dim3(256), 0, st, g, u, stride, ffn, rows,
-                    gelu ? 1 : 0, act) == cudaSuccess
+                    gelu ? 1 : 0, act, out, out_stride) == cudaSuccess
                ? kOk
                : kErrCuda;
 }

@@ -140,11 +140,44 @@ int qkv_post_launch(float* qkv, int32_t row_stride, int32_t rows, int32_t nh, in
                     const float* q_norm, const float* k_norm, bool do_norm, float eps, const float* cos_tab,
                     const float* sin_tab, int32_t pos0, const int32_t* pos_dev, float* kc, float* vc,
                     int64_t kv_pos_stride, int64_t kv_head_stride, cudaStream_t st);
+// GLU of `rows` rows (gate and up `stride` floats apart between rows) into the
+// re-quantized `act` and/or fp32 `out` (row r at out + r * out_stride).
 int glu_quant_launch(const float* g, const float* u, int32_t stride, int32_t ffn, int32_t rows, bool gelu,
-                     ActOut act, cudaStream_t st);
+                     ActOut act, cudaStream_t st, float* out = nullptr, int32_t out_stride = 0);
 size_t argmax_state_scratch_bytes();
 int argmax_state_launch(const float* logits, int32_t vocab, DecodeState* st, double penalty, int32_t* out_ids,
                         int advance_pos, void* scratch, cudaStream_t s);
+
+// ---- tensor parallelism (tp.cu) ----
+// One exchange region per rank: kTpCtlBytes of control words (the epoch each
+// peer last published, this rank's epoch, a CTA arrival counter), then the
+// gather buffers at byte offsets chosen by the caller.
+constexpr int kTpMaxRanks = 8;
+constexpr int kTpHandleBytes = 64;   // sizeof(cudaIpcMemHandle_t)
+constexpr size_t kTpCtlBytes = 256;
+constexpr int kTpEpoch = kTpMaxRanks;
+constexpr int kTpArrive = kTpMaxRanks + 1;
+constexpr int kTpInfo = kTpMaxRanks + 2;   // 5 words: magic, bytes (lo, hi), rank, size
+constexpr uint32_t kTpMagic = 0x58544e47u;
+struct TpComm {
+    int rank = 0, size = 1;
+    bool connected = false;
+    uint8_t* local = nullptr;             // this rank's region
+    size_t bytes = 0;
+    uint8_t* region[kTpMaxRanks] = {};    // every rank's region mapped here (region[rank] == local)
+};
+int tp_alloc(TpComm& c, int rank, int size, size_t bytes);
+int tp_handle(const TpComm& c, void* out);          // kTpHandleBytes
+int tp_connect(TpComm& c, const void* handles);     // size x kTpHandleBytes, in rank order
+void tp_free(TpComm& c);
+// The float buffer at byte offset `buf` of the data area, in this rank's region.
+inline float* tp_buffer(const TpComm& c, size_t buf) { return reinterpret_cast<float*>(c.local + kTpCtlBytes + buf); }
+// All-gather of `rows` rows of `row_floats` floats: this rank supplies floats
+// [off, off + len) of every row (already in its own buffer); afterwards every
+// rank's buffer holds every rank's slices.  A peer that does not arrive within
+// 2 s records kErrTimeout in *err.
+int tp_gather_launch(const TpComm& c, size_t buf, int32_t rows, int32_t row_floats, int32_t off, int32_t len,
+                     int32_t* err, cudaStream_t st);
 
 // ---- embedding ----
 int embed_launch(const uint8_t* tensor, int32_t type, const int32_t* tokens, int32_t n_tokens, int32_t dim,

@@ -1,0 +1,200 @@
+// tp.cu -- tensor-parallel exchange between the GPUs of one NVLink/NVSwitch box.
+//
+// The decoder is split Megatron-style with every output element computed whole
+// on one GPU (q/k/v, attention heads, gate/up, attn_output, ffn_down and the
+// LM head are all split by output rows), so after each split GEMV or attention
+// the ranks all-gather the pieces of one fp32 vector.  The all-gather is this
+// file's own kernel over peer memory: each rank owns one exchange region
+// (cudaMalloc, shared with the other processes through CUDA IPC handles); a
+// rank writes its slice straight into every peer's region with NVLink stores,
+// then publishes an epoch number in each peer's control words, then waits
+// (bounded) for every peer's epoch in its own.
+//
+// Why no buffer is overwritten while a peer still reads it: the exchange
+// points of a step alternate between buffers, and a rank can only write the
+// next use of a buffer into a peer after it has seen that peer's epoch for a
+// later exchange, which the peer publishes after the kernels that read the
+// buffer have finished (stream order).
+#include <cuda_runtime.h>
+#include <string.h>
+
+#include "kernels.h"
+#include "launch.cuh"
+#include "tma.cuh"
+
+namespace gncx {
+
+namespace {
+
+constexpr int kTpThreads = 256;
+constexpr unsigned long long kTpWaitNs = 2000000000ull;  // 2 s: a peer that never arrives is an error
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+struct GatherArgs {
+    uint8_t* region[kTpMaxRanks];  // every rank's exchange region as mapped in this process
+    int rank, size;
+    size_t buf;                    // byte offset of the gathered buffer within a region
+    int rows, row_floats;          // rows x row_floats floats
+    int off, len;                  // this rank's slice of every row
+    int32_t* err;
+};
+
+// Copy this rank's slice into every peer, then the last CTA to finish
+// publishes the epoch to every peer and waits for theirs.
+__global__ void __launch_bounds__(kTpThreads) tp_gather_kernel(const GatherArgs a) {
+    pdl_wait();  // the slice comes from the preceding kernel
+    const float* src = reinterpret_cast<const float*>(a.region[a.rank] + a.buf);
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    if (((a.off | a.len | a.row_floats) & 3) == 0) {
+        const int l4 = a.len >> 2;
+        const size_t total = (size_t)a.rows * l4;
+        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+            const size_t r = i / l4, c = i - r * l4;
+            const size_t o = r * a.row_floats + a.off + 4 * c;
+            const float4 v = *reinterpret_cast<const float4*>(src + o);
+            for (int q = 0; q < a.size; ++q)
+                if (q != a.rank) *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.region[q] + a.buf) + o) = v;
+        }
+    } else {
+        const size_t total = (size_t)a.rows * a.len;
+        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+            const size_t r = i / a.len, c = i - r * a.len;
+            const size_t o = r * a.row_floats + a.off + c;
+            const float v = src[o];
+            for (int q = 0; q < a.size; ++q)
+                if (q != a.rank) reinterpret_cast<float*>(a.region[q] + a.buf)[o] = v;
+        }
+    }
+    __threadfence_system();  // this thread's peer stores before the CTA's arrival
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    uint32_t* ctl = reinterpret_cast<uint32_t*>(a.region[a.rank]);
+    if (atomicAdd(&ctl[kTpArrive], 1u) != gridDim.x - 1) return;
+    // Last CTA: every CTA fenced its stores before arriving.
+    __threadfence_system();
+    ctl[kTpArrive] = 0u;
+    const uint32_t ep = ctl[kTpEpoch] + 1u;
+    ctl[kTpEpoch] = ep;
+    for (int q = 0; q < a.size; ++q)
+        if (q != a.rank) st_release_sys(reinterpret_cast<uint32_t*>(a.region[q]) + a.rank, ep);
+    if (*(volatile int32_t*)a.err != 0) return;  // a rank already gave up: do not wait again
+    const unsigned long long t0 = global_ns();
+    for (int q = 0; q < a.size; ++q) {
+        if (q == a.rank) continue;
+        while ((int32_t)(ld_acquire_sys(ctl + q) - ep) < 0) {
+            if (global_ns() - t0 > kTpWaitNs) {
+                record_error(a.err, kErrTimeout);
+                return;
+            }
+            __nanosleep(64);
+        }
+    }
+}
+
+}  // namespace
+
+int tp_alloc(TpComm& c, int rank, int size, size_t bytes) {
+    if (size < 1 || size > kTpMaxRanks || rank < 0 || rank >= size) return kErrInvalidArg;
+    c.rank = rank;
+    c.size = size;
+    c.bytes = (bytes + kTpCtlBytes + 255) & ~(size_t)255;
+    if (cudaMalloc(&c.local, c.bytes) != cudaSuccess) {
+        cudaGetLastError();
+        c.local = nullptr;
+        return kErrOutOfMemory;
+    }
+    if (cudaMemset(c.local, 0, c.bytes) != cudaSuccess) return kErrCuda;
+    // layout words, checked by every peer before it writes into this region
+    const uint32_t info[5] = {kTpMagic, (uint32_t)c.bytes, (uint32_t)((uint64_t)c.bytes >> 32), (uint32_t)rank,
+                              (uint32_t)size};
+    if (cudaMemcpy(reinterpret_cast<uint32_t*>(c.local) + kTpInfo, info, sizeof(info), cudaMemcpyHostToDevice) !=
+            cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess)
+        return kErrCuda;
+    for (auto& p : c.region) p = nullptr;
+    c.region[rank] = c.local;
+    c.connected = size == 1;
+    return kOk;
+}
+
+int tp_handle(const TpComm& c, void* out) {
+    if (!c.local || !out) return kErrInvalidArg;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, c.local) != cudaSuccess) return kErrCuda;
+    static_assert(sizeof(h) == kTpHandleBytes, "IPC handle size");
+    memcpy(out, &h, sizeof(h));
+    return kOk;
+}
+
+int tp_connect(TpComm& c, const void* handles) {
+    if (!c.local || !handles) return kErrInvalidArg;
+    if (c.connected) return kOk;
+    for (int q = 0; q < c.size; ++q) {
+        if (q == c.rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)q * kTpHandleBytes, sizeof(h));
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            return kErrCuda;
+        }
+        c.region[q] = static_cast<uint8_t*>(p);
+        // The peer's region must have this region's size and belong to rank q
+        // of the same group: the gather writes at this region's offsets.
+        uint32_t info[5] = {};
+        if (cudaMemcpy(info, static_cast<uint32_t*>(p) + kTpInfo, sizeof(info), cudaMemcpyDeviceToHost) !=
+            cudaSuccess)
+            return kErrCuda;
+        const uint64_t bytes = (uint64_t)info[1] | ((uint64_t)info[2] << 32);
+        if (info[0] != kTpMagic || bytes != c.bytes || info[3] != (uint32_t)q || info[4] != (uint32_t)c.size)
+            return kErrInvalidArg;
+    }
+    c.connected = true;
+    return kOk;
+}
+
+void tp_free(TpComm& c) {
+    for (int q = 0; q < kTpMaxRanks; ++q)
+        if (q != c.rank && c.region[q]) cudaIpcCloseMemHandle(c.region[q]);
+    if (c.local) cudaFree(c.local);
+    c = TpComm{};
+}
+
+int tp_gather_launch(const TpComm& c, size_t buf, int32_t rows, int32_t row_floats, int32_t off, int32_t len,
+                     int32_t* err, cudaStream_t st) {
+    if (c.size == 1) return kOk;
+    if (!c.connected || rows < 0 || off < 0 || len < 0 || off + len > row_floats || !err) return kErrInvalidArg;
+    if (rows == 0) return kOk;
+    GatherArgs a{};
+    for (int q = 0; q < kTpMaxRanks; ++q) a.region[q] = c.region[q];
+    a.rank = c.rank;
+    a.size = c.size;
+    a.buf = buf + kTpCtlBytes;
+    a.rows = rows;
+    a.row_floats = row_floats;
+    a.off = off;
+    a.len = len;
+    a.err = err;
+    const size_t items = (size_t)rows * ((len + 3) / 4);
+    size_t blocks = (items + kTpThreads - 1) / kTpThreads;
+    const size_t cap = (size_t)device_info().sm_count * 2;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    return launch_k(tp_gather_kernel, dim3((unsigned)blocks), dim3(kTpThreads), 0, st, a) == cudaSuccess ? kOk
+                                                                                                        : kErrCuda;
+}
+
+}  // namespace gncx

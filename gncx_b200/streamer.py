@@ -15,16 +15,48 @@ import numpy as np
 from . import core
 
 
+TP_HANDLE_BYTES = 64
+
+
+def torch_exchange(blob: bytes) -> list:
+    """All ranks' `blob`s in rank order over the default torch.distributed group."""
+    import torch.distributed as dist
+    out = [None] * dist.get_world_size()
+    dist.all_gather_object(out, blob)
+    return out
+
+
 class GNCXStreamer:
+    """tp_size > 1: this process is rank tp_rank of a tensor-parallel engine on
+    the current (or `device`) GPU; `exchange(bytes) -> [bytes per rank]` passes
+    the exchange-region handles between the ranks (default: torch.distributed)."""
+
     def __init__(self, model_path: str | Path, max_seq_len: int = 4096, device: int | None = None,
-                 exact_attention: bool = False):
+                 exact_attention: bool = False, tp_rank: int = 0, tp_size: int = 1, exchange=None):
         self.lib = core.load()
         if device is not None:
             if self.lib.gncx_set_device(int(device)) != 0:
                 core.check(self.lib)
-        self.handle = self.lib.gncx_engine_create(str(model_path).encode(), int(max_seq_len))
+        self.tp_rank, self.tp_size = int(tp_rank), int(tp_size)
+        self.handle = self.lib.gncx_engine_create_tp(str(model_path).encode(), int(max_seq_len), self.tp_rank,
+                                                     self.tp_size)
         if not self.handle:
             raise core.GncxError(1, f"could not load {model_path} on the GPU (see stderr)")
+        if self.tp_size > 1:
+            mine = (ctypes.c_uint8 * TP_HANDLE_BYTES)()
+            self._check(self.lib.gncx_engine_tp_handle(self.handle, mine))
+            blobs = (exchange or torch_exchange)(bytes(mine))
+            if len(blobs) != self.tp_size or any(len(b) != TP_HANDLE_BYTES for b in blobs):
+                raise core.GncxError(1, "tensor-parallel handle exchange returned the wrong number of handles")
+            allh = (ctypes.c_uint8 * (TP_HANDLE_BYTES * self.tp_size)).from_buffer_copy(b"".join(blobs))
+            st = self.lib.gncx_engine_tp_connect(self.handle, allh)
+            # all ranks connect or none does: no rank may write into a peer that gave up
+            oks = (exchange or torch_exchange)(bytes([st == 0]))
+            if st or not all(b == b"\x01" for b in oks):
+                msg = (self.lib.gncx_engine_error(self.handle) or b"").decode()
+                self.close()
+                raise core.GncxError(st or 1, "tensor-parallel connect failed on " +
+                                     ("this rank: " + msg if st else "another rank"))
         hp = (ctypes.c_int32 * 12)()
         self.lib.gncx_engine_hparams(self.handle, hp)
         (self.n_layers, self.embed_dim, self.n_heads, self.n_kv_heads, self.head_dim, self.ffn_dim, self.vocab_size,

@@ -229,6 +229,24 @@ int32_t gncx_engine_generate(void* engine, const int32_t* prompt, int32_t n_prom
 /* Device time (ms) of the last prefill and decode loop, and the decode step count. */
 int32_t gncx_engine_timing(void* engine, double* prefill_ms, double* decode_ms, int32_t* decode_steps);
 
+/* Tensor parallel over the GPUs of one box (no counterpart in the reference),
+ * one process per GPU, each on its own current device.  Rank r of tp_size
+ * loads its share: attention heads (q/k/v rows and its KV heads), ffn
+ * gate/up rows, attn_output / ffn_down output rows and LM-head vocabulary
+ * rows.  Every output element is computed whole on one GPU, in the 1-GPU
+ * order, so logits and token streams equal the 1-GPU engine's.  After the
+ * split steps the ranks all-gather over NVLink peer memory.  tp_size <= 8 and
+ * must divide the KV heads, hidden/4 and ffn/32.  Set-up: each rank creates
+ * its engine, passes gncx_engine_tp_handle's bytes to the others (any host
+ * channel), and calls gncx_engine_tp_connect with all ranks' handles in rank
+ * order; then every rank makes the same prefill / forward / generate calls.
+ * A peer that stops arriving makes the others' calls fail with
+ * GNCX_ERR_TIMEOUT after 2 s instead of hanging. */
+#define GNCX_TP_HANDLE_BYTES 64
+void* gncx_engine_create_tp(const char* gguf_path, int32_t max_seq_len, int32_t tp_rank, int32_t tp_size);
+int32_t gncx_engine_tp_handle(void* engine, void* out /* GNCX_TP_HANDLE_BYTES */);
+int32_t gncx_engine_tp_connect(void* engine, const void* handles /* tp_size * GNCX_TP_HANDLE_BYTES */);
+
 
 #ifdef __cplusplus
 }
