@@ -280,6 +280,48 @@ def decode_bench(args, torch) -> dict:
     return res
 
 
+def tp_decode_bench(args, torch, dist, rank: int, world: int, local: int) -> dict:
+    """Configuration 5 tensor-parallel over the `world` GPUs of this job: every
+    rank loads its row share of the same random-init 8B-shaped model and the
+    ranks all-gather over NVLink peer memory; device time, max over ranks."""
+    import tempfile
+
+    from gncx_b200 import gguf
+    from gncx_b200.streamer import GNCXStreamer
+    tmp = Path(os.environ.get("GNCX_BENCH_DIR", tempfile.gettempdir()))
+    path = tmp / f"gncx_bench_{args.model}_{args.seed}.gguf"
+    t0 = time.time()
+    if rank == 0 and not path.exists():
+        gguf.write_random_model(path, args.model, seed=args.seed)
+    dist.barrier()
+    write_s = time.time() - t0
+    prompt = np.random.default_rng(args.seed).integers(0, 151936, args.prompt).tolist()
+
+    def exchange(blob: bytes) -> list:
+        out = [None] * world
+        dist.all_gather_object(out, blob)
+        return out
+
+    eng = GNCXStreamer(path, max_seq_len=args.prompt + args.new_tokens, device=local, tp_rank=rank, tp_size=world,
+                       exchange=exchange)
+    try:
+        eng.generate_ids(prompt[:64], 8, eos_id=-1)  # warm-up (graph capture)
+        ids = eng.generate_ids(prompt, args.new_tokens, eos_id=-1)
+        t = eng.timing()
+    finally:
+        dist.barrier()  # no rank unmaps its exchange region while another may still write into it
+        eng.close()
+    tt = torch.tensor([t["decode_ms"], t["prefill_ms"]], device="cuda", dtype=torch.float64)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    decode_ms, prefill_ms = tt.tolist()
+    steps = max(1, t["decode_steps"])
+    return {"model": args.model, "prompt": args.prompt, "new_tokens": args.new_tokens, "weights": "Q4_K, Q6_K head",
+            "model_write_s": round(write_s, 1), "tensor_parallel": world,
+            "split_kv": {"decode_tok_s": steps / (decode_ms / 1e3), "ms_per_token": decode_ms / steps,
+                         "prefill_tok_s": args.prompt / (prefill_ms / 1e3), "prefill_ms": prefill_ms,
+                         "tokens": len(ids), "first_ids": ids[:8], "timing": "device, max over ranks"}}
+
+
 def run_gpu(args) -> None:
     import torch
     rank, world, local = dist_env()
@@ -380,6 +422,14 @@ def run_gpu(args) -> None:
     if pg:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
     ms, e2e_ms, big_ms = t.tolist()
+    tp_decode = None
+    if pg and not args.no_decode:  # every rank takes part in the tensor-parallel decode
+        del weights
+        torch.cuda.empty_cache()
+        try:
+            tp_decode = tp_decode_bench(args, torch, pg, rank, world, local)
+        except Exception as exc:  # reported in the line; the GEMV numbers stand
+            tp_decode = {"error": f"{type(exc).__name__}: {exc}"[:300]}
 
     if rank == 0:
         peaks = measured_peaks()
@@ -414,7 +464,9 @@ def run_gpu(args) -> None:
         if not args.no_sweep:
             lib.gncx_set_weight_prefetch(0)  # each sweep entry is timed alone
             line["sweep"] = format_sweep(torch, lib, P)
-        if not args.no_decode:
+        if tp_decode is not None:
+            line["decode"] = tp_decode
+        elif not args.no_decode:
             del weights
             torch.cuda.empty_cache()
             line["decode"] = decode_bench(args, torch)

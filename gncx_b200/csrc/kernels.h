@@ -149,16 +149,18 @@ int argmax_state_launch(const float* logits, int32_t vocab, DecodeState* st, dou
                         int advance_pos, void* scratch, cudaStream_t s);
 
 // ---- tensor parallelism (tp.cu) ----
-// One exchange region per rank: kTpCtlBytes of control words (the epoch each
-// peer last published, this rank's epoch, a CTA arrival counter), then the
-// gather buffers at byte offsets chosen by the caller.
+// One exchange region per rank: kTpCtlBytes of control words, then the gather
+// buffers at byte offsets chosen by the caller.  Control words: flags
+// [kTpMaxRanks][kTpMaxCtas] (the epoch CTA c of rank q last published here),
+// this rank's epoch per gather CTA, and the layout words peers check.
 constexpr int kTpMaxRanks = 8;
-constexpr int kTpHandleBytes = 64;   // sizeof(cudaIpcMemHandle_t)
-constexpr size_t kTpCtlBytes = 256;
-constexpr int kTpEpoch = kTpMaxRanks;
-constexpr int kTpArrive = kTpMaxRanks + 1;
-constexpr int kTpInfo = kTpMaxRanks + 2;   // 5 words: magic, bytes (lo, hi), rank, size
+constexpr int kTpMaxCtas = 64;        // CTAs of one gather launch
+constexpr int kTpHandleBytes = 64;    // sizeof(cudaIpcMemHandle_t)
+constexpr size_t kTpCtlBytes = 4096;
+constexpr int kTpEpochs = kTpMaxRanks * kTpMaxCtas;
+constexpr int kTpInfo = kTpEpochs + kTpMaxCtas;  // 5 words: magic, bytes (lo, hi), rank, size
 constexpr uint32_t kTpMagic = 0x58544e47u;
+static_assert((kTpInfo + 5) * 4 <= (int)kTpCtlBytes, "control words fit");
 struct TpComm {
     int rank = 0, size = 1;
     bool connected = false;

@@ -52,54 +52,54 @@ struct GatherArgs {
     int32_t* err;
 };
 
-// Copy this rank's slice into every peer, then the last CTA to finish
-// publishes the epoch to every peer and waits for theirs.
+// CTA c copies its share of this rank's slice into every peer, then tells
+// each peer "CTA c of rank r is done" (flags[r][c] = its epoch) and waits
+// until CTA c of every peer has told it the same.  Every rank launches the
+// same grid for the same gather, so when all CTAs are through, every peer's
+// slice has landed here.  No cross-CTA counter, one system fence per CTA.
 __global__ void __launch_bounds__(kTpThreads) tp_gather_kernel(const GatherArgs a) {
-    pdl_wait();  // the slice comes from the preceding kernel
+    pdl_launch_dependents();  // the next kernel may start streaming its weights
+    pdl_wait();               // the slice comes from the preceding kernel
     const float* src = reinterpret_cast<const float*>(a.region[a.rank] + a.buf);
-    const size_t stride = (size_t)gridDim.x * blockDim.x;
-    if (((a.off | a.len | a.row_floats) & 3) == 0) {
-        const int l4 = a.len >> 2;
-        const size_t total = (size_t)a.rows * l4;
-        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-            const size_t r = i / l4, c = i - r * l4;
+    const bool vec = ((a.off | a.len | a.row_floats) & 3) == 0;
+    const int per_row = vec ? a.len >> 2 : a.len;
+    const size_t items = (size_t)a.rows * per_row;
+    const size_t per_cta = (items + gridDim.x - 1) / gridDim.x;
+    const size_t i0 = (size_t)blockIdx.x * per_cta;
+    const size_t i1 = i0 + per_cta < items ? i0 + per_cta : items;
+    for (size_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+        const size_t r = i / per_row, c = i - r * per_row;
+        if (vec) {
             const size_t o = r * a.row_floats + a.off + 4 * c;
             const float4 v = *reinterpret_cast<const float4*>(src + o);
             for (int q = 0; q < a.size; ++q)
                 if (q != a.rank) *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.region[q] + a.buf) + o) = v;
-        }
-    } else {
-        const size_t total = (size_t)a.rows * a.len;
-        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-            const size_t r = i / a.len, c = i - r * a.len;
+        } else {
             const size_t o = r * a.row_floats + a.off + c;
             const float v = src[o];
             for (int q = 0; q < a.size; ++q)
                 if (q != a.rank) reinterpret_cast<float*>(a.region[q] + a.buf)[o] = v;
         }
     }
-    __threadfence_system();  // this thread's peer stores before the CTA's arrival
     __syncthreads();
     if (threadIdx.x != 0) return;
+    __threadfence_system();  // the CTA's peer stores (ordered before by the barrier) before its flags
     uint32_t* ctl = reinterpret_cast<uint32_t*>(a.region[a.rank]);
-    if (atomicAdd(&ctl[kTpArrive], 1u) != gridDim.x - 1) return;
-    // Last CTA: every CTA fenced its stores before arriving.
-    __threadfence_system();
-    ctl[kTpArrive] = 0u;
-    const uint32_t ep = ctl[kTpEpoch] + 1u;
-    ctl[kTpEpoch] = ep;
+    const int cta = blockIdx.x;
+    const uint32_t ep = ctl[kTpEpochs + cta] + 1u;
+    ctl[kTpEpochs + cta] = ep;
     for (int q = 0; q < a.size; ++q)
-        if (q != a.rank) st_release_sys(reinterpret_cast<uint32_t*>(a.region[q]) + a.rank, ep);
+        if (q != a.rank) st_release_sys(reinterpret_cast<uint32_t*>(a.region[q]) + a.rank * kTpMaxCtas + cta, ep);
     if (*(volatile int32_t*)a.err != 0) return;  // a rank already gave up: do not wait again
     const unsigned long long t0 = global_ns();
     for (int q = 0; q < a.size; ++q) {
         if (q == a.rank) continue;
-        while ((int32_t)(ld_acquire_sys(ctl + q) - ep) < 0) {
+        const uint32_t* f = ctl + q * kTpMaxCtas + cta;
+        while ((int32_t)(ld_acquire_sys(f) - ep) < 0) {
             if (global_ns() - t0 > kTpWaitNs) {
                 record_error(a.err, kErrTimeout);
                 return;
             }
-            __nanosleep(64);
         }
     }
 }
@@ -188,10 +188,10 @@ int tp_gather_launch(const TpComm& c, size_t buf, int32_t rows, int32_t row_floa
     a.off = off;
     a.len = len;
     a.err = err;
+    // one CTA per 1024 float4 (each thread moves 4), at most kTpMaxCtas
     const size_t items = (size_t)rows * ((len + 3) / 4);
-    size_t blocks = (items + kTpThreads - 1) / kTpThreads;
-    const size_t cap = (size_t)device_info().sm_count * 2;
-    if (blocks > cap) blocks = cap;
+    size_t blocks = (items + 4 * kTpThreads - 1) / (4 * kTpThreads);
+    if (blocks > (size_t)kTpMaxCtas) blocks = kTpMaxCtas;
     if (blocks < 1) blocks = 1;
     return launch_k(tp_gather_kernel, dim3((unsigned)blocks), dim3(kTpThreads), 0, st, a) == cudaSuccess ? kOk
                                                                                                         : kErrCuda;
