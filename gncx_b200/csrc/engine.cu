@@ -14,11 +14,14 @@
 //   * the KV cache is fp32 like the reference's, laid out head-major
 //     [n_kv][max_seq][head_dim] so a run of positions of one head is contiguous
 //     (one bulk copy per attention chunk);
-//   * tensor parallel (one process per GPU): every linear layer and the
-//     attention heads are split by output rows, so each output element is
-//     computed whole on one GPU in the 1-GPU order and the token stream is the
-//     same; the ranks all-gather (tp.cu) the attention output, the
-//     attn_output and ffn_down results, the GLU output and the logits.
+//   * tensor parallel (one process per GPU): q/k/v with the attention heads,
+//     gate/up and the LM head are split by output rows, so each output
+//     element is computed whole on one GPU in the 1-GPU order and the token
+//     stream is the same.  Decode all-gathers (tp.cu) the attention output
+//     and the GLU output, then every rank computes all of attn_output and
+//     ffn_down (two exchanges per layer, at those two boundaries); prefill,
+//     which is compute-bound, splits those two by rows as well and gathers
+//     their results.  The logits are gathered once per token.
 #include <cuda_runtime.h>
 #include <fcntl.h>
 #include <math.h>
@@ -265,12 +268,12 @@ static int gather(Engine* e, size_t buf, int rows, int row_floats, int off, int 
 static int decode_step(Engine* e, bool sample, double penalty) {
     cudaStream_t s = e->stream;
     const int D = e->dim, QD = e->q_dim, F = e->ffn;
-    const int qd = e->qd_l, kvd = e->kvd_l, fl = e->ffn_l, dl = e->dim_l;
+    const int qd = e->qd_l, kvd = e->kvd_l, fl = e->ffn_l;
     const int qkv_w = qd + 2 * kvd;
     const bool tp = e->tp.size > 1;
     const int rk = e->tp.rank;
     float* gq = tp ? tp_buffer(e->tp, e->x_q) : nullptr;  // attention output (gathered)
-    float* gp = tp ? tp_buffer(e->tp, e->x_p) : e->proj;  // attn_output / ffn_down result
+    float* gp = e->proj;  // attn_output / ffn_down result (every rank computes all of it)
     float* gf = tp ? tp_buffer(e->tp, e->x_f) : nullptr;  // GLU output (gathered)
     CK(dequant_launch(e->tok_embd, e->embd_type, 1, D, e->embd_scale, &e->st->token, e->hidden, s));
     for (int l = 0; l < e->n_layers; ++l) {
@@ -318,10 +321,9 @@ static int decode_step(Engine* e, bool sample, double penalty) {
         a.scores = e->scores;
         a.score_cap = e->max_splits * kDecodeChunk;
         CK(attention_run(a, 1, s));
-        if (tp) {
+        if (tp) {  // gather the heads, then the whole attn_output on every rank
             CK(gather(e, e->x_q, 1, QD, rk * qd, qd));
-            CK(gemv_x(e, w.wo, w.to, gq, QD, dl, gp + (size_t)rk * dl));
-            CK(gather(e, e->x_p, 1, D, rk * dl, dl));
+            CK(gemv_x(e, w.wo, w.to, gq, QD, D, e->proj));
         } else {
             CK(gemv(e, w.wo, w.to, e->act_q, nullptr, QD, D, e->proj));
         }
@@ -336,8 +338,7 @@ static int decode_step(Engine* e, bool sample, double penalty) {
             CK(glu_quant_launch(e->gu, e->gu + fl, 2 * fl, fl, 1, e->arch == 2, ActOut{nullptr, nullptr}, s,
                                 gf + (size_t)rk * fl, F));
             CK(gather(e, e->x_f, 1, F, rk * fl, fl));
-            CK(gemv_x(e, w.wd, w.td, gf, F, dl, gp + (size_t)rk * dl));
-            CK(gather(e, e->x_p, 1, D, rk * dl, dl));
+            CK(gemv_x(e, w.wd, w.td, gf, F, D, e->proj));  // the whole ffn_down on every rank
         } else {
             CK(glu_quant_launch(e->gu, e->gu + F, 2 * F, F, 1, e->arch == 2, ActOut{nullptr, e->act_f}, s));
             CK(gemv(e, w.wd, w.td, e->act_f, nullptr, F, D, e->proj));
@@ -443,7 +444,8 @@ static int prefill_batch(Engine* e, int B) {
         if (tp) {
             CK(gather(e, e->x_q, B, QD, rk * qd, qd));
             CK(act_quantize_launch(gq, B, QD, e->pf_actq, s));
-            CK(matbatch_launch(w.wo, w.to, nullptr, e->pf_actq, B, QD, dl, gp + (size_t)rk * dl, e->d_err, s, D));
+            CK(matbatch_launch(w.wo + (size_t)rk * dl * row_bytes(w.to, QD), w.to, nullptr, e->pf_actq, B, QD, dl,
+                               gp + (size_t)rk * dl, e->d_err, s, D));
             CK(gather(e, e->x_p, B, D, rk * dl, dl));
         } else {
             CK(matbatch_launch(w.wo, w.to, nullptr, e->pf_actq, B, QD, D, e->pf_p, e->d_err, s));
@@ -460,7 +462,8 @@ static int prefill_batch(Engine* e, int B) {
                                 gf + (size_t)rk * fl, F));
             CK(gather(e, e->x_f, B, F, rk * fl, fl));
             CK(act_quantize_launch(gf, B, F, e->pf_actf, s));
-            CK(matbatch_launch(w.wd, w.td, nullptr, e->pf_actf, B, F, dl, gp + (size_t)rk * dl, e->d_err, s, D));
+            CK(matbatch_launch(w.wd + (size_t)rk * dl * row_bytes(w.td, F), w.td, nullptr, e->pf_actf, B, F, dl,
+                               gp + (size_t)rk * dl, e->d_err, s, D));
             CK(gather(e, e->x_p, B, D, rk * dl, dl));
         } else {
             CK(glu_quant_launch(e->pf_gu, e->pf_gu + F, 2 * F, F, B, e->arch == 2, ActOut{e->pf_actf, nullptr}, s));
@@ -634,11 +637,14 @@ static int engine_load(Engine* e, const char* path, int max_seq, int tp_rank, in
         O.q = place_rows(lt[0], rk * e->qd_l, (rk + 1) * e->qd_l, false);
         O.k = place_rows(lt[1], rk * e->kvd_l, (rk + 1) * e->kvd_l, O.qkv_f);
         O.v = place_rows(lt[2], rk * e->kvd_l, (rk + 1) * e->kvd_l, O.qkv_f);
-        O.o = place_rows(lt[3], rk * e->dim_l, (rk + 1) * e->dim_l, false);
+        // attn_output and ffn_down whole on every rank: decode computes all their
+        // rows everywhere (two gathers per layer instead of four), prefill this
+        // rank's rows of them (compute-bound there) and gathers
+        O.o = place_rows(lt[3], 0, e->dim, false);
         O.gu_f = lt[4]->type == lt[5]->type;
         O.gt = place_rows(lt[4], rk * e->ffn_l, (rk + 1) * e->ffn_l, false);
         O.up = place_rows(lt[5], rk * e->ffn_l, (rk + 1) * e->ffn_l, O.gu_f);
-        O.dn = place_rows(lt[6], rk * e->dim_l, (rk + 1) * e->dim_l, false);
+        O.dn = place_rows(lt[6], 0, e->dim, false);
         O.tq = lt[0]->type; O.tk = lt[1]->type; O.tv = lt[2]->type; O.to = lt[3]->type;
         O.tg = lt[4]->type; O.tu = lt[5]->type; O.td = lt[6]->type;
     }

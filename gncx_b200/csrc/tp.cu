@@ -1,9 +1,8 @@
 // tp.cu -- tensor-parallel exchange between the GPUs of one NVLink/NVSwitch box.
 //
 // The decoder is split Megatron-style with every output element computed whole
-// on one GPU (q/k/v, attention heads, gate/up, attn_output, ffn_down and the
-// LM head are all split by output rows), so after each split GEMV or attention
-// the ranks all-gather the pieces of one fp32 vector.  The all-gather is this
+// on one GPU (weights split by output rows), so after each split GEMV or
+// attention the ranks all-gather the pieces of one fp32 vector.  The all-gather is this
 // file's own kernel over peer memory: each rank owns one exchange region
 // (cudaMalloc, shared with the other processes through CUDA IPC handles); a
 // rank writes its slice straight into every peer's region with NVLink stores,

@@ -232,10 +232,12 @@ int32_t gncx_engine_timing(void* engine, double* prefill_ms, double* decode_ms, 
 /* Tensor parallel over the GPUs of one box (no counterpart in the reference),
  * one process per GPU, each on its own current device.  Rank r of tp_size
  * loads its share: attention heads (q/k/v rows and its KV heads), ffn
- * gate/up rows, attn_output / ffn_down output rows and LM-head vocabulary
- * rows.  Every output element is computed whole on one GPU, in the 1-GPU
- * order, so logits and token streams equal the 1-GPU engine's.  After the
- * split steps the ranks all-gather over NVLink peer memory.  tp_size <= 8 and
+ * gate/up rows and LM-head vocabulary rows, plus attn_output and ffn_down
+ * whole.  Every output element is computed whole on one GPU, in the 1-GPU
+ * order, so logits and token streams equal the 1-GPU engine's.  Decode
+ * all-gathers over NVLink peer memory at the attention output and the
+ * ffn_down input (then every rank runs attn_output and ffn_down on all rows)
+ * and once for the logits; prefill splits attn_output / ffn_down rows too.  tp_size <= 8 and
  * must divide the KV heads, hidden/4 and ffn/32.  Set-up: each rank creates
  * its engine, passes gncx_engine_tp_handle's bytes to the others (any host
  * channel), and calls gncx_engine_tp_connect with all ranks' handles in rank
