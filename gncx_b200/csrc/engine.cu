@@ -182,6 +182,7 @@ struct Engine {
     TpComm tp;
     int nh_l = 0, nkv_l = 0, qd_l = 0, kvd_l = 0, ffn_l = 0, dim_l = 0, voc0 = 0, voc_l = 0;
     size_t x_q = 0, x_p = 0, x_f = 0, x_l = 0;  // gather buffers (byte offsets in the exchange region)
+    size_t ll_q = 0, ll_f = 0, ll_l = 0;        // one-row (decode) staging areas of the same gathers
     int x_rows = 0;                              // rows each gather buffer holds
     const uint8_t* tok_embd = nullptr;
     int embd_type = 0;
@@ -244,14 +245,23 @@ static int gemv(Engine* e, const uint8_t* w, int t, const uint8_t* act, const fl
                        e->stream);
 }
 
+// Rows [r0, r1) of `n` split over `tp` ranks in pieces of `unit` rows (the last
+// rank takes what remains).
+static void split_rows(int n, int tp, int rank, int unit, int& r0, int& r1) {
+    const int per = ((n + tp - 1) / tp + unit - 1) / unit * unit;
+    r0 = rank * per < n ? rank * per : n;
+    r1 = r0 + per < n ? r0 + per : n;
+}
+
 static int gather(Engine* e, size_t buf, int rows, int row_floats, int off, int len);
+static int gather_row(Engine* e, int slot);
 
 // LM head over this rank's vocabulary rows of the staged act_d, then (tensor
 // parallel) the all-gather that gives every rank all logits.
 static int lm_head(Engine* e) {
     const uint8_t* w = e->tok_embd + (size_t)e->voc0 * row_bytes(e->embd_type, e->dim);
     CK(gemv(e, w, e->embd_type, e->act_d, e->normed, e->dim, e->voc_l, e->logits + e->voc0, e->softcap));
-    return gather(e, e->x_l, 1, e->vocab, e->voc0, e->voc_l);
+    return gather_row(e, 2);  // the logits slot of the one-row gathers
 }
 
 // GEMV whose input is an fp32 vector (re-quantized inside the GEMV).
@@ -261,6 +271,24 @@ static int gemv_x(Engine* e, const uint8_t* w, int t, const float* x, int in, in
 
 static int gather(Engine* e, size_t buf, int rows, int row_floats, int off, int len) {
     return tp_gather_launch(e->tp, buf, rows, row_floats, off, len, e->d_err, e->stream);
+}
+
+// Decode's one-row gathers: attention output, GLU output, logits.
+enum LlSlot { kLlAttn = 0, kLlGlu = 1, kLlLogits = 2 };
+static int gather_row(Engine* e, int slot) {
+    TpSlices sl{};
+    const int n = e->tp.size;
+    size_t buf = 0, ll = 0;
+    int row = 0;
+    for (int q = 0; q < n; ++q) {
+        if (slot == kLlAttn) { sl.off[q] = q * e->qd_l; sl.len[q] = e->qd_l; }
+        else if (slot == kLlGlu) { sl.off[q] = q * e->ffn_l; sl.len[q] = e->ffn_l; }
+        else { int v0, v1; split_rows(e->vocab, n, q, 4, v0, v1); sl.off[q] = v0; sl.len[q] = v1 - v0; }
+    }
+    if (slot == kLlAttn) { buf = e->x_q; ll = e->ll_q; row = e->q_dim; }
+    else if (slot == kLlGlu) { buf = e->x_f; ll = e->ll_f; row = e->ffn; }
+    else { buf = e->x_l; ll = e->ll_l; row = e->vocab; }
+    return tp_gather_ll_launch(e->tp, buf, ll, row, sl, slot, e->d_err, e->stream);
 }
 
 // One decode step: forward(st->token at st->pos) and, if `sample`, the
@@ -322,7 +350,7 @@ static int decode_step(Engine* e, bool sample, double penalty) {
         a.score_cap = e->max_splits * kDecodeChunk;
         CK(attention_run(a, 1, s));
         if (tp) {  // gather the heads, then the whole attn_output on every rank
-            CK(gather(e, e->x_q, 1, QD, rk * qd, qd));
+            CK(gather_row(e, kLlAttn));
             CK(gemv_x(e, w.wo, w.to, gq, QD, D, e->proj));
         } else {
             CK(gemv(e, w.wo, w.to, e->act_q, nullptr, QD, D, e->proj));
@@ -337,7 +365,7 @@ static int decode_step(Engine* e, bool sample, double penalty) {
         if (tp) {
             CK(glu_quant_launch(e->gu, e->gu + fl, 2 * fl, fl, 1, e->arch == 2, ActOut{nullptr, nullptr}, s,
                                 gf + (size_t)rk * fl, F));
-            CK(gather(e, e->x_f, 1, F, rk * fl, fl));
+            CK(gather_row(e, kLlGlu));
             CK(gemv_x(e, w.wd, w.td, gf, F, D, e->proj));  // the whole ffn_down on every rank
         } else {
             CK(glu_quant_launch(e->gu, e->gu + F, 2 * F, F, 1, e->arch == 2, ActOut{nullptr, e->act_f}, s));
@@ -520,14 +548,6 @@ static int check_device_error(Engine* e) {
 }
 
 static const LayerW* layer_or_null(const Engine* e, int l) { return l < (int)e->L.size() ? &e->L[l] : nullptr; }
-
-// Rows [r0, r1) of `n` split over `tp` ranks in pieces of `unit` rows (the last
-// rank takes what remains).
-static void split_rows(int n, int tp, int rank, int unit, int& r0, int& r1) {
-    const int per = ((n + tp - 1) / tp + unit - 1) / unit * unit;
-    r0 = rank * per < n ? rank * per : n;
-    r1 = r0 + per < n ? r0 + per : n;
-}
 
 // Load: read hyper-parameters, lay this rank's share of the tensors out in one
 // device arena, upload.
@@ -717,7 +737,11 @@ static int engine_load(Engine* e, const char* path, int max_seq, int tp_rank, in
         e->x_p = e->x_q + R * e->q_dim * 4;
         e->x_f = e->x_p + R * D * 4;
         e->x_l = e->x_f + R * F * 4;
-        const int st = tp_alloc(e->tp, tp_rank, tp, tp > 1 ? e->x_l + (size_t)e->vocab * 4 : 0);
+        const size_t T = tp > 1 ? (size_t)tp : 0;
+        e->ll_q = e->x_l + (tp > 1 ? (size_t)e->vocab * 4 : 0);
+        e->ll_f = e->ll_q + T * e->q_dim * 8;
+        e->ll_l = e->ll_f + T * F * 8;
+        const int st = tp_alloc(e->tp, tp_rank, tp, e->ll_l + T * e->vocab * 8);
         if (st != kOk) return st;
     }
     if (tp > 1) {

@@ -160,7 +160,10 @@ constexpr size_t kTpCtlBytes = 4096;
 constexpr int kTpEpochs = kTpMaxRanks * kTpMaxCtas;
 constexpr int kTpInfo = kTpEpochs + kTpMaxCtas;  // 5 words: magic, bytes (lo, hi), rank, size
 constexpr uint32_t kTpMagic = 0x58544e47u;
-static_assert((kTpInfo + 5) * 4 <= (int)kTpCtlBytes, "control words fit");
+constexpr int kTpLlSlots = 4;
+constexpr int kTpLlEpochs = 640;  // word offset: [kTpLlSlots][kTpMaxCtas] epochs of the one-row gather
+static_assert(kTpInfo + 5 <= kTpLlEpochs && (kTpLlEpochs + kTpLlSlots * kTpMaxCtas) * 4 <= (int)kTpCtlBytes,
+              "control words fit");
 struct TpComm {
     int rank = 0, size = 1;
     bool connected = false;
@@ -180,6 +183,19 @@ inline float* tp_buffer(const TpComm& c, size_t buf) { return reinterpret_cast<f
 // 2 s records kErrTimeout in *err.
 int tp_gather_launch(const TpComm& c, size_t buf, int32_t rows, int32_t row_floats, int32_t off, int32_t len,
                      int32_t* err, cudaStream_t st);
+// Every rank's slice [off[q], off[q] + len[q]) of one gathered row.
+struct TpSlices {
+    int32_t off[kTpMaxRanks];
+    int32_t len[kTpMaxRanks];
+};
+// One-row all-gather for decode: each value travels with the gather's epoch in
+// one 8-byte store ({value, epoch}) into the peer's staging area at byte
+// offset `ll` (size x row_floats x 8 bytes), and the receiver polls its own
+// staging area until every peer value of this epoch is there -- one NVLink
+// trip, no fence, no separate flag.  slot < kTpLlSlots names the gather (each
+// slot keeps its own epochs; the same slot must always have the same shape).
+int tp_gather_ll_launch(const TpComm& c, size_t buf, size_t ll, int32_t row_floats, const TpSlices& sl, int32_t slot,
+                        int32_t* err, cudaStream_t st);
 
 // ---- embedding ----
 int embed_launch(const uint8_t* tensor, int32_t type, const int32_t* tokens, int32_t n_tokens, int32_t dim,

@@ -103,7 +103,92 @@ __global__ void __launch_bounds__(kTpThreads) tp_gather_kernel(const GatherArgs 
     }
 }
 
+struct LlArgs {
+    uint8_t* region[kTpMaxRanks];
+    int rank, size, slot;
+    size_t buf, ll;  // byte offsets (data area) of the gathered row and of the staging area
+    int row_floats;
+    TpSlices sl;
+    int32_t* err;
+};
+
+__global__ void __launch_bounds__(kTpThreads) tp_ll_gather_kernel(const LlArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();  // this rank's slice comes from the preceding kernel
+    __shared__ uint32_t s_ep;
+    uint32_t* ctl = reinterpret_cast<uint32_t*>(a.region[a.rank]);
+    if (threadIdx.x == 0) {
+        // every CTA of every launch of this slot counts the same launches, so
+        // the epochs agree across CTAs and ranks
+        uint32_t* e = ctl + kTpLlEpochs + a.slot * kTpMaxCtas + blockIdx.x;
+        s_ep = *e + 1u;
+        *e = s_ep;
+    }
+    __syncthreads();
+    const uint32_t ep = s_ep;
+    const int gid = blockIdx.x * blockDim.x + threadIdx.x, stride = gridDim.x * blockDim.x;
+    float* row = reinterpret_cast<float*>(a.region[a.rank] + kTpCtlBytes + a.buf);
+    // send: {value, epoch} words into every peer's staging row of this rank
+    const int o_me = a.sl.off[a.rank], n_me = a.sl.len[a.rank];
+    for (int i = gid; i < n_me; i += stride) {
+        const uint64_t w = ((uint64_t)ep << 32) | __float_as_uint(row[o_me + i]);
+        for (int q = 0; q < a.size; ++q) {
+            if (q == a.rank) continue;
+            uint64_t* dst = reinterpret_cast<uint64_t*>(a.region[q] + kTpCtlBytes + a.ll) +
+                            (size_t)a.rank * a.row_floats + o_me + i;
+            asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst), "l"(w) : "memory");
+        }
+    }
+    // receive: poll this rank's staging rows until each peer value carries the epoch
+    if (*(volatile int32_t*)a.err != 0) return;  // a rank already gave up: do not wait again
+    const unsigned long long t0 = global_ns();
+    const uint64_t* st = reinterpret_cast<const uint64_t*>(a.region[a.rank] + kTpCtlBytes + a.ll);
+    for (int q = 0; q < a.size; ++q) {
+        if (q == a.rank) continue;
+        const int o = a.sl.off[q], n = a.sl.len[q];
+        for (int j = gid; j < n; j += stride) {
+            const uint64_t* p = st + (size_t)q * a.row_floats + o + j;
+            uint64_t w;
+            for (;;) {
+                asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+                if ((uint32_t)(w >> 32) == ep) break;
+                if (global_ns() - t0 > kTpWaitNs) {
+                    record_error(a.err, kErrTimeout);
+                    return;
+                }
+            }
+            row[o + j] = __uint_as_float((uint32_t)w);
+        }
+    }
+}
+
 }  // namespace
+
+int tp_gather_ll_launch(const TpComm& c, size_t buf, size_t ll, int32_t row_floats, const TpSlices& sl, int32_t slot,
+                        int32_t* err, cudaStream_t st) {
+    if (c.size == 1) return kOk;
+    if (!c.connected || !err || slot < 0 || slot >= kTpLlSlots || row_floats <= 0) return kErrInvalidArg;
+    int most = 0;
+    for (int q = 0; q < c.size; ++q) {
+        if (sl.off[q] < 0 || sl.len[q] < 0 || sl.off[q] + sl.len[q] > row_floats) return kErrInvalidArg;
+        most = sl.len[q] > most ? sl.len[q] : most;
+    }
+    LlArgs a{};
+    for (int q = 0; q < kTpMaxRanks; ++q) a.region[q] = c.region[q];
+    a.rank = c.rank;
+    a.size = c.size;
+    a.slot = slot;
+    a.buf = buf;
+    a.ll = ll;
+    a.row_floats = row_floats;
+    a.sl = sl;
+    a.err = err;
+    // one thread per 4 values of the largest slice (a fixed grid per slot shape)
+    int blocks = (most + 4 * kTpThreads - 1) / (4 * kTpThreads);
+    if (blocks > kTpMaxCtas) blocks = kTpMaxCtas;
+    if (blocks < 1) blocks = 1;
+    return launch_k(tp_ll_gather_kernel, dim3(blocks), dim3(kTpThreads), 0, st, a) == cudaSuccess ? kOk : kErrCuda;
+}
 
 int tp_alloc(TpComm& c, int rank, int size, size_t bytes) {
     if (size < 1 || size > kTpMaxRanks || rank < 0 || rank >= size) return kErrInvalidArg;
