@@ -360,7 +360,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
             const float2* ws = stage_ws(s);
             const uint8_t* as = stage_as(s);
             if constexpr (T == kQ4_K) {
-                // per 64-input chunk c: st = (0 + lo) + hi, a half skipped when its act scale is 0 (:1546-1618)
+                // per 64-input chunk c: st = (0 + lo) + hi, a half skipped when its act scale
+                // is 0 (:1546-1618).  Adding such a half instead changes nothing for finite
+                // weight scales: it is a zero whose sign the row accumulator (never -0)
+                // absorbs, so both halves are always added.
 #pragma unroll 1
                 for (int c = 0; c < 4; ++c) {
                     int dl[TN], dh[TN];
@@ -372,10 +375,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
 #pragma unroll
                     for (int t = 0; t < TN; ++t) {
                         const float4 a = a4[t];  // {d_lo, S_lo, d_hi, S_hi}
-                        float st = 0.0f;
-                        if (a.x != 0.0f) st = fadd(st, fmul(a.x, fsub(fmul(w1.x, i2f(dl[t])), fmul(w1.y, a.y))));
-                        if (a.z != 0.0f) st = fadd(st, fmul(a.z, fsub(fmul(w2.x, i2f(dh[t])), fmul(w2.y, a.w))));
-                        acc[t] = fadd(acc[t], st);
+                        const float lo = fmul(a.x, fsub(fmul(w1.x, i2f(dl[t])), fmul(w1.y, a.y)));
+                        const float hi = fmul(a.z, fsub(fmul(w2.x, i2f(dh[t])), fmul(w2.y, a.w)));
+                        acc[t] = fadd(acc[t], fadd(lo, hi));
                     }
                 }
             } else {
@@ -391,9 +393,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
                         const float2 a = a2[t];
                         float term;
                         if constexpr (T == kQ4_0) {
-                            // (float)(dot - 8*sum_q) * (d_w * d_a), 0 when d_a == 0
+                            // (float)(dot - 8*sum_q) * (d_w * d_a); a block with d_a == 0 has a zero
+                            // dot and sum, so it adds +0 like the reference's skip
                             const int folded = dv[t] - 8 * __float2int_rn(a.y);
-                            term = a.x == 0.0f ? 0.0f : fmul(i2f(folded), fmul(wd, a.x));
+                            term = fmul(i2f(folded), fmul(wd, a.x));
                         } else {
                             term = fmul(i2f(dv[t]), fmul(wd, a.x));
                         }
