@@ -32,6 +32,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "launch.cuh"
+#include "norm.cuh"
 
 namespace gncx {
 
@@ -211,6 +212,41 @@ __device__ __forceinline__ void pv_reduce(const float (&acc)[kPvHeads], int ng, 
     __syncthreads();
 }
 
+// One warp: per-head RMSNorm (the reference's four serial fp32 lanes over
+// x[4k+j]^2, combined in double) with gain w (may be null) and rotate-half
+// RoPE at `pos`, in place on x[hd] in shared memory -- the arithmetic of the
+// Q/K post step (csrc/gncx_llm_kernels.cpp:895-953, :1760-1863).
+__device__ __forceinline__ void warp_head_norm_rope(float* x, int hd, const float* __restrict__ w, bool do_norm,
+                                                    float eps, const float* __restrict__ ct,
+                                                    const float* __restrict__ stab, int pos, int lane) {
+    if (do_norm) {
+        const float acc = lane < 4 ? lane_sumsq(x, lane, hd >> 2) : 0.0f;
+        const float a1 = __shfl_sync(0xffffffffu, acc, 1);
+        const float a2 = __shfl_sync(0xffffffffu, acc, 2);
+        const float a3 = __shfl_sync(0xffffffffu, acc, 3);
+        float inv = 0.0f;
+        if (lane == 0) {
+            const double s = __dadd_rn(__dadd_rn(__dadd_rn((double)acc, (double)a1), (double)a2), (double)a3);
+            const float ms = __double2float_rn(__ddiv_rn(s, (double)hd));
+            inv = fdiv(1.0f, __fsqrt_rn(fadd(ms, eps)));
+        }
+        inv = __shfl_sync(0xffffffffu, inv, 0);
+        for (int i = lane; i < hd; i += 32) {
+            const float v = fmul(x[i], inv);
+            x[i] = w ? fmul(v, w[i]) : v;
+        }
+        __syncwarp();
+    }
+    const int half = hd >> 1;
+    for (int i = lane; i < half; i += 32) {
+        const float c = ct[(size_t)pos * half + i], s = stab[(size_t)pos * half + i];
+        const float x1 = x[i], x2 = x[i + half];
+        x[i] = fsub(fmul(x1, c), fmul(x2, s));
+        x[i + half] = fadd(fmul(x2, c), fmul(x1, s));
+    }
+    __syncwarp();
+}
+
 // Partial record per (query, head, split): [0] = max, [1] = sum of exp, [4..] = o[hd]
 template <bool VEC, bool SCORES_ONLY>
 __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnArgs a) {
@@ -266,9 +302,38 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
     };
     if (n_old > 0) stage_rows(0, n_old);
     pdl_wait();
-    if (n_old < cn) stage_rows(n_old, cn);
+    // with the fused post step the query's own row (the last of the window) is
+    // made here, not loaded
+    const int pn = t0 + len - 1 - (t0 + c0);  // the query's position within this chunk
+    const bool own_row = a.post_k && pn >= 0 && pn < cn;
+    if (n_old < cn) stage_rows(n_old, own_row ? pn : cn);
     const float* qz = a.q + (size_t)z * a.q_stride + (size_t)kvh * G * hd;
     for (int i = tid; i < G * hd; i += kAttnThreads) qs[(size_t)(i / hd) * qrs + i % hd] = qz[i];
+    if (a.post_k) {
+        const int pos = t0 + len - 1;
+        if (own_row) {
+            const float* kz = a.post_k + (size_t)kvh * hd;
+            const float* vz = a.post_v + (size_t)kvh * hd;
+            for (int i = tid; i < hd; i += kAttnThreads) {
+                ks[(size_t)pn * rs + i] = kz[i];
+                const float v = vz[i];
+                if (!SCORES_ONLY) vs[(size_t)pn * rs + i] = v;
+                // the cache's new V row (the caches are writable whenever post_k is set)
+                const_cast<float*>(a.vc)[(size_t)pos * ps + (size_t)kvh * a.kv_head_stride + i] = v;
+            }
+        }
+        __syncthreads();
+        // warps 0..G-1: the group's q heads; warp G: the new K row
+        for (int task = warp; task < G + (own_row ? 1 : 0); task += kAttnThreads / 32) {
+            const bool isq = task < G;
+            float* x = isq ? qs + (size_t)task * qrs : ks + (size_t)pn * rs;
+            warp_head_norm_rope(x, hd, isq ? a.post_qn : a.post_kn, a.post_norm != 0, a.post_eps, a.rope_c, a.rope_s,
+                                pos, lane);
+            if (!isq)
+                for (int i = lane; i < hd; i += 32)
+                    const_cast<float*>(a.kc)[(size_t)pos * ps + (size_t)kvh * a.kv_head_stride + i] = x[i];
+        }
+    }
     if (VEC) cp_async_wait<0>();
     __syncthreads();
 
@@ -659,6 +724,7 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
         return kErrInvalidArg;
     const bool act = a.act_out.blocks || a.act_out.staged;
     if (act && a.hd % 32) return kErrInvalidArg;
+    if (a.post_k && (n_tok != 1 || !a.post_v || !a.rope_c || !a.rope_s || (a.hd & 1))) return kErrInvalidArg;
     if (a.act_out.staged && (n_tok != 1 || (a.n_heads * a.hd) % 256 || ((uintptr_t)a.act_out.staged & 15)))
         return kErrInvalidArg;
     const DeviceInfo& dev = device_info();

@@ -315,9 +315,17 @@ static int decode_step(Engine* e, bool sample, double penalty) {
             CK(gemv(e, w.wk, w.tk, e->act_d, e->normed, D, kvd, e->qkv + qd));
             CK(gemv(e, w.wv, w.tv, e->act_d, e->normed, D, kvd, e->qkv + qd + kvd));
         }
-        CK(qkv_post_launch(e->qkv, qkv_w, 1, e->nh_l, e->nkv_l, e->hd, w.q_norm, w.k_norm, e->qk_norm, e->eps,
-                           e->rope_c, e->rope_s, 0, &e->st->pos, w.kc, w.vc, e->hd, (int64_t)e->max_seq * e->hd, s));
+        // the attention kernel itself norms and rotates q and the new K row and
+        // writes the new K/V row to the cache (the Q/K post step, fused)
         AttnArgs a{};
+        a.post_k = e->qkv + qd;
+        a.post_v = e->qkv + qd + kvd;
+        a.post_qn = w.q_norm;
+        a.post_kn = w.k_norm;
+        a.post_norm = e->qk_norm ? 1 : 0;
+        a.post_eps = e->eps;
+        a.rope_c = e->rope_c;
+        a.rope_s = e->rope_s;
         a.q = e->qkv;
         a.q_stride = qkv_w;
         a.kc = w.kc;

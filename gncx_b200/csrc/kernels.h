@@ -100,6 +100,20 @@ struct AttnArgs {
     // preceding kernel ran (single-query decode), so a CTA may load them before
     // its dependency wait under programmatic dependent launch.  0: load nothing early.
     int prefetch_old;
+    // Decode only (one query, window 0): when post_k is set, q is the QKV
+    // GEMV's raw output and the kernel does what the Q/K post step does
+    // otherwise -- per-head RMSNorm (post_norm, gains post_qn / post_kn, may
+    // be null) and RoPE (tables [max_pos][hd/2]) of q, and of the new K row
+    // post_k + kv_head * hd, which it writes with the new V row (post_v) into
+    // the cache at the query's position.
+    const float* post_k;
+    const float* post_v;
+    const float* post_qn;
+    const float* post_kn;
+    int post_norm;
+    float post_eps;
+    const float* rope_c;
+    const float* rope_s;
 };
 int attention_run(const AttnArgs& a, int32_t n_tok, cudaStream_t st);
 int attention_geometry_chunk(int32_t len, int32_t n_kv, int sm_count);
