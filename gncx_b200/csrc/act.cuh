@@ -78,63 +78,84 @@ __device__ __forceinline__ void load_block32(const float* x, bool vec16, float (
     }
 }
 
+// Quantize one quarter (8 inputs) of block b and store it into the
+// shared-memory act layout; the four threads of the block run it together
+// (amax and sums via shuffles).
+__device__ __forceinline__ void act_quant_quarter(const float (&v)[8], bool ok, int b, int q4, int8_t* qs,
+                                                  float4* rec) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    uint32_t w0 = 0, w1 = 0;
+    int part = 0;
+    float d = 0.0f;
+    if (amax != 0.0f) {
+        const float inv = fdiv(127.0f, amax);
+        d = fdiv(amax, 127.0f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int qv = __float2int_rn(fmul(v[i], inv));
+            part += qv;
+            if (i < 4) w0 |= ((uint32_t)qv & 0xFFu) << (8 * i);
+            else w1 |= ((uint32_t)qv & 0xFFu) << (8 * (i - 4));
+        }
+    }
+    // lanes q4 = 0,1 hold inputs 0..15, lanes 2,3 inputs 16..31
+    const int pair = part + __shfl_xor_sync(0xffffffffu, part, 1);
+    const int other = __shfl_xor_sync(0xffffffffu, pair, 2);
+    if (ok) {
+        const int u = b >> 3, j = b & 7;
+        // 8-byte piece q4 of the block's 32 quants: chunk 2j + (q4 >> 1), half (q4 & 1)
+        uint2* dst = reinterpret_cast<uint2*>(qs + act_chunk_pos(u, 2 * j + (q4 >> 1)) + 8 * (q4 & 1));
+        *dst = make_uint2(w0, w1);
+        if (q4 == 0) {
+            const int lo = pair, hi = other;
+            rec[act_rec_pos(b)] = make_float4(d, __int_as_float(lo), __int_as_float(hi), __int_as_float(lo + hi));
+        }
+    }
+}
+
 // Stage act blocks for `in_dim` inputs into shared memory.  Four threads
-// quantize one 32-input block (8 inputs each; amax and sums via shuffles).
-// Must be called by a multiple of 32 threads, all of them.
+// quantize one 32-input block (8 inputs each).  A thread's loads for up to
+// four blocks are issued before any of them is quantized, so a long x costs
+// one L2 round trip per four blocks, not one per block.  Must be called by a
+// multiple of 32 threads, all of them.
 __device__ __forceinline__ void stage_act_fp32(const float* __restrict__ x, int in_dim, int8_t* qs, float4* rec,
                                                int tid, int nthreads) {
+    constexpr int K = 4;
     const int nb = in_dim >> 5;
     const bool vec = (((uintptr_t)x) & 15) == 0;
     const int q4 = tid & 3;
-    for (int base = tid >> 2; base < ((nb + (nthreads >> 2) - 1) / (nthreads >> 2)) * (nthreads >> 2);
-         base += nthreads >> 2) {
-        const int b = base;
-        const bool ok = b < nb;
-        float v[8];
-        if (ok) {
-            const float* src = x + (size_t)b * 32 + q4 * 8;
-            if (vec) {
-                const float4 t0 = reinterpret_cast<const float4*>(src)[0];
-                const float4 t1 = reinterpret_cast<const float4*>(src)[1];
-                v[0] = t0.x; v[1] = t0.y; v[2] = t0.z; v[3] = t0.w; v[4] = t1.x; v[5] = t1.y; v[6] = t1.z; v[7] = t1.w;
+    const int step = nthreads >> 2;
+    const int iters = (nb + step - 1) / step;  // the same for every thread
+    for (int it0 = 0; it0 < iters; it0 += K) {
+        float v[K][8];
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const int b = (tid >> 2) + (it0 + k) * step;
+            if (it0 + k < iters && b < nb) {
+                const float* src = x + (size_t)b * 32 + q4 * 8;
+                if (vec) {
+                    const float4 t0 = reinterpret_cast<const float4*>(src)[0];
+                    const float4 t1 = reinterpret_cast<const float4*>(src)[1];
+                    v[k][0] = t0.x; v[k][1] = t0.y; v[k][2] = t0.z; v[k][3] = t0.w;
+                    v[k][4] = t1.x; v[k][5] = t1.y; v[k][6] = t1.z; v[k][7] = t1.w;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) v[k][i] = src[i];
+                }
             } else {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = src[i];
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = 0.0f;
-        }
-        float amax = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-        uint32_t w0 = 0, w1 = 0;
-        int part = 0;
-        float d = 0.0f;
-        if (amax != 0.0f) {
-            const float inv = fdiv(127.0f, amax);
-            d = fdiv(amax, 127.0f);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int qv = __float2int_rn(fmul(v[i], inv));
-                part += qv;
-                if (i < 4) w0 |= ((uint32_t)qv & 0xFFu) << (8 * i);
-                else w1 |= ((uint32_t)qv & 0xFFu) << (8 * (i - 4));
+                for (int i = 0; i < 8; ++i) v[k][i] = 0.0f;
             }
         }
-        // lanes q4 = 0,1 hold inputs 0..15, lanes 2,3 inputs 16..31
-        const int pair = part + __shfl_xor_sync(0xffffffffu, part, 1);
-        const int other = __shfl_xor_sync(0xffffffffu, pair, 2);
-        if (ok) {
-            const int u = b >> 3, j = b & 7;
-            // 8-byte piece q4 of the block's 32 quants: chunk 2j + (q4 >> 1), half (q4 & 1)
-            uint2* dst = reinterpret_cast<uint2*>(qs + act_chunk_pos(u, 2 * j + (q4 >> 1)) + 8 * (q4 & 1));
-            *dst = make_uint2(w0, w1);
-            if (q4 == 0) {
-                const int lo = pair, hi = other;
-                rec[act_rec_pos(b)] = make_float4(d, __int_as_float(lo), __int_as_float(hi), __int_as_float(lo + hi));
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            if (it0 + k < iters) {  // uniform: every lane takes part in the shuffles
+                const int b = (tid >> 2) + (it0 + k) * step;
+                act_quant_quarter(v[k], b < nb, b, q4, qs, rec);
             }
         }
     }
