@@ -119,12 +119,12 @@ __device__ __forceinline__ void act_quant_quarter(const float (&v)[8], bool ok, 
 
 // Stage act blocks for `in_dim` inputs into shared memory.  Four threads
 // quantize one 32-input block (8 inputs each).  A thread's loads for up to
-// four blocks are issued before any of them is quantized, so a long x costs
-// one L2 round trip per four blocks, not one per block.  Must be called by a
+// eight blocks are issued before any of them is quantized, so a long x costs
+// one L2 round trip per eight blocks, not one per block.  Must be called by a
 // multiple of 32 threads, all of them.
 __device__ __forceinline__ void stage_act_fp32(const float* __restrict__ x, int in_dim, int8_t* qs, float4* rec,
                                                int tid, int nthreads) {
-    constexpr int K = 4;
+    constexpr int K = 8;
     const int nb = in_dim >> 5;
     const bool vec = (((uintptr_t)x) & 15) == 0;
     const int q4 = tid & 3;
