@@ -6,6 +6,7 @@ other rank's call fail with GNCX_ERR_TIMEOUT instead of hanging.
 Skipped on a box with fewer than 2 GPUs."""
 import json
 import os
+import signal
 import socket
 import subprocess
 import sys
@@ -38,10 +39,19 @@ def _port():
 
 
 def _launch(n, args, timeout=300):
+    """Run under torch.distributed.run in a session of its own, so that on a
+    timeout the launcher and all its ranks end together."""
     env = dict(os.environ, PYTHONPATH=str(ROOT), NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}", "--master-addr",
            "127.0.0.1", "--master-port", str(_port()), *args]
-    return subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=timeout)
+    p = subprocess.Popen(cmd, cwd=ROOT, env=env, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True,
+                         start_new_session=True)
+    try:
+        out, err = p.communicate(timeout=timeout)
+    except subprocess.TimeoutExpired:
+        os.killpg(p.pid, signal.SIGKILL)  # the process group this test started
+        out, err = p.communicate()
+    return subprocess.CompletedProcess(cmd, p.returncode, out, err)
 
 
 def _tp_run(tmp_path, model, n, exact):
