@@ -608,6 +608,7 @@ __global__ void __launch_bounds__(kExactThreads) attn_exact_softmax_kernel(const
 // thread (g, d) runs one chain.  V rows and p stream through double-buffered
 // shared memory in tiles of kExactTile positions.
 constexpr int kExactSlice = 32;
+static_assert(kExactSlice == 32, "one warp per (head, 32 columns): one act block, quantized in the PV kernel");
 constexpr int kExactTile = 64;
 constexpr int kExactHeads = kExactThreads / kExactSlice;  // 8
 template <bool VEC>
@@ -680,23 +681,16 @@ __global__ void __launch_bounds__(kExactThreads) attn_exact_pv_kernel(const Attn
         }
         __syncthreads();  // the buffer is refilled two tiles on
     }
-    if (!active) return;
+    if (!active) return;  // whole warps: g is the warp, and with act every lane of it is active
     const int h = kvh * G + g0 + g;
-    a.out[(size_t)z * a.out_stride + (size_t)h * a.hd + d0 + dl] = o;
+    const size_t col = (size_t)h * a.hd + d0 + dl;
+    a.out[(size_t)z * a.out_stride + col] = o;
+    // re-quantized for the next GEMV here: a warp holds one 32-column block of one head
+    if (a.act_out.blocks || a.act_out.staged)
+        act_out_store(a.act_out, o, a.n_heads * a.hd, (size_t)z, (int)(col >> 5), dl);
 }
 
 // Re-quantize exact-mode outputs for the next GEMV (one warp per 32 outputs).
-__global__ void attn_exact_quant_kernel(const AttnArgs a) {
-    pdl_launch_dependents();
-    pdl_wait();
-    const int z = blockIdx.y;
-    const int dim = a.n_heads * a.hd;
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i - (int)(threadIdx.x & 31) >= dim) return;  // whole warp
-    const float o = a.out[(size_t)z * a.out_stride + i];
-    act_out_store(a.act_out, o, dim, (size_t)z, i >> 5, threadIdx.x & 31);
-}
-
 int attention_geometry_chunk(int32_t len, int32_t n_kv, int sm_count) {
     int c = 64;
     // shorter chunks when the window is small, so every SM gets ~2 CTAs
@@ -749,12 +743,7 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
                 ? launch_k(attn_exact_pv_kernel<true>, pv_grid, dim3(kExactThreads), 0, st, a)
                 : launch_k(attn_exact_pv_kernel<false>, pv_grid, dim3(kExactThreads), 0, st, a);
         if (e != cudaSuccess) return kErrCuda;
-        if (act) {
-            const int dim = a.n_heads * a.hd;
-            if (launch_k(attn_exact_quant_kernel, dim3((dim + 255) / 256, n_tok), dim3(256), 0, st, a) != cudaSuccess)
-                return kErrCuda;
-        }
-        return kOk;
+        return kOk;  // the PV kernel also wrote act_out
     }
     const int Gq = a.n_heads / a.n_kv;
     if (n_tok > 1 && vec && a.window == 0 && a.chunk == kPfChunk && (a.hd == 128 || a.hd == 64) &&
