@@ -243,7 +243,9 @@ int32_t gncx_engine_timing(void* engine, double* prefill_ms, double* decode_ms, 
  * channel), and calls gncx_engine_tp_connect with all ranks' handles in rank
  * order; then every rank makes the same prefill / forward / generate calls.
  * A peer that stops arriving makes the others' calls fail with
- * GNCX_ERR_TIMEOUT after 2 s instead of hanging. */
+ * GNCX_ERR_TIMEOUT after 2 s instead of hanging.  A tensor-parallel prefill
+ * takes at most min(max_seq_len, 4096) prompt tokens per call
+ * (GNCX_ERR_CAPACITY beyond). */
 #define GNCX_TP_HANDLE_BYTES 64
 void* gncx_engine_create_tp(const char* gguf_path, int32_t max_seq_len, int32_t tp_rank, int32_t tp_size);
 int32_t gncx_engine_tp_handle(void* engine, void* out /* GNCX_TP_HANDLE_BYTES */);
