@@ -112,6 +112,7 @@ _SIGS = {
     "gncx_engine_create_tp": (c_void_p, [c_char_p, c_int32, c_int32, c_int32]),
     "gncx_engine_tp_handle": (c_int32, [c_void_p, c_void_p]),
     "gncx_engine_tp_connect": (c_int32, [c_void_p, c_void_p]),
+    "gncx_engine_tp_share": (c_int32, [POINTER(c_int32), c_int32, c_int32, POINTER(c_int32)]),
     "gncx_engine_destroy": (None, [c_void_p]),
     "gncx_engine_hparams": (c_int32, [c_void_p, POINTER(c_int32)]),
     "gncx_engine_error": (c_char_p, [c_void_p]),

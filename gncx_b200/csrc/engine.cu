@@ -560,6 +560,30 @@ static int check_device_error(Engine* e) {
 
 static const LayerW* layer_or_null(const Engine* e, int l) { return l < (int)e->L.size() ? &e->L[l] : nullptr; }
 
+// Rank `rank` of `tp`: its q heads [rank*nh, ..), KV heads, ffn rows, model
+// rows (prefill's attn_output / ffn_down) and vocabulary rows (LM head).
+struct TpShare {
+    int nh, nkv, ffn, dim, voc0, voc;
+};
+static int tp_share(int nh, int nkv, int hd, int dim, int ffn, int vocab, int tp, int rank, TpShare& sh,
+                    std::string& err) {
+    if (tp < 1 || tp > kTpMaxRanks || rank < 0 || rank >= tp) { err = "bad tensor-parallel rank/size"; return kErrInvalidArg; }
+    if (nh <= 0 || nkv <= 0 || hd <= 0 || nh % nkv || nkv % tp || dim % (4 * tp) || ffn % (32 * tp)) {
+        err = "tensor parallel size must divide the KV heads, hidden/4 and ffn/32";
+        return kErrInvalidArg;
+    }
+    sh.nh = nh / tp;
+    sh.nkv = nkv / tp;
+    sh.ffn = ffn / tp;
+    sh.dim = dim / tp;
+    int v0, v1;
+    split_rows(vocab, tp, rank, 4, v0, v1);
+    sh.voc0 = v0;
+    sh.voc = v1 - v0;
+    if (sh.voc <= 0) { err = "vocabulary too small for the tensor parallel size"; return kErrInvalidArg; }
+    return kOk;
+}
+
 // Load: read hyper-parameters, lay this rank's share of the tensors out in one
 // device arena, upload.
 static int engine_load(Engine* e, const char* path, int max_seq, int tp_rank, int tp_size, std::string& err) {
@@ -596,23 +620,18 @@ static int engine_load(Engine* e, const char* path, int max_seq, int tp_rank, in
     }
     // ---- this rank's share (tensor parallel: heads, ffn rows, model rows, vocabulary rows)
     const int tp = tp_size;
-    if (tp < 1 || tp > kTpMaxRanks || tp_rank < 0 || tp_rank >= tp) { err = "bad tensor-parallel rank/size"; return kErrInvalidArg; }
-    if (e->nkv % tp || e->dim % (4 * tp) || e->ffn % (32 * tp)) {
-        err = "tensor parallel size must divide the KV heads, hidden/4 and ffn/32";
-        return kErrInvalidArg;
-    }
-    e->nh_l = e->nh / tp;
-    e->nkv_l = e->nkv / tp;
-    e->qd_l = e->nh_l * e->hd;
-    e->kvd_l = e->nkv_l * e->hd;
-    e->ffn_l = e->ffn / tp;
-    e->dim_l = e->dim / tp;
     {
-        int v0, v1;
-        split_rows(e->vocab, tp, tp_rank, 4, v0, v1);
-        e->voc0 = v0;
-        e->voc_l = v1 - v0;
-        if (e->voc_l <= 0) { err = "vocabulary too small for the tensor parallel size"; return kErrInvalidArg; }
+        TpShare sh{};
+        const int st = tp_share(e->nh, e->nkv, e->hd, e->dim, e->ffn, e->vocab, tp, tp_rank, sh, err);
+        if (st != kOk) return st;
+        e->nh_l = sh.nh;
+        e->nkv_l = sh.nkv;
+        e->qd_l = sh.nh * e->hd;
+        e->kvd_l = sh.nkv * e->hd;
+        e->ffn_l = sh.ffn;
+        e->dim_l = sh.dim;
+        e->voc0 = sh.voc0;
+        e->voc_l = sh.voc;
     }
     // ---- arena layout
     auto T = [&](const std::string& n) -> const GgufTensor* { auto it = g.tensors.find(n); return it == g.tensors.end() ? nullptr : &it->second; };
@@ -847,6 +866,20 @@ void* gncx_engine_create_tp(const char* gguf_path, int32_t max_seq_len, int32_t 
         return nullptr;
     }
     return e;
+}
+
+// Host only (no GPU needed): rank `tp_rank`'s share of a model with hp = {n_heads,
+// n_kv, head_dim, dim, ffn, vocab}: out = {q heads, kv heads, ffn rows, model
+// rows, first vocabulary row, vocabulary rows}.  The split gncx_engine_create_tp uses.
+int32_t gncx_engine_tp_share(const int32_t* hp, int32_t tp_size, int32_t tp_rank, int32_t* out) {
+    if (!hp || !out) return kErrInvalidArg;
+    TpShare sh{};
+    std::string err;
+    const int st = tp_share(hp[0], hp[1], hp[2], hp[3], hp[4], hp[5], tp_size, tp_rank, sh, err);
+    if (st != kOk) return st;
+    const int32_t v[6] = {sh.nh, sh.nkv, sh.ffn, sh.dim, sh.voc0, sh.voc};
+    memcpy(out, v, sizeof(v));
+    return kOk;
 }
 
 // This rank's exchange-region handle (GNCX_TP_HANDLE_BYTES bytes) for the other ranks.

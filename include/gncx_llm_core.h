@@ -247,6 +247,11 @@ int32_t gncx_engine_timing(void* engine, double* prefill_ms, double* decode_ms, 
  * takes at most min(max_seq_len, 4096) prompt tokens per call
  * (GNCX_ERR_CAPACITY beyond). */
 #define GNCX_TP_HANDLE_BYTES 64
+/* Host only: rank tp_rank's share of a model, hp = {n_heads, n_kv_heads,
+ * head_dim, dim, ffn_dim, vocab}; out[6] = {q heads, KV heads, ffn rows,
+ * model rows, first vocabulary row, vocabulary rows}, or an error status for
+ * a size that does not divide the model. */
+int32_t gncx_engine_tp_share(const int32_t* hp, int32_t tp_size, int32_t tp_rank, int32_t* out);
 void* gncx_engine_create_tp(const char* gguf_path, int32_t max_seq_len, int32_t tp_rank, int32_t tp_size);
 int32_t gncx_engine_tp_handle(void* engine, void* out /* GNCX_TP_HANDLE_BYTES */);
 int32_t gncx_engine_tp_connect(void* engine, const void* handles /* tp_size * GNCX_TP_HANDLE_BYTES */);
