@@ -141,6 +141,11 @@ static int bind_library(kernel_table* k, const char* path) {
 typedef struct {
     orc_model_desc d;
     kernel_table k;
+    void* (*ram_alloc)(size_t); /* the bound library's arena calls (lib_memory), else NULL: */
+    uint8_t* (*ram_get_ptr)(void*); /* alloc returns a handle, get_ptr its memory */
+    void (*ram_free)(void*);
+    void* ram_handle[32];          /* live arena blocks and their memory */
+    float* ram_ptr[32];
     uint64_t* off;
     int32_t* typ;
     int32_t q_dim, kv_dim;
@@ -152,12 +157,55 @@ typedef struct {
 #define TYP(m, l, t) ((m)->typ[(size_t)(l) * ORC_NT + (t)])
 #define HAS(m, l, t) (OFF(m, l, t) != UINT64_MAX)
 
-void* orc_model_create(const orc_model_desc* desc, const char* ref_lib) {
+static float* vec_alloc(model* m, size_t n) {
+    if (!m->ram_alloc) return (float*)calloc(n, 4);
+    for (int i = 0; i < 32; ++i) {
+        if (m->ram_handle[i]) continue;
+        void* h = m->ram_alloc(n * 4);
+        float* p = h ? (float*)m->ram_get_ptr(h) : NULL;
+        if (!p) return NULL;
+        memset(p, 0, n * 4);
+        m->ram_handle[i] = h;
+        m->ram_ptr[i] = p;
+        return p;
+    }
+    return NULL;
+}
+static void vec_free(model* m, float* p) {
+    if (!p) return;
+    if (!m->ram_free) {
+        free(p);
+        return;
+    }
+    for (int i = 0; i < 32; ++i)
+        if (m->ram_ptr[i] == p) {
+            m->ram_free(m->ram_handle[i]);
+            m->ram_handle[i] = NULL;
+            m->ram_ptr[i] = NULL;
+            return;
+        }
+}
+
+void* orc_model_create(const orc_model_desc* desc, const char* ref_lib) { return orc_model_create_ex(desc, ref_lib, 0); }
+
+void* orc_model_create_ex(const orc_model_desc* desc, const char* ref_lib, int32_t lib_memory) {
     model* m = (model*)calloc(1, sizeof(model));
     m->d = *desc;
     if (ref_lib ? bind_library(&m->k, ref_lib) : bind_oracle(&m->k)) {
         free(m);
         return NULL;
+    }
+    if (lib_memory) {
+        void* h = ref_lib ? dlopen(ref_lib, RTLD_NOW | RTLD_LOCAL) : NULL;  /* the handle bind_library holds */
+        if (h) {
+            *(void**)&m->ram_alloc = dlsym(h, "gncx_ram_alloc");
+            *(void**)&m->ram_get_ptr = dlsym(h, "gncx_ram_get_ptr");
+            *(void**)&m->ram_free = dlsym(h, "gncx_ram_free");
+        }
+        if (!m->ram_alloc || !m->ram_get_ptr || !m->ram_free) {
+            free(m);
+            return NULL;
+        }
     }
     const size_t nt = (size_t)desc->n_layers * ORC_NT;
     m->off = (uint64_t*)malloc(nt * sizeof(uint64_t));
@@ -170,20 +218,20 @@ void* orc_model_create(const orc_model_desc* desc, const char* ref_lib) {
     m->kv_dim = desc->n_kv * desc->head_dim;
     const int32_t dim = desc->dim;
     const int32_t big = dim > m->q_dim ? dim : m->q_dim;
-    m->hidden = (float*)calloc((size_t)dim, 4);
-    m->normed = (float*)calloc((size_t)big, 4);
-    m->q = (float*)calloc((size_t)m->q_dim, 4);
-    m->kb = (float*)calloc((size_t)m->kv_dim, 4);
-    m->vb = (float*)calloc((size_t)m->kv_dim, 4);
-    m->attn = (float*)calloc((size_t)m->q_dim, 4);
-    m->proj = (float*)calloc((size_t)dim, 4);
-    m->gate = (float*)calloc((size_t)desc->ffn_dim, 4);
-    m->up = (float*)calloc((size_t)desc->ffn_dim, 4);
-    m->act = (float*)calloc((size_t)desc->ffn_dim, 4);
-    m->logits = (float*)calloc((size_t)desc->vocab, 4);
+    m->hidden = vec_alloc(m, (size_t)dim);
+    m->normed = vec_alloc(m, (size_t)big);
+    m->q = vec_alloc(m, (size_t)m->q_dim);
+    m->kb = vec_alloc(m, (size_t)m->kv_dim);
+    m->vb = vec_alloc(m, (size_t)m->kv_dim);
+    m->attn = vec_alloc(m, (size_t)m->q_dim);
+    m->proj = vec_alloc(m, (size_t)dim);
+    m->gate = vec_alloc(m, (size_t)desc->ffn_dim);
+    m->up = vec_alloc(m, (size_t)desc->ffn_dim);
+    m->act = vec_alloc(m, (size_t)desc->ffn_dim);
+    m->logits = vec_alloc(m, (size_t)desc->vocab);
     const size_t kvn = (size_t)desc->n_layers * desc->max_seq * m->kv_dim;
-    m->kc = (float*)calloc(kvn, 4);
-    m->vc = (float*)calloc(kvn, 4);
+    m->kc = vec_alloc(m, kvn);
+    m->vc = vec_alloc(m, kvn);
     if (!m->kc || !m->vc) {
         orc_model_destroy(m);
         return NULL;
@@ -195,9 +243,9 @@ void orc_model_destroy(void* h) {
     model* m = (model*)h;
     if (!m) return;
     free(m->off); free(m->typ);
-    free(m->hidden); free(m->normed); free(m->q); free(m->kb); free(m->vb); free(m->attn);
-    free(m->proj); free(m->gate); free(m->up); free(m->act); free(m->logits);
-    free(m->kc); free(m->vc);
+    float* v[] = {m->hidden, m->normed, m->q, m->kb, m->vb, m->attn, m->proj, m->gate, m->up, m->act, m->logits,
+                  m->kc, m->vc};
+    for (size_t i = 0; i < sizeof(v) / sizeof(v[0]); ++i) vec_free(m, v[i]);
     free(m);
 }
 
@@ -259,16 +307,16 @@ const float* orc_model_prefill(void* h, const int32_t* ids, int32_t n) {
     if (n == 1) return orc_model_forward(h, ids[0], 0);
     const uint8_t* B = d->base;
     const int32_t dim = d->dim, qd = m->q_dim, kvd = m->kv_dim, fd = d->ffn_dim;
-    float* bh = (float*)calloc((size_t)n * dim, 4);
-    float* bn = (float*)calloc((size_t)n * dim, 4);
-    float* bq = (float*)calloc((size_t)n * qd, 4);
-    float* bk = (float*)calloc((size_t)n * kvd, 4);
-    float* bv = (float*)calloc((size_t)n * kvd, 4);
-    float* ba = (float*)calloc((size_t)n * qd, 4);
-    float* bp = (float*)calloc((size_t)n * dim, 4);
-    float* bg = (float*)calloc((size_t)n * fd, 4);
-    float* bu = (float*)calloc((size_t)n * fd, 4);
-    float* bf = (float*)calloc((size_t)n * fd, 4);
+    float* bh = vec_alloc(m, (size_t)n * dim);
+    float* bn = vec_alloc(m, (size_t)n * dim);
+    float* bq = vec_alloc(m, (size_t)n * qd);
+    float* bk = vec_alloc(m, (size_t)n * kvd);
+    float* bv = vec_alloc(m, (size_t)n * kvd);
+    float* ba = vec_alloc(m, (size_t)n * qd);
+    float* bp = vec_alloc(m, (size_t)n * dim);
+    float* bg = vec_alloc(m, (size_t)n * fd);
+    float* bu = vec_alloc(m, (size_t)n * fd);
+    float* bf = vec_alloc(m, (size_t)n * fd);
     for (int32_t t = 0; t < n; ++t) fetch_embedding(m, ids[t], bh + (size_t)t * dim);
     for (int32_t l = 0; l < d->n_layers; ++l) {
         for (int32_t t = 0; t < n; ++t)
@@ -304,7 +352,8 @@ const float* orc_model_prefill(void* h, const int32_t* ids, int32_t n) {
         for (size_t i = 0; i < (size_t)n * dim; ++i) bh[i] = bh[i] + bp[i];
     }
     memcpy(m->hidden, bh + (size_t)(n - 1) * dim, (size_t)dim * 4);
-    free(bh); free(bn); free(bq); free(bk); free(bv); free(ba); free(bp); free(bg); free(bu); free(bf);
+    float* tmp[] = {bh, bn, bq, bk, bv, ba, bp, bg, bu, bf};
+    for (size_t i = 0; i < sizeof(tmp) / sizeof(tmp[0]); ++i) vec_free(m, tmp[i]);
     m->k.rmsnorm(m->hidden, B, d->out_norm_off, dim, d->eps, 0, m->normed, NULL, NULL);
     m->k.lm_head(B, d->tok_embd_off, d->tok_embd_type, m->normed, dim, d->vocab, d->softcap, m->logits);
     return m->logits;

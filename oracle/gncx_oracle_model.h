@@ -27,6 +27,11 @@ typedef struct {
 } orc_model_desc;
 
 void* orc_model_create(const orc_model_desc* desc, const char* ref_lib /* NULL: oracle kernels */);
+/* lib_memory != 0: the model's vectors and KV caches come from the bound
+ * library's gncx_ram_alloc (and go back through gncx_ram_free), as the Lua
+ * streamer's scratch does (lua/gncx_streamer.lua:462-464, :539-561) -- for a
+ * library whose kernels need memory they can reach (the B200 library). */
+void* orc_model_create_ex(const orc_model_desc* desc, const char* ref_lib, int32_t lib_memory);
 void orc_model_destroy(void* m);
 const float* orc_model_forward(void* m, int32_t tok, int32_t pos);
 const float* orc_model_prefill(void* m, const int32_t* ids, int32_t n);

@@ -262,12 +262,19 @@ class OracleModel:
                     ("base", c_void_p), ("tok_embd_off", ctypes.c_uint64), ("tok_embd_type", c_int32),
                     ("out_norm_off", ctypes.c_uint64), ("off", c_void_p), ("typ", c_void_p)]
 
-    def __init__(self, gguf_path, max_seq: int, ref_lib: Path | None = REF_STRICT_SO):
+    def __init__(self, gguf_path, max_seq: int, ref_lib: Path | None = REF_STRICT_SO, drive_lib=None):
+        """drive_lib: a loaded library with the reference's entry points whose
+        kernels need memory they can reach (the B200 library): the orchestration
+        then runs its kernels, with the model file mapped through the library's
+        gncx_gla_map_readonly and the vectors from its gncx_ram_alloc, as the
+        Lua streamer sets them up (lua/gncx_streamer.lua:462-464, :539-662)."""
         from gncx_b200 import gguf as _gguf
         o = Oracle()
         L = o.lib
         L.orc_model_create.restype = c_void_p
         L.orc_model_create.argtypes = [c_void_p, c_char_p]
+        L.orc_model_create_ex.restype = c_void_p
+        L.orc_model_create_ex.argtypes = [c_void_p, c_char_p, c_int32]
         L.orc_model_destroy.argtypes = [c_void_p]
         L.orc_model_forward.restype = c_void_p
         L.orc_model_forward.argtypes = [c_void_p, c_int32, c_int32]
@@ -279,7 +286,17 @@ class OracleModel:
         g = _gguf.read(gguf_path)
         hp = _gguf.model_desc(g)
         self.hp = hp
-        self.mm = np.memmap(gguf_path, dtype=np.uint8, mode="r")
+        if drive_lib is not None:
+            size = ctypes.c_size_t()
+            handle = drive_lib.gncx_gla_map_readonly(str(gguf_path).encode(), ctypes.byref(size))
+            base = drive_lib.gncx_gla_get_base_ptr(handle) if handle else None
+            if not base:
+                raise RuntimeError("gncx_gla_map_readonly failed")
+            self.mm = None
+            base_ptr = c_void_p(base)
+        else:
+            self.mm = np.memmap(gguf_path, dtype=np.uint8, mode="r")
+            base_ptr = self.mm.ctypes.data_as(c_void_p)
         names = ["attn_norm", "attn_q", "attn_k", "attn_v", "attn_q_norm", "attn_k_norm", "attn_output", "ffn_norm",
                  "ffn_gate", "ffn_up", "ffn_down"]
         off = np.full((hp["n_layers"], self.NT), np.iinfo(np.uint64).max, dtype=np.uint64)
@@ -295,12 +312,17 @@ class OracleModel:
         arch = {"qwen": 0, "llam": 1, "gemm": 2}.get(hp["arch"][:4], 0)
         d = self._Desc(hp["n_layers"], hp["dim"], hp["n_heads"], hp["n_kv"], hp["head_dim"], hp["ffn"], hp["vocab"],
                        int(max_seq), hp["eps"], hp["rope_base"], hp["softcap"], arch,
-                       self.mm.ctypes.data_as(c_void_p), emb.abs_offset, emb.ggml_type,
+                       base_ptr, emb.abs_offset, emb.ggml_type,
                        g.tensors["output_norm.weight"].abs_offset, off.ctypes.data_as(c_void_p),
                        typ.ctypes.data_as(c_void_p))
-        lib_path = str(ref_lib).encode() if ref_lib is not None and Path(ref_lib).exists() else None
-        self.kind = "reference" if lib_path else "port"
-        self.h = L.orc_model_create(ctypes.byref(d), lib_path)
+        if drive_lib is not None:
+            lib_path = str(ref_lib).encode()
+            self.kind = "drop-in"
+            self.h = L.orc_model_create_ex(ctypes.byref(d), lib_path, 1)
+        else:
+            lib_path = str(ref_lib).encode() if ref_lib is not None and Path(ref_lib).exists() else None
+            self.kind = "reference" if lib_path else "port"
+            self.h = L.orc_model_create(ctypes.byref(d), lib_path)
         if not self.h:
             raise RuntimeError("oracle model creation failed")
 

@@ -67,3 +67,32 @@ def test_oracle_model_single_token_prefill_is_forward(tmp_path):
     b = m.forward_token(17, 0)
     assert np.array_equal(a, b)
     m.close()
+
+
+def test_orchestration_over_a_librarys_own_memory(tmp_path):
+    """The drop-in harness of tests/test_dropin_orchestration_gpu.py, checked
+    on CPU with the reference library itself as the driven library: the model
+    file mapped by its gncx_gla_map_readonly, every vector and KV cache from
+    its gncx_ram_alloc arena -- the same logits and stream as the plain run."""
+    import ctypes
+    from oracle.oracle import REF_STRICT_SO, OracleModel
+    if not REF_STRICT_SO.exists():
+        pytest.skip("reference library not built here (oracle/_ref)")
+    ref = ctypes.CDLL(str(REF_STRICT_SO))
+    ref.gncx_gla_map_readonly.restype = ctypes.c_void_p
+    ref.gncx_gla_map_readonly.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_size_t)]
+    ref.gncx_gla_get_base_ptr.restype = ctypes.c_void_p
+    ref.gncx_gla_get_base_ptr.argtypes = [ctypes.c_void_p]
+    cfg = dict(n_layers=2, dim=256, n_heads=4, n_kv=2, head_dim=64, ffn=512, vocab=1500, eps=1e-6, rope_base=1e6)
+    path = gguf.write_random_model(tmp_path / "m.gguf", cfg, seed=4, wtype=Q8_0)
+    prompt = np.random.default_rng(2).integers(0, cfg["vocab"], 13).tolist()
+    a = OracleModel(path, 48, REF_STRICT_SO)
+    b = OracleModel(path, 48, REF_STRICT_SO, drive_lib=ref)
+    try:
+        assert b.kind == "drop-in"
+        assert np.array_equal(a.prefill(prompt), b.prefill(prompt))
+        assert np.array_equal(a.forward_token(prompt[-1], 13), b.forward_token(prompt[-1], 13))
+        assert a.generate(prompt, 12, 1.15, -1) == b.generate(prompt, 12, 1.15, -1)
+    finally:
+        a.close()
+        b.close()
