@@ -292,6 +292,8 @@ __device__ Best am_block_best(Best p) {
 
 __global__ void am_state_stage1(const float* __restrict__ logits, int vocab, const DecodeState* st, double penalty,
                                 double* part_v, int* part_i) {
+    pdl_launch_dependents();
+    pdl_wait();  // the logits come from the preceding kernel
     const int per = (vocab + gridDim.x - 1) / gridDim.x;
     const int lo = blockIdx.x * per, hi = min(vocab, lo + per);
     extern __shared__ unsigned pen[];
@@ -316,6 +318,8 @@ __global__ void am_state_stage1(const float* __restrict__ logits, int vocab, con
 
 __global__ void am_state_stage2(const double* part_v, const int* part_i, int n, DecodeState* st, int32_t* out_ids,
                                 int advance_pos) {
+    pdl_launch_dependents();
+    pdl_wait();
     Best b{-1e30, 0};
     for (int k = threadIdx.x; k < n; k += blockDim.x) b = pick(b, Best{part_v[k], part_i[k]});
     b = am_block_best(b);
@@ -344,9 +348,12 @@ int argmax_state_launch(const float* logits, int32_t vocab, DecodeState* st, dou
     int* pi = reinterpret_cast<int*>(pv + kAmBlocks);
     const int blocks = vocab < kAmBlocks * 64 ? (vocab + 63) / 64 : kAmBlocks;
     const int per = (vocab + blocks - 1) / blocks;
-    am_state_stage1<<<blocks, kAmThreads, (size_t)((per + 31) / 32) * 4, s>>>(logits, vocab, st, penalty, pv, pi);
-    am_state_stage2<<<1, kAmThreads, 0, s>>>(pv, pi, blocks, st, out_ids, advance_pos);
-    return status();
+    if (launch_k(am_state_stage1, dim3(blocks), dim3(kAmThreads), (size_t)((per + 31) / 32) * 4, s, logits, vocab, st,
+                 penalty, pv, pi) != cudaSuccess ||
+        launch_k(am_state_stage2, dim3(1), dim3(kAmThreads), 0, s, pv, pi, blocks, st, out_ids, advance_pos) !=
+            cudaSuccess)
+        return kErrCuda;
+    return kOk;
 }
 
 }  // namespace gncx

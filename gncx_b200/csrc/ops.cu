@@ -6,6 +6,7 @@
 #include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 #include "norm.cuh"
 
 namespace gncx {
@@ -114,6 +115,8 @@ __device__ __forceinline__ float dequant_elem(const uint8_t* row, int32_t type, 
 
 __global__ void dequant_kernel(const uint8_t* __restrict__ w, int32_t type, int32_t rows, int32_t n, float scale,
                                const int32_t* __restrict__ row_ids, float* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();  // row ids (the decode step's token) come from the preceding kernel
     const size_t rb = row_bytes(type, n);
     const int64_t total = (int64_t)rows * n;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -135,8 +138,10 @@ int dequant_launch(const uint8_t* w, int32_t type, int32_t rows, int32_t n, floa
     if (total == 0) return kOk;
     const int threads = 256;
     const int64_t want = (total + threads - 1) / threads;
-    dequant_kernel<<<(int)(want < 65535 ? want : 65535), threads, 0, st>>>(w, type, rows, n, scale, row_ids, out);
-    return launch_status();
+    return launch_k(dequant_kernel, dim3((unsigned)(want < 65535 ? want : 65535)), dim3(threads), 0, st, w, type, rows,
+                    n, scale, row_ids, out) == cudaSuccess
+               ? kOk
+               : kErrCuda;
 }
 
 int embed_launch(const uint8_t* tensor, int32_t type, const int32_t* tokens, int32_t n_tokens, int32_t dim,
