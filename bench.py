@@ -231,6 +231,47 @@ def format_sweep(torch, lib, P, reps: int = 20) -> dict:
     return res
 
 
+def attention_sweep(torch, lib, P, reps: int = 20) -> dict:
+    """Configuration 3: one decode attention step (32 query heads, 8 KV heads,
+    head_dim 128, fp32 KV cache ~ N(0,1)) through gncx_mqa_attention_step_ext
+    at context 512 / 4096 / 32768 and a 4096 window; each call timed alone
+    with L2 flushed.  Bytes: the K and V rows the window reads, the new K/V
+    row written, q read and the output written."""
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    nh, nkv, hd = 32, 8, 128
+    scale = float(np.float32(1.0 / np.sqrt(hd)))
+    peak = float(measured_peaks().get("hbm_gbs", 6650.0))
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+    res = {}
+    for ctx, win in ((512, 0), (4096, 0), (32768, 0), (32768, 4096)):
+        kc = torch.randn(ctx * nkv * hd, device="cuda", generator=g)
+        vc = torch.randn(ctx * nkv * hd, device="cuda", generator=g)
+        q = torch.randn(nh * hd, device="cuda", generator=g)
+        k = torch.randn(nkv * hd, device="cuda", generator=g)
+        v = torch.randn(nkv * hd, device="cuda", generator=g)
+        out = torch.empty(nh * hd, device="cuda")
+        times = []
+        for r in range(reps + 2):
+            flush.fill_(float(r))
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            lib.gncx_mqa_attention_step_ext(P(q), P(k), P(v), P(kc), P(vc), ctx - 1, nh, nkv, hd, scale, win, 1,
+                                            P(out))
+            b.record(stream)
+            torch.cuda.synchronize()
+            if r >= 2:
+                times.append(a.elapsed_time(b))
+        ms = statistics.median(times)
+        span = min(ctx, win) if win > 0 else ctx
+        nbytes = 2 * span * nkv * hd * 4 + 2 * nkv * hd * 4 + 2 * nh * hd * 4
+        gbs = nbytes / (ms / 1e3) / 1e9
+        res[f"ctx {ctx}" + (f" window {win}" if win else "")] = {"us": ms * 1e3, "GB/s": gbs, "frac": gbs / peak}
+        del kc, vc
+    return res
+
+
 def decode_bench(args, torch) -> dict:
     """Benchmark configuration 5: random-init 8B-shaped Qwen3 decoder (Q4_K
     weights, Q6_K tied head), 2048-token seeded prompt prefilled through the
@@ -497,6 +538,10 @@ def run_gpu(args) -> None:
         if not args.no_sweep:
             lib.gncx_set_weight_prefetch(0)  # each sweep entry is timed alone
             line["sweep"] = format_sweep(torch, lib, P)
+            try:
+                line["attention"] = attention_sweep(torch, lib, P)
+            except Exception as exc:  # reported; the GEMV numbers stand
+                line["attention"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
         if tp_decode is not None:
             line["decode"] = tp_decode
         elif not args.no_decode:
