@@ -690,7 +690,8 @@ __global__ void __launch_bounds__(kExactThreads) attn_exact_pv_kernel(const Attn
         act_out_store(a.act_out, o, a.n_heads * a.hd, (size_t)z, (int)(col >> 5), dl);
 }
 
-// Re-quantize exact-mode outputs for the next GEMV (one warp per 32 outputs).
+// Positions per split of the drop-in decode step: 64, halved (down to 16)
+// while the window gives fewer than two CTAs per SM (splits x KV heads).
 int attention_geometry_chunk(int32_t len, int32_t n_kv, int sm_count) {
     int c = 64;
     // shorter chunks when the window is small, so every SM gets ~2 CTAs
@@ -700,14 +701,13 @@ int attention_geometry_chunk(int32_t len, int32_t n_kv, int sm_count) {
 
 template <bool VEC, bool SCORES_ONLY>
 static cudaError_t launch_partial(const AttnArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
-    static size_t set_bytes = 0;
-    if (smem > set_bytes) {
-        const cudaError_t e = cudaFuncSetAttribute(attn_partial_kernel<VEC, SCORES_ONLY>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        set_bytes = smem;
-    }
+    const cudaError_t e = set_smem_limit(attn_partial_kernel<VEC, SCORES_ONLY>, smem);
+    if (e != cudaSuccess) return e;
     return launch_k(attn_partial_kernel<VEC, SCORES_ONLY>, grid, dim3(kAttnThreads), smem, st, a);
+}
+
+bool attention_shape_ok(int32_t n_heads, int32_t n_kv, int32_t hd) {
+    return n_heads > 0 && n_kv > 0 && hd > 0 && n_heads % n_kv == 0 && hd <= kMaxHeadDim && (hd & 3) == 0;
 }
 
 int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
@@ -754,22 +754,11 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
         const int qt = kPfRows / Gq;
         const dim3 pgrid(a.max_splits, a.n_kv, (n_tok + qt - 1) / qt);
         const size_t psm = attn_prefill_smem_bytes(a.hd);
-        static size_t set128 = 0, set64 = 0;
         if (a.hd == 128) {
-            if (psm > set128) {
-                if (cudaFuncSetAttribute(attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)psm) != cudaSuccess)
-                    return kErrCuda;
-                set128 = psm;
-            }
+            if (set_smem_limit(attn_prefill_kernel<128>, psm) != cudaSuccess) return kErrCuda;
             e = launch_k(attn_prefill_kernel<128>, pgrid, dim3(kAttnThreads), psm, st, b);
         } else {
-            if (psm > set64) {
-                if (cudaFuncSetAttribute(attn_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)psm) != cudaSuccess)
-                    return kErrCuda;
-                set64 = psm;
-            }
+            if (set_smem_limit(attn_prefill_kernel<64>, psm) != cudaSuccess) return kErrCuda;
             e = launch_k(attn_prefill_kernel<64>, pgrid, dim3(kAttnThreads), psm, st, b);
         }
     } else {
@@ -777,9 +766,7 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
     }
     if (e != cudaSuccess) return kErrCuda;
     const size_t csm = (size_t)a.max_splits * 8;
-    if (csm > 48 * 1024 &&
-        cudaFuncSetAttribute(attn_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csm) != cudaSuccess)
-        return kErrCuda;
+    if (set_smem_limit(attn_combine_kernel, csm) != cudaSuccess) return kErrCuda;
     return launch_k(attn_combine_kernel, dim3(a.n_heads, n_tok), dim3(128), csm, st, a) == cudaSuccess ? kOk
                                                                                                     : kErrCuda;
 }

@@ -10,6 +10,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -43,7 +44,10 @@ static std::mutex g_maps_mu;
 static int32_t g_status = kOk;
 static std::string g_message;
 
+static std::mutex g_status_mu;  // entry points in other threads (the no-alloc one) report here too
+
 static void set_error(int32_t code, const char* what) {
+    std::lock_guard<std::mutex> lock(g_status_mu);
     if (code == kOk || g_status != kOk) return;
     g_status = code;
     g_message = what ? what : "";
@@ -68,6 +72,19 @@ const DeviceInfo& device_info() {
         cudaDeviceGetAttribute(&d.l2_bytes, cudaDevAttrL2CacheSize, dev);
     }
     return d;
+}
+
+cudaError_t set_smem_limit(const void* k, size_t bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, size_t> done;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorNoDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    size_t& have = done[std::make_pair(k, dev)];
+    if (bytes <= have || bytes <= 48 * 1024) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) have = bytes;
+    return e;
 }
 
 // Initialise on first use: pick up the current device, create the library
@@ -222,6 +239,7 @@ extern "C" {
 int32_t gncx_last_error(void) { return g_status; }
 const char* gncx_last_error_message(void) { return g_message.c_str(); }
 void gncx_clear_error(void) {
+    std::lock_guard<std::mutex> lock(g_status_mu);
     g_status = kOk;
     g_message.clear();
 }

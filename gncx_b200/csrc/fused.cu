@@ -160,16 +160,13 @@ int add_norm_quant_launch(float* hidden, const float* residual, const float* w, 
     const bool vec = ((uintptr_t)hidden & 15) == 0 && ((uintptr_t)residual & 15) == 0 && ((uintptr_t)w & 15) == 0 &&
                      ((uintptr_t)normed & 15) == 0;
     if (act.staged && vec && dim <= kRowPasses * 8 * kRowThreads) {
-        if (smem > 48 * 1024 && cudaFuncSetAttribute(add_norm_quant_row_kernel,
-                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return kErrCuda;
+        if (set_smem_limit(add_norm_quant_row_kernel, smem) != cudaSuccess) return kErrCuda;
         return launch_k(add_norm_quant_row_kernel, dim3(1), dim3(kRowThreads), smem, st, hidden, residual, w, dim,
                         eps, act.staged, normed) == cudaSuccess
                    ? kOk
                    : kErrCuda;
     }
-    if (smem > 48 * 1024)
-        cudaFuncSetAttribute(add_norm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (set_smem_limit(add_norm_quant_kernel, smem) != cudaSuccess) return kErrCuda;
     add_norm_quant_kernel<<<rows, 256, smem, st>>>(hidden, residual, w, dim, eps, act, normed);
     return status();
 }

@@ -279,14 +279,9 @@ static int env_int(const char* name, int dflt) {
 template <int T, bool ALIGNED, bool PREQ, int CW>
 static int launch_t(const GemvArgs& a, size_t smem, int, cudaStream_t st) {
     auto k = gemv_kernel<T, ALIGNED, PREQ, CW>;
-    static int configured_bytes = 0;  // per instantiation, per process (single device at a time)
-    static size_t occ_smem = 0;
+    static size_t occ_smem = 0;  // occupancy per instantiation (devices of one model alike)
     static int occ_blocks = 1;
-    if ((int)smem > configured_bytes) {
-        if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return kErrCuda;
-        configured_bytes = (int)smem;
-    }
+    if (set_smem_limit(k, smem) != cudaSuccess) return kErrCuda;
     if (smem != occ_smem) {  // resident CTAs per SM for this shared-memory size (registers included)
         int nb = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k, (CW + 1) * 32, smem) != cudaSuccess) nb = 1;

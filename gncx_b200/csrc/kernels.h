@@ -18,6 +18,14 @@ struct DeviceInfo {
 };
 // Properties of the current device (queried once per device).
 const DeviceInfo& device_info();
+// Raise kernel `k`'s dynamic shared-memory limit to at least `bytes` on the
+// current device.  The attribute belongs to one device, so the limit already
+// set is remembered per (kernel, device) and each device is configured once.
+cudaError_t set_smem_limit(const void* k, size_t bytes);
+template <class K>
+inline cudaError_t set_smem_limit(K* k, size_t bytes) {
+    return set_smem_limit(reinterpret_cast<const void*>(k), bytes);
+}
 
 // ---- GEMV / prefill ----
 // `act` (16-byte aligned), when given, is a staged activation vector
@@ -116,6 +124,8 @@ struct AttnArgs {
     const float* rope_s;
 };
 int attention_run(const AttnArgs& a, int32_t n_tok, cudaStream_t st);
+// True when attention_run supports these head counts and head size.
+bool attention_shape_ok(int32_t n_heads, int32_t n_kv, int32_t head_dim);
 int attention_geometry_chunk(int32_t len, int32_t n_kv, int sm_count);
 struct AttnScratch {
     float* part;        // partial (max, sum, o[hd]) records

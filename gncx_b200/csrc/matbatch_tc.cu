@@ -426,13 +426,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
 template <int T>
 static int launch_tc(const uint8_t* w, size_t rb, const ActBlock* act, int batch, int in_dim, int out_dim, float* y,
                      int ldy, int32_t* err, cudaStream_t st) {
-    static bool configured = false;
-    if (!configured) {
-        if (cudaFuncSetAttribute(matbatch_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemAlloc) !=
-            cudaSuccess)
-            return kErrCuda;
-        configured = true;
-    }
+    if (set_smem_limit(matbatch_tc_kernel<T>, kTcSmemAlloc) != cudaSuccess) return kErrCuda;
     const dim3 grid((batch + kTcN - 1) / kTcN, (out_dim + kTcM - 1) / kTcM);
     matbatch_tc_kernel<T><<<grid, kTcThreads, kTcSmemAlloc, st>>>(w, rb, act, batch, in_dim, out_dim, y, ldy, err);
     return cudaPeekAtLastError() == cudaSuccess ? kOk : kErrCuda;

@@ -15,7 +15,10 @@
 //
 // Set-up: the first call on a device (with that device current) looks up the
 // array's device address with cudaGetSymbolAddress; make that first call
-// before any stream capture.  Every later call on the device reuses it.
+// before any stream capture.  Every later call on the device reuses it.  A
+// cudaDeviceReset discards the device's copy of the array; the cached address
+// is then stale, so a process that resets a device must not call this entry
+// point on that device again.
 //
 // Sharing: all calls on a device share the one array and leave their records
 // in it.  Nothing in it needs to start at zero: every record the merge reads
@@ -70,9 +73,13 @@ extern "C" int32_t gncx_mqa_attention_step_noalloc(const float* q_vec, const flo
                                                    int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                                                    float attn_scale, int32_t sliding_window, int32_t write_kv,
                                                    float* out_attn_vec, void* cuda_stream) {
-    if (!q_vec || !k_cache_layer || !v_cache_layer || !out_attn_vec || pos < 0 || n_heads <= 0 || n_kv_heads <= 0 ||
-        head_dim <= 0) {
-        record_api_error(kErrInvalidArg, "gncx_mqa_attention_step_noalloc: null pointer or bad dimension");
+    // Everything the launch would reject is rejected here, before the KV-cache
+    // write, so a refused call leaves the caller's cache untouched.
+    if (!q_vec || !k_cache_layer || !v_cache_layer || !out_attn_vec || pos < 0 ||
+        !attention_shape_ok(n_heads, n_kv_heads, head_dim)) {
+        record_api_error(kErrInvalidArg,
+                         "gncx_mqa_attention_step_noalloc: null pointer, bad dimension, n_heads not a multiple of "
+                         "n_kv_heads, or head_dim not a multiple of 4 up to 256");
         return kErrInvalidArg;
     }
     void* scratch = nullptr;

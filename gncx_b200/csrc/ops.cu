@@ -173,7 +173,7 @@ int rmsnorm_launch(const float* x, const float* w, int32_t rows, int32_t dim, fl
     if (rows == 0) return kOk;
     const size_t smem = (size_t)dim * 4;
     if (smem > 200 * 1024) return kErrCapacity;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (set_smem_limit(rmsnorm_kernel, smem) != cudaSuccess) return kErrCuda;
     rmsnorm_kernel<<<rows, kNormThreads, smem, st>>>(x, w, out, 1, dim, eps);
     return launch_status();
 }
@@ -184,7 +184,7 @@ int rmsnorm_heads_launch(float* v, const float* w, int32_t rows, int32_t n_heads
     if (rows == 0) return kOk;
     const size_t smem = (size_t)head_dim * 4;
     if (smem > 200 * 1024) return kErrCapacity;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (set_smem_limit(rmsnorm_kernel, smem) != cudaSuccess) return kErrCuda;
     const int threads = head_dim >= 256 ? 256 : 128;
     rmsnorm_kernel<<<rows * n_heads, threads, smem, st>>>(v, w, v, n_heads, head_dim, eps);
     return launch_status();

@@ -191,8 +191,11 @@ int32_t gncx_sample_greedy(const float* logits, int32_t vocab, const int32_t* re
  * of 128 fit a window of ~15,800 positions), else GNCX_ERR_CAPACITY with a
  * message in gncx_last_error_message().  The first call on a device does a
  * one-time set-up (looks up the array's address) and should come before any
- * stream capture.  All calls on a device share the array, so calls whose GPU
- * work overlaps race and must be serialised by the caller.  Returns a status. */
+ * stream capture; after a cudaDeviceReset of that device the looked-up
+ * address is stale and the entry point must not be called there again.  All
+ * calls on a device share the array, so calls whose GPU work overlaps race
+ * and must be serialised by the caller.  A call rejected with a status has
+ * not written the KV cache.  Returns a status. */
 int32_t gncx_mqa_attention_step_noalloc(const float* q_vec, const float* k_vec, const float* v_vec,
                                         float* k_cache_layer, float* v_cache_layer, int32_t pos, int32_t n_heads,
                                         int32_t n_kv_heads, int32_t head_dim, float attn_scale,

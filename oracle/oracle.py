@@ -27,7 +27,24 @@ HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "_build" / "liboracle.so"
 REF_STRICT_SO = HERE / "_ref" / "libgncx_ref_strict.so"
 REF_NATIVE_SO = HERE / "_ref" / "libgncx_ref.so"
-REFERENCE_SRC = Path(os.environ.get("GNCX_REFERENCE", "/root/reference"))
+
+
+def reference_source() -> Path | None:
+    """Where the reference's sources lie, if anywhere: ``$GNCX_REFERENCE``, else
+    the ``reference_path`` that BASELINE.json at the repository root names.
+    None when neither exists (the GPU box carries only the prebuilt _ref/)."""
+    cand = os.environ.get("GNCX_REFERENCE")
+    if not cand:
+        try:
+            import json
+            cand = json.loads((HERE.parent / "BASELINE.json").read_text()).get("reference_path")
+        except (OSError, ValueError):
+            cand = None
+    if not cand:
+        return None
+    p = Path(cand)
+    return p if (p / "csrc" / "gncx_llm_kernels.cpp").exists() else None
+
 
 ACT_DTYPE = np.dtype([("d", "<f4"), ("sum_q", "<i4"), ("sum_lo", "<i4"), ("sum_hi", "<i4"), ("qs", "i1", (32,))])
 
@@ -37,8 +54,9 @@ def build(with_reference: bool = True) -> None:
     if shutil.which("make") is None:
         return
     subprocess.run(["make", "-s", "-C", str(HERE), "all"], check=True)
-    if with_reference and (REFERENCE_SRC / "csrc" / "gncx_llm_kernels.cpp").exists():
-        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={REFERENCE_SRC}"], check=True)
+    src = reference_source() if with_reference else None
+    if src is not None:
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={src}"], check=True)
 
 
 def _ptr(a: np.ndarray | None):

@@ -43,9 +43,11 @@ def test_ctypes_signatures_cover_header():
 
 
 def test_reference_signature_arity_matches_reference_source():
-    src = Path("/root/reference/csrc/gncx_llm_kernels.cpp")
-    if not src.exists():
-        pytest.skip("reference sources not present")
+    from oracle.oracle import reference_source
+    root = reference_source()
+    if root is None:
+        pytest.skip("reference sources not present (set GNCX_REFERENCE)")
+    src = root / "csrc" / "gncx_llm_kernels.cpp"
     text = src.read_text(errors="replace")
     for name in declared_functions():
         m = re.search(r"GNCX_LLM_API\s+[\w\s\*]+?\b" + name + r"\s*\((.*?)\)\s*\{", text, flags=re.S)
