@@ -110,6 +110,32 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def host_info() -> dict:
+    """The host the CPU baseline runs on: CPU model, the ISA extensions that
+    matter to the reference's kernels, logical CPUs, the CPUs this process
+    may use, and the reference pool's thread cap (clamp(hw, 2, 12),
+    csrc/gncx_llm_kernels.cpp:141)."""
+    model, flags = "unknown", set()
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name") and model == "unknown":
+                model = line.split(":", 1)[1].strip()
+            elif line.startswith("flags") and not flags:
+                flags = set(line.split(":", 1)[1].split())
+    except OSError:
+        pass
+    isa = [f for f in ("sse4_2", "avx", "avx2", "fma", "avx512f", "avx512bw", "avx512_vnni", "avx_vnni", "amx_int8")
+           if f in flags]
+    logical = os.cpu_count() or 1
+    try:
+        usable = len(os.sched_getaffinity(0))
+    except AttributeError:
+        usable = logical
+    from oracle.oracle import REF_NATIVE_SO, ref_build_flags
+    return {"cpu_model": model, "isa": isa, "logical_cpus": logical, "usable_cpus": usable,
+            "reference_pool_threads": max(2, min(usable, 12)), "reference_build": ref_build_flags(REF_NATIVE_SO)}
+
+
 def gen_weights_gpu(torch, t: int, out_dim: int, in_dim: int, seed: int):
     """Seeded random blocks generated on the device (same distributions as gncx_b200.synth)."""
     from gncx_b200.core import BLOCK, Q4_0, Q4_K, Q6_K, Q8_0
@@ -151,7 +177,7 @@ def cpu_baseline(seconds: float = 8.0) -> dict:
     from oracle.oracle import REF_NATIVE_SO, Oracle, RefLib
     kind = "reference" if REF_NATIVE_SO.exists() else "port"
     impl = RefLib(REF_NATIVE_SO) if kind == "reference" else Oracle()
-    cores = min(os.cpu_count() or 1, 12) if kind == "reference" else (os.cpu_count() or 1)
+    cores = max(2, min(os.cpu_count() or 1, 12)) if kind == "reference" else 1  # the port is one thread
     data = []
     for i, (o, n) in enumerate(SHAPES):
         data.append((synth.random_weights_fast(12, o, n, seed=10 + i), synth.random_activations(n, seed=20 + i), o))
@@ -165,7 +191,8 @@ def cpu_baseline(seconds: float = 8.0) -> dict:
             total_bytes += algo_bytes(12, o, x.size)
         reps += 1
     return {"value": total_bytes / total_t / 1e9, "unit": "GB/s", "cores": cores, "kind": kind,
-            "sample": f"{reps} passes over the Q4_K sweep (all four shapes), {total_t:.1f} s of CPU time"}
+            "sample": f"{reps} passes over the Q4_K sweep (all four shapes), {total_t:.1f} s of CPU time",
+            "host": host_info()}
 
 
 def run_reference(args) -> None:
@@ -176,7 +203,7 @@ def run_reference(args) -> None:
     from oracle.oracle import REF_NATIVE_SO, Oracle, RefLib
     kind = "reference" if REF_NATIVE_SO.exists() else "port"
     impl = RefLib(REF_NATIVE_SO) if kind == "reference" else Oracle()
-    cores = min(os.cpu_count() or 1, 12) if kind == "reference" else (os.cpu_count() or 1)
+    cores = max(2, min(os.cpu_count() or 1, 12)) if kind == "reference" else 1  # the port is one thread
     data = [(synth.random_weights_fast(12, o, n, seed=10 + i), synth.random_activations(n, seed=20 + i), o)
             for i, (o, n) in enumerate(SHAPES)]
     step_bytes = sum(algo_bytes(12, o, x.size) for _, x, o in data)
@@ -197,7 +224,7 @@ def run_reference(args) -> None:
         "config": {"workload": "Q4_K GEMV sweep 4096x4096, 4096x12288, 12288x4096, 151936x4096 (out x in), batch 1",
                    "l2": "inputs larger than L2 (417 MB of weights per step)"},
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind,
-                         "sample": f"{args.steps} full passes over the sweep"},
+                         "sample": f"{args.steps} full passes over the sweep", "host": host_info()},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -228,6 +255,58 @@ def format_sweep(torch, lib, P, reps: int = 20) -> dict:
             ms = statistics.median(times)
             res[f"{names[t]} {o}x{n}"] = {"us": ms * 1e3, "GB/s": algo_bytes(t, o, n) / (ms / 1e3) / 1e9}
             del w
+    return res
+
+
+DECODE_SHAPES = [(6144, 4096), (24576, 4096), (4096, 12288), (4096, 4096)]  # 8B decode: qkv, gate/up, down, o
+
+
+def gemv_kernel_sweep(torch, lib, P, shapes=DECODE_SHAPES, t: int = 12, reps: int = 5) -> dict:
+    """Kernel time of the decode-sized GEMVs, no host API time: one CUDA graph
+    per shape holds back-to-back drop-in matvec launches, each on its own copy
+    of the weights (copies totalling >= 2x L2, so every launch streams from
+    HBM), with weight prefetch across launch boundaries as in decode.  The
+    graph is replayed `reps` times; time per launch = replay time / launches."""
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    peak = float(measured_peaks().get("hbm_gbs", 6650.0))
+    names = {2: "Q4_0", 8: "Q8_0", 12: "Q4_K", 14: "Q6_K"}
+    res = {}
+    outer = torch.cuda.current_stream()
+    for i, (o, n) in enumerate(shapes):
+        nbytes = algo_bytes(t, o, n)
+        copies = max(4, -(-2 * l2 // nbytes))
+        ws = [gen_weights_gpu(torch, t, o, n, seed=500 + 31 * i + c) for c in range(copies)]
+        x = torch.randn(n, device="cuda")
+        y = torch.empty(o, device="cuda")
+        ptrs = [P(w) for w in ws]
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(outer)
+        with torch.cuda.stream(s):
+            lib.gncx_set_stream(ctypes.c_void_p(s.cuda_stream))
+            lib.gncx_xfold_universal_matvec(ptrs[0], 0, t, P(x), None, n, o, P(y), None)  # configure outside capture
+            s.synchronize()
+            with torch.cuda.graph(g, stream=s):
+                for c in range(copies):
+                    lib.gncx_xfold_universal_matvec(ptrs[c], 0, t, P(x), None, n, o, P(y), None)
+        lib.gncx_set_stream(ctypes.c_void_p(outer.cuda_stream))
+        from gncx_b200 import core
+        core.check(lib)
+        g.replay()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(outer)
+            g.replay()
+            b.record(outer)
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b) / copies)
+        ms = statistics.median(times)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        res[f"{names[t]} {o}x{n}"] = {"us": ms * 1e3, "GB/s": gbs, "frac": gbs / peak, "launches": copies}
+        del g, ws
+        torch.cuda.empty_cache()
     return res
 
 
@@ -302,23 +381,42 @@ def decode_bench(args, torch) -> dict:
                          "ms_per_token": t["decode_ms"] / max(1, t["decode_steps"]),
                          "prefill_tok_s": args.prompt / (t["prefill_ms"] / 1e3), "prefill_ms": t["prefill_ms"],
                          "tokens": len(ids), "first_ids": ids[:8]}
-    # reference CPU decode on the same file (bounded sample)
+    # reference CPU decode and prefill on the same file (bounded samples)
     if not args.no_cpu_baseline:
-        from oracle.oracle import REF_NATIVE_SO, OracleModel
-        ref = OracleModel(path, 64, REF_NATIVE_SO)
-        ref.prefill(prompt[:8])
-        t1 = time.perf_counter()
-        n = 3
-        tok = prompt[8]
-        for i in range(n):
-            ref.forward_token(tok, 8 + i)
-        dt = time.perf_counter() - t1
-        ref.close()
-        res["cpu_reference"] = {"decode_tok_s": n / dt, "kind": ref.kind, "cores": min(os.cpu_count() or 1, 12),
-                                "sample": f"{n} decode steps after an 8-token prefill, pool of min(cores,12) threads"}
-        if "split_kv" in res:
-            res["speedup_vs_cpu_decode"] = res["split_kv"]["decode_tok_s"] / res["cpu_reference"]["decode_tok_s"]
+        res["cpu_reference"] = cpu_model_baseline(path, prompt, args.prompt + args.new_tokens)
+        cpu = res["cpu_reference"]["decode_tok_s"]
+        for mode in ("split_kv", "exact_softmax"):
+            if mode in res:
+                res[mode]["speedup_vs_cpu_decode"] = res[mode]["decode_tok_s"] / cpu
+                res[mode]["speedup_vs_cpu_prefill"] = res[mode]["prefill_tok_s"] / res["cpu_reference"]["prefill_tok_s"]
     return res
+
+
+def cpu_model_baseline(path, prompt, max_seq: int, n_prefill: int = 128) -> dict:
+    """The reference's own kernels (oracle/_ref, its thread pool) driven by the
+    restated orchestrator on the same model file: prefill tok/s over the
+    first `n_prefill` prompt tokens, and decode tok/s of forward_token at the
+    positions the GPU decode covers (5 steps at the start of the decode
+    range and 5 at its end; a step's time does not depend on the cache's
+    contents, only on its length)."""
+    from oracle.oracle import REF_NATIVE_SO, OracleModel
+    ref = OracleModel(path, max_seq, REF_NATIVE_SO)
+    try:
+        t0 = time.perf_counter()
+        ref.prefill(prompt[:n_prefill])
+        prefill_s = time.perf_counter() - t0
+        start = len(prompt)
+        positions = list(range(start, start + 5)) + list(range(max_seq - 5, max_seq))
+        t0 = time.perf_counter()
+        for p in positions:
+            ref.forward_token(int(prompt[p % len(prompt)]), p)
+        decode_s = time.perf_counter() - t0
+    finally:
+        ref.close()
+    return {"decode_tok_s": len(positions) / decode_s, "prefill_tok_s": n_prefill / prefill_s, "kind": ref.kind,
+            "host": host_info(),
+            "sample": f"prefill of {n_prefill} prompt tokens; forward_token at positions {positions[0]}-"
+                      f"{positions[4]} and {positions[5]}-{positions[-1]} of the {max_seq}-position cache"}
 
 
 def tp_decode_bench(args, torch, dist, rank: int, world: int, local: int) -> dict:
@@ -538,6 +636,12 @@ def run_gpu(args) -> None:
         if not args.no_sweep:
             lib.gncx_set_weight_prefetch(0)  # each sweep entry is timed alone
             line["sweep"] = format_sweep(torch, lib, P)
+            lib.gncx_set_weight_prefetch(1)
+            try:
+                line["gemv_kernel_only"] = gemv_kernel_sweep(torch, lib, P)
+            except Exception as exc:  # reported; the GEMV numbers stand
+                line["gemv_kernel_only"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+            lib.gncx_set_weight_prefetch(0)
             try:
                 line["attention"] = attention_sweep(torch, lib, P)
             except Exception as exc:  # reported; the GEMV numbers stand

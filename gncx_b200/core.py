@@ -105,6 +105,7 @@ _SIGS = {
     "gncx_matvec_preq": (c_int32, [P, c_size_t, c_int32, P, c_int32, c_int32, P]),
     "gncx_dequantize_rows": (c_int32, [P, c_size_t, c_int32, c_int32, c_int32, P]),
     "gncx_sample_greedy": (c_int32, [P, c_int32, POINTER(c_int32), c_int32, c_double]),
+    "gncx_attention_prefill": (c_int32, [P, P, P, c_int32, c_int32, c_int32, c_int32, c_int32, c_float, P]),
     "gncx_mqa_attention_step_noalloc": (c_int32, [P, P, P, P, P, c_int32, c_int32, c_int32, c_int32, c_float,
                                                   c_int32, c_int32, P, P]),
     # model engine

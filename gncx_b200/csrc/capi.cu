@@ -634,7 +634,7 @@ void gncx_mqa_attention_step_ext(const float* q_vec, const float* k_vec, const f
     GNCX_CHECK(kc);
     GNCX_CHECK(vc);
     GNCX_CHECK(out);
-    if (pos < 0 || n_kv <= 0 || hd <= 0) {
+    if (pos < 0 || !attention_shape_ok(n_heads, n_kv, hd)) {  // rejected before the KV write
         finish(kErrInvalidArg);
         return;
     }
@@ -654,6 +654,61 @@ void gncx_mqa_attention_step_ext(const float* q_vec, const float* k_vec, const f
     float* scores = g_exact_attention ? reinterpret_cast<float*>(ws + part_bytes) : nullptr;
     finish(attention_launch(q, kc, vc, pos, n_heads, n_kv, hd, attn_scale, window, out, AttnScratch{part, recs},
                             g_rt.d_err, stream(), scores));
+}
+
+// Causal attention of a block of prompt positions: the reference's prefill
+// calls gncx_mqa_attention_step_ext once per position (write_kv = 0, no
+// window; lua/gncx_streamer.lua:1079-1109); here every query of the block
+// runs in one launch per group of kPfGroup positions.
+constexpr int kPfGroup = 256;
+constexpr int kPfChunkApi = 64;
+int32_t gncx_attention_prefill(const float* q, const float* k_cache, const float* v_cache, int32_t pos0, int32_t n_tok,
+                               int32_t n_heads, int32_t n_kv, int32_t hd, float attn_scale, float* out) {
+    if (ensure_init() != kOk) return g_status;
+    const float* qq = xl(q);
+    const float* kc = xl(k_cache);
+    const float* vc = xl(v_cache);
+    if (check_dev(qq, "q") || check_dev(kc, "k_cache") || check_dev(vc, "v_cache") || check_dev(out, "out"))
+        return g_status;
+    if (pos0 < 0 || n_tok <= 0 || !attention_shape_ok(n_heads, n_kv, hd)) {
+        set_error(kErrInvalidArg, "gncx_attention_prefill: bad position, count or head shape");
+        return kErrInvalidArg;
+    }
+    const int32_t last = pos0 + n_tok - 1;
+    const size_t splits = (size_t)(last + kPfChunkApi) / kPfChunkApi;
+    const size_t grp = n_tok < kPfGroup ? (size_t)n_tok : (size_t)kPfGroup;
+    const size_t part_bytes = align256(grp * n_heads * splits * attn_record_floats(hd) * 4);
+    const size_t score_bytes = g_exact_attention ? grp * n_heads * splits * kPfChunkApi * 4 : 0;
+    uint8_t* ws = workspace(part_bytes + score_bytes);
+    if (!ws) return g_status;
+    const int32_t qd = n_heads * hd;
+    for (int32_t z0 = 0; z0 < n_tok; z0 += kPfGroup) {
+        const int32_t nz = n_tok - z0 < kPfGroup ? n_tok - z0 : kPfGroup;
+        AttnArgs a{};
+        a.q = qq + (size_t)z0 * qd;
+        a.q_stride = qd;
+        a.kc = kc;
+        a.vc = vc;
+        a.kv_pos_stride = n_kv * hd;  // the reference's [pos][n_kv][head_dim]
+        a.kv_head_stride = hd;
+        a.pos0 = pos0 + z0;
+        a.n_heads = n_heads;
+        a.n_kv = n_kv;
+        a.hd = hd;
+        a.scale = attn_scale;
+        a.chunk = kPfChunkApi;
+        a.max_splits = (pos0 + z0 + nz + kPfChunkApi - 1) / kPfChunkApi;
+        a.part = reinterpret_cast<float*>(ws);
+        a.out = out + (size_t)z0 * qd;
+        a.out_stride = qd;
+        a.err = g_rt.d_err;
+        a.exact = g_exact_attention ? 1 : 0;
+        a.scores = g_exact_attention ? reinterpret_cast<float*>(ws + part_bytes) : nullptr;
+        a.score_cap = a.max_splits * kPfChunkApi;
+        const int st = attention_run(a, nz, stream());
+        if (st != kOk) return finish(st);
+    }
+    return finish(kOk);
 }
 
 void gncx_mqa_attention_step(const float* q_vec, const float* k_vec, const float* v_vec, float* k_cache,

@@ -196,6 +196,19 @@ int32_t gncx_sample_greedy(const float* logits, int32_t vocab, const int32_t* re
  * calls on a device share the array, so calls whose GPU work overlaps race
  * and must be serialised by the caller.  A call rejected with a status has
  * not written the KV cache.  Returns a status. */
+/* Causal attention over a block of prompt positions (no reference
+ * counterpart as one call; it replaces the per-position loop of the
+ * reference's prefill, lua/gncx_streamer.lua:1079-1109, which calls
+ * gncx_mqa_attention_step_ext with write_kv = 0 and no window):
+ * n_tok queries at positions pos0 .. pos0 + n_tok - 1, query z attending to
+ * cache rows 0 .. pos0 + z.  q and out are [n_tok][n_heads * head_dim]; the
+ * caches use the reference layout [pos][n_kv][head_dim] and already hold
+ * rows 0 .. pos0 + n_tok - 1.  Follows gncx_set_exact_attention.  Returns a
+ * status. */
+int32_t gncx_attention_prefill(const float* q, const float* k_cache, const float* v_cache, int32_t pos0,
+                               int32_t n_tok, int32_t n_heads, int32_t n_kv, int32_t head_dim, float attn_scale,
+                               float* out);
+
 int32_t gncx_mqa_attention_step_noalloc(const float* q_vec, const float* k_vec, const float* v_vec,
                                         float* k_cache_layer, float* v_cache_layer, int32_t pos, int32_t n_heads,
                                         int32_t n_kv_heads, int32_t head_dim, float attn_scale,

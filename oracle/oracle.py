@@ -261,6 +261,12 @@ class RefLib:
         return out
 
 
+def ref_build_flags(so: Path) -> str:
+    """The compiler and flags a reference library under _ref/ was built with."""
+    f = Path(str(so) + ".flags")
+    return f.read_text().strip() if f.exists() else "unknown"
+
+
 def reference_available(strict: bool = True) -> bool:
     return (REF_STRICT_SO if strict else REF_NATIVE_SO).exists()
 

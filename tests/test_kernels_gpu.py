@@ -345,3 +345,81 @@ def test_sample_greedy(gpu, oracle):
         got = gpu.gncx_sample_greedy(P(dev(logits)), 151936, rc, recent.size, 1.15)
         core.check(gpu)
         assert got == oracle.sample_greedy(logits, recent, 1.15)
+
+
+# ---------------------------------------------------------------- headline GEMV instantiations
+@pytest.mark.parametrize("t", [Q4_K, Q4_0, Q8_0])
+def test_gemv_headline_shape(gpu, oracle, t):
+    """151936 x 4096, the shape whose launch carries the bench's roofline:
+    at >= 16 eight-warp tiles per SM the launcher takes the 4-warp, two
+    CTAs per SM instantiation (aligned rows, fp32 x re-quantized in the
+    kernel), csrc/gncx_llm_kernels.cpp:1362-1431."""
+    w = synth.random_weights_fast(t, 151936, 4096, seed=100 + t)
+    x = synth.random_activations(4096, seed=101)
+    x[1024:1056] = 0.0  # an all-zero act block
+    assert np.array_equal(matvec(gpu, dev(w), t, x, 151936), oracle.matvec(w, t, x, 151936))
+
+
+@pytest.mark.parametrize("t", [Q4_K, Q6_K])
+def test_gemv_headline_shape_staged_act(gpu, oracle, t):
+    """The same shape fed a pre-quantized (staged) activation vector, as the
+    engine's LM head and decode GEMVs are."""
+    w = synth.random_weights_fast(t, 151936, 4096, seed=200 + t)
+    x = synth.random_activations(4096, seed=201)
+    a = torch.zeros(4096 // 32 * 48, dtype=torch.uint8, device="cuda")
+    _KEEP.append(a)
+    assert gpu.gncx_act_quantize(P(dev(x)), 1, 4096, P(a)) == 0
+    y = out(151936)
+    assert gpu.gncx_matvec_preq(P(dev(w)), 0, t, P(a), 4096, 151936, P(y)) == 0
+    assert np.array_equal(host(y), oracle.matvec(w, t, x, 151936))
+
+
+# ---------------------------------------------------------------- causal prefill attention
+def _prefill_rows(n_tok):
+    """Rows to check against the oracle: the first 70, every chunk and group
+    edge, a stride through the middle, the last."""
+    rows = set(range(min(70, n_tok)))
+    for e in (63, 64, 65, 127, 128, 129, 255, 256, 257, 511, 512, 513, 1023, 1024, 1025, 1535, 2047):
+        if e < n_tok:
+            rows.add(e)
+    rows.update(range(0, n_tok, 29))
+    rows.add(n_tok - 1)
+    return sorted(rows)
+
+
+@pytest.mark.parametrize("nh,nkv,hd,pos0,n_tok", [(32, 8, 128, 0, 2048), (32, 8, 128, 300, 333), (16, 8, 64, 0, 600),
+                                                  (6, 2, 96, 5, 300)])
+@pytest.mark.parametrize("exact", [0, 1])
+def test_attention_prefill(gpu, oracle, nh, nkv, hd, pos0, n_tok, exact):
+    """The causal prefill kernel (query-tiled, split records merged per query)
+    row by row against the reference's decode step at that row's position
+    (csrc/gncx_llm_kernels.cpp:1887-1994 called per prompt position,
+    lua/gncx_streamer.lua:1079-1109).  32/8 x 128 and 16/8 x 64 take the
+    query-tiled kernel; 6/2 x 96 the general split kernel; exact mode the
+    serial-order kernels."""
+    if exact and n_tok > 1000:
+        pytest.skip("exact mode: the shorter prompts cover it")
+    total = pos0 + n_tok
+    kvd = nkv * hd
+    kc_np = synth.random_activations(total * kvd, seed=total)
+    vc_np = synth.random_activations(total * kvd, seed=total + 1)
+    q = synth.random_activations(nh * hd, seed=nh + hd, rows=n_tok)
+    scale = float(np.float32(1.0 / np.sqrt(hd)))
+    y = out(n_tok * nh * hd)
+    gpu.gncx_set_exact_attention(exact)
+    try:
+        st = gpu.gncx_attention_prefill(P(dev(q)), P(dev(kc_np)), P(dev(vc_np)), pos0, n_tok, nh, nkv, hd, scale, P(y))
+        assert st == 0, (gpu.gncx_last_error_message() or b"").decode()
+    finally:
+        gpu.gncx_set_exact_attention(0)
+    got = host(y).reshape(n_tok, nh * hd)
+    worst = 0.0
+    for z in _prefill_rows(n_tok):
+        pos = pos0 + z
+        ref, _, _ = oracle.attention(q[z], None, None, kc_np[:(pos + 1) * kvd], vc_np[:(pos + 1) * kvd], pos, nh, nkv,
+                                     hd, scale, 0, 0)
+        err = np.max(np.abs(got[z] - ref)) / np.max(np.abs(ref))
+        worst = max(worst, err)
+        assert err <= ATTN_TOL, (z, err)
+    assert np.all(np.isfinite(got))
+    print(f"prefill attention {nh}/{nkv}x{hd} pos0={pos0} n={n_tok} exact={exact}: worst rel err {worst:.2e}")
