@@ -131,9 +131,9 @@ def host_info() -> dict:
         usable = len(os.sched_getaffinity(0))
     except AttributeError:
         usable = logical
-    from oracle.oracle import REF_NATIVE_SO, ref_build_flags
+    from oracle.oracle import ref_build_flags, timing_reference_so
     return {"cpu_model": model, "isa": isa, "logical_cpus": logical, "usable_cpus": usable,
-            "reference_pool_threads": max(2, min(usable, 12)), "reference_build": ref_build_flags(REF_NATIVE_SO)}
+            "reference_pool_threads": max(2, min(usable, 12)), "reference_build": ref_build_flags(timing_reference_so())}
 
 
 def gen_weights_gpu(torch, t: int, out_dim: int, in_dim: int, seed: int):
@@ -174,9 +174,10 @@ def read_traffic() -> float | None:
 def cpu_baseline(seconds: float = 8.0) -> dict:
     """The reference's CPU matvec (oracle/_ref, as-shipped flags) on the Q4_K sweep."""
     from gncx_b200 import synth
-    from oracle.oracle import REF_NATIVE_SO, Oracle, RefLib
-    kind = "reference" if REF_NATIVE_SO.exists() else "port"
-    impl = RefLib(REF_NATIVE_SO) if kind == "reference" else Oracle()
+    from oracle.oracle import Oracle, RefLib, timing_reference_so
+    so = timing_reference_so()
+    kind = "reference" if so.exists() else "port"
+    impl = RefLib(so) if kind == "reference" else Oracle()
     cores = max(2, min(os.cpu_count() or 1, 12)) if kind == "reference" else 1  # the port is one thread
     data = []
     for i, (o, n) in enumerate(SHAPES):
@@ -200,9 +201,10 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     from gncx_b200 import synth
-    from oracle.oracle import REF_NATIVE_SO, Oracle, RefLib
-    kind = "reference" if REF_NATIVE_SO.exists() else "port"
-    impl = RefLib(REF_NATIVE_SO) if kind == "reference" else Oracle()
+    from oracle.oracle import Oracle, RefLib, timing_reference_so
+    so = timing_reference_so()
+    kind = "reference" if so.exists() else "port"
+    impl = RefLib(so) if kind == "reference" else Oracle()
     cores = max(2, min(os.cpu_count() or 1, 12)) if kind == "reference" else 1  # the port is one thread
     data = [(synth.random_weights_fast(12, o, n, seed=10 + i), synth.random_activations(n, seed=20 + i), o)
             for i, (o, n) in enumerate(SHAPES)]
@@ -399,8 +401,8 @@ def cpu_model_baseline(path, prompt, max_seq: int, n_prefill: int = 128) -> dict
     positions the GPU decode covers (5 steps at the start of the decode
     range and 5 at its end; a step's time does not depend on the cache's
     contents, only on its length)."""
-    from oracle.oracle import REF_NATIVE_SO, OracleModel
-    ref = OracleModel(path, max_seq, REF_NATIVE_SO)
+    from oracle.oracle import OracleModel, timing_reference_so
+    ref = OracleModel(path, max_seq, timing_reference_so())
     try:
         t0 = time.perf_counter()
         ref.prefill(prompt[:n_prefill])

@@ -41,15 +41,20 @@ def _stale(obj: Path, src: Path) -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
-def build(verbose: bool = False, force: bool = False) -> Path:
-    OUT_DIR.mkdir(exist_ok=True)
+def build(verbose: bool = False, force: bool = False, trace: bool = False) -> Path:
+    """Compile the library; `trace` builds the diagnostic variant with kernel
+    timeline records (trace.cuh) as libgncx_llm_core_trace.so instead."""
+    out_dir = OUT_DIR.with_name(OUT_DIR.name + "_trace") if trace else OUT_DIR
+    lib = LIB.with_name(LIB.stem + "_trace.so") if trace else LIB
+    flags = NVCC_FLAGS + (["-DGNCX_TRACE"] if trace else [])
+    out_dir.mkdir(exist_ok=True)
     nvcc = _nvcc()
     srcs = [CSRC / s for s in SOURCES if (CSRC / s).exists()]
     jobs = []
     for s in srcs:
-        obj = OUT_DIR / (s.stem + ".o")
+        obj = out_dir / (s.stem + ".o")
         if force or _stale(obj, s):
-            jobs.append([nvcc, *NVCC_FLAGS, "-c", str(s), "-o", str(obj)])
+            jobs.append([nvcc, *flags, "-c", str(s), "-o", str(obj)])
 
     def run(cmd):
         r = subprocess.run(cmd, capture_output=True, text=True)
@@ -60,12 +65,12 @@ def build(verbose: bool = False, force: bool = False) -> Path:
 
     with ThreadPoolExecutor(max_workers=min(8, max(1, len(jobs)))) as ex:
         list(ex.map(run, jobs))
-    objs = [str(OUT_DIR / (s.stem + ".o")) for s in srcs]
-    if jobs or not LIB.exists() or force:
-        run([nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", str(LIB), *objs,
+    objs = [str(out_dir / (s.stem + ".o")) for s in srcs]
+    if jobs or not lib.exists() or force:
+        run([nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", str(lib), *objs,
              "-lcudart", "-ldl"])
-    return LIB
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(verbose=True, force="--force" in sys.argv))
+    print(build(verbose=True, force="--force" in sys.argv, trace="--trace" in sys.argv))

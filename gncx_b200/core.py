@@ -12,6 +12,7 @@ machine without a GPU records GNCX_ERR_NO_DEVICE and :func:`check` raises.
 from __future__ import annotations
 
 import ctypes
+import os
 from ctypes import POINTER, c_char_p, c_double, c_float, c_int32, c_size_t, c_uint8, c_uint64, c_void_p
 from pathlib import Path
 
@@ -105,6 +106,7 @@ _SIGS = {
     "gncx_matvec_preq": (c_int32, [P, c_size_t, c_int32, P, c_int32, c_int32, P]),
     "gncx_dequantize_rows": (c_int32, [P, c_size_t, c_int32, c_int32, c_int32, P]),
     "gncx_sample_greedy": (c_int32, [P, c_int32, POINTER(c_int32), c_int32, c_double]),
+    "gncx_trace_enable": (c_int32, [P, P, ctypes.c_uint32]),
     "gncx_attention_prefill": (c_int32, [P, P, P, c_int32, c_int32, c_int32, c_int32, c_int32, c_float, P]),
     "gncx_mqa_attention_step_noalloc": (c_int32, [P, P, P, P, P, c_int32, c_int32, c_int32, c_int32, c_float,
                                                   c_int32, c_int32, P, P]),
@@ -134,7 +136,8 @@ def load(path: str | Path | None = None) -> ctypes.CDLL:
     global _lib
     if _lib is not None and path is None:
         return _lib
-    p = Path(path) if path else LIB_PATH
+    # GNCX_LIB names another build of the library (e.g. the tracing one)
+    p = Path(path) if path else Path(os.environ.get("GNCX_LIB") or LIB_PATH)
     if not p.exists():
         raise FileNotFoundError(f"{p} is missing: build it with `python -m gncx_b200.build` "
                                 "(this package has no CPU fallback)")

@@ -31,6 +31,7 @@
 #include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "trace.cuh"
 #include "launch.cuh"
 #include "norm.cuh"
 
@@ -251,6 +252,7 @@ __device__ __forceinline__ void warp_head_norm_rope(float* x, int hd, const floa
 template <bool VEC, bool SCORES_ONLY>
 __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnArgs a) {
     extern __shared__ __align__(16) uint8_t smraw[];
+    GNCX_TRACE_SCOPE(kTagAttnPartial, gridDim.x);
     const int z = blockIdx.z;
     int t0, len;
     attn_window(a, z, t0, len);
@@ -301,7 +303,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
         }
     };
     if (n_old > 0) stage_rows(0, n_old);
+    if (tid == 0) GNCX_TRACE_MARK(10, n_old);
     pdl_wait();
+    if (tid == 0) GNCX_TRACE_MARK(11, 0);
     // with the fused post step the query's own row (the last of the window) is
     // made here, not loaded
     const int pn = t0 + len - 1 - (t0 + c0);  // the query's position within this chunk
@@ -334,8 +338,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
                     const_cast<float*>(a.kc)[(size_t)pos * ps + (size_t)kvh * a.kv_head_stride + i] = x[i];
         }
     }
+    if (tid == 0) GNCX_TRACE_MARK(12, 0);
     if (VEC) cp_async_wait<0>();
     __syncthreads();
+    if (tid == 0) GNCX_TRACE_MARK(13, 0);
 
     // ---- scores (the reference's eight chains per dot) ----
     if (SCORES_ONLY) {
@@ -352,6 +358,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
     }
     __syncthreads();
 
+    if (tid == 0) GNCX_TRACE_MARK(14, 0);
     // ---- per head: chunk max, exp (position-major copy for the PV), sum ----
     for (int g = warp; g < G; g += kAttnThreads / 32) {
         float mx = -INFINITY;
@@ -369,6 +376,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
     for (int i = tid; i < cn * (G4 - G); i += kAttnThreads) es[(size_t)(i / (G4 - G)) * G4 + G + i % (G4 - G)] = 0.0f;
     __syncthreads();
 
+    if (tid == 0) GNCX_TRACE_MARK(15, 0);
     // ---- o[g][d] = sum_p e[p][g] * v[p][d] ----
     const int npg = kAttnThreads / hd > 0 ? kAttnThreads / hd : 1;
     const int d = tid % hd, pg = tid / hd;
@@ -393,8 +401,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
 __global__ void attn_combine_kernel(const AttnArgs a) {
     extern __shared__ float wsm[];  // [max_splits] weights, then [max_splits] sums
     __shared__ float s_inv[1];
+    GNCX_TRACE_SCOPE(kTagAttnCombine, gridDim.x);
     pdl_launch_dependents();
     pdl_wait();
+    if (threadIdx.x == 0) GNCX_TRACE_MARK(30, 0);
     const int h = blockIdx.x, z = blockIdx.y;
     int t0, len;
     attn_window(a, z, t0, len);
@@ -420,6 +430,7 @@ static size_t attn_prefill_smem_bytes(int hd) {
 template <int HD>
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_prefill_kernel(const AttnArgs a) {
     extern __shared__ __align__(16) float psm[];
+    GNCX_TRACE_SCOPE(kTagAttnPrefill, gridDim.x);
     constexpr int RS = HD + kRowPad;
     constexpr int SL = kPfChunk + 4;
     const int G = a.n_heads / a.n_kv;
@@ -567,6 +578,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_prefill_kernel(const Att
 // scores are replaced by p_t = e_t * inv.  One CTA per (head, query).
 constexpr int kExactThreads = 256;
 __global__ void __launch_bounds__(kExactThreads) attn_exact_softmax_kernel(const AttnArgs a) {
+    GNCX_TRACE_SCOPE(kTagAttnExactSoftmax, gridDim.x);
     pdl_launch_dependents();
     pdl_wait();
     const int h = blockIdx.x, z = blockIdx.y;
@@ -613,6 +625,7 @@ constexpr int kExactTile = 64;
 constexpr int kExactHeads = kExactThreads / kExactSlice;  // 8
 template <bool VEC>
 __global__ void __launch_bounds__(kExactThreads) attn_exact_pv_kernel(const AttnArgs a) {
+    GNCX_TRACE_SCOPE(kTagAttnExactPv, gridDim.x);
     pdl_launch_dependents();
     pdl_wait();
     __shared__ __align__(16) float vt[2][kExactTile][kExactSlice];

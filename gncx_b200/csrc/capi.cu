@@ -17,6 +17,7 @@
 
 #include "../../include/gncx_llm_core.h"
 #include "kernels.h"
+#include "trace.cuh"
 
 namespace gncx {
 
@@ -72,6 +73,16 @@ const DeviceInfo& device_info() {
         cudaDeviceGetAttribute(&d.l2_bytes, cudaDevAttrL2CacheSize, dev);
     }
     return d;
+}
+
+// Timeline-record binders of the translation units built with tracing.
+static std::vector<void (*)(TraceRec*, unsigned*, unsigned)>& trace_binders() {
+    static std::vector<void (*)(TraceRec*, unsigned*, unsigned)> v;
+    return v;
+}
+int trace_register(void (*bind)(TraceRec*, unsigned*, unsigned)) {
+    trace_binders().push_back(bind);
+    return (int)trace_binders().size();
 }
 
 cudaError_t set_smem_limit(const void* k, size_t bytes) {
@@ -242,6 +253,25 @@ void gncx_clear_error(void) {
     std::lock_guard<std::mutex> lock(g_status_mu);
     g_status = kOk;
     g_message.clear();
+}
+
+int32_t gncx_trace_enable(void* records, uint32_t* counter, uint32_t capacity) {
+    if (ensure_init() != kOk) return g_status;
+    if (trace_binders().empty()) {
+        set_error(kErrInvalidArg, "gncx_trace_enable: this library was built without timeline tracing");
+        return kErrInvalidArg;
+    }
+    if ((records == nullptr) != (counter == nullptr)) {
+        set_error(kErrInvalidArg, "gncx_trace_enable: records and counter go together");
+        return kErrInvalidArg;
+    }
+    for (auto bind : trace_binders()) bind(static_cast<TraceRec*>(records), counter, records ? capacity : 0);
+    const cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        set_error(kErrCuda, cuda_msg(e));
+        return kErrCuda;
+    }
+    return kOk;
 }
 
 int32_t gncx_sync(void) {

@@ -13,6 +13,7 @@
 #include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "trace.cuh"
 #include "launch.cuh"
 #include "norm.cuh"
 
@@ -28,6 +29,7 @@ __global__ void __launch_bounds__(256) add_norm_quant_kernel(float* hidden, cons
                                                              const float* __restrict__ w, int dim, float eps,
                                                              ActOut act, float* normed) {
     extern __shared__ float xs[];
+    GNCX_TRACE_SCOPE(kTagAddNormQuant, gridDim.x);
     const size_t base = (size_t)blockIdx.x * dim;
     for (int i = threadIdx.x; i < dim; i += blockDim.x) {
         float v = hidden[base + i];
@@ -61,6 +63,7 @@ __global__ void __launch_bounds__(kRowThreads) add_norm_quant_row_kernel(float* 
                                                                          const float* __restrict__ w, int dim,
                                                                          float eps, uint8_t* staged, float* normed) {
     extern __shared__ __align__(16) float sq[];  // [4][dim/4]
+    GNCX_TRACE_SCOPE(kTagAddNormQuantRow, dim);
     const int tid = threadIdx.x;
     const int n4 = dim >> 2;
     float g[kRowPasses][8];
@@ -74,8 +77,10 @@ __global__ void __launch_bounds__(kRowThreads) add_norm_quant_row_kernel(float* 
             g[ps][4] = b.x; g[ps][5] = b.y; g[ps][6] = b.z; g[ps][7] = b.w;
         }
     }
+    if (tid == 0) GNCX_TRACE_MARK(20, 0);
     pdl_launch_dependents();
     pdl_wait();
+    if (tid == 0) GNCX_TRACE_MARK(21, 0);
     float x[kRowPasses][8];
 #pragma unroll
     for (int ps = 0; ps < kRowPasses; ++ps) {
@@ -102,7 +107,9 @@ __global__ void __launch_bounds__(kRowThreads) add_norm_quant_row_kernel(float* 
         }
     }
     __syncthreads();
+    if (tid == 0) GNCX_TRACE_MARK(22, 0);
     const float inv = rms_inv_sq(sq, n4, eps);
+    if (tid == 0) GNCX_TRACE_MARK(23, 0);
     const int q4 = tid & 3;
     float4* rec = reinterpret_cast<float4*>(staged + dim);
 #pragma unroll
@@ -179,6 +186,7 @@ __global__ void qkv_post_kernel(float* qkv, int row_stride, int nh, int nkv, int
                                 const float* __restrict__ stab, int pos0, const int* pos_dev, float* kc, float* vc,
                                 int64_t kps, int64_t khs) {
     extern __shared__ float xs[];
+    GNCX_TRACE_SCOPE(kTagQkvPost, gridDim.x);
     pdl_launch_dependents();
     pdl_wait();
     const int x = blockIdx.x, r = blockIdx.y;
@@ -232,8 +240,10 @@ int qkv_post_launch(float* qkv, int32_t row_stride, int32_t rows, int32_t nh, in
 // One warp per 32-output block: out = glu(gate, up), re-quantized for ffn_down.
 __global__ void glu_quant_kernel(const float* __restrict__ g, const float* __restrict__ u, int stride, int ffn,
                                  int rows, int gelu, ActOut act, float* out, int out_stride) {
+    GNCX_TRACE_SCOPE(kTagGluQuant, ffn);
     pdl_launch_dependents();
     pdl_wait();
+    if (threadIdx.x == 0) GNCX_TRACE_MARK(40, 0);
     const int lane = threadIdx.x & 31;
     const int nbf = ffn >> 5;
     const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -289,6 +299,7 @@ __device__ Best am_block_best(Best p) {
 
 __global__ void am_state_stage1(const float* __restrict__ logits, int vocab, const DecodeState* st, double penalty,
                                 double* part_v, int* part_i) {
+    GNCX_TRACE_SCOPE(kTagArgmax1, vocab);
     pdl_launch_dependents();
     pdl_wait();  // the logits come from the preceding kernel
     const int per = (vocab + gridDim.x - 1) / gridDim.x;
@@ -315,6 +326,7 @@ __global__ void am_state_stage1(const float* __restrict__ logits, int vocab, con
 
 __global__ void am_state_stage2(const double* part_v, const int* part_i, int n, DecodeState* st, int32_t* out_ids,
                                 int advance_pos) {
+    GNCX_TRACE_SCOPE(kTagArgmax2, n);
     pdl_launch_dependents();
     pdl_wait();
     Best b{-1e30, 0};

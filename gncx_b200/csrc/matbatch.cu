@@ -13,6 +13,7 @@
 #include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "trace.cuh"
 #include "units.cuh"
 
 namespace gncx {
@@ -36,6 +37,7 @@ __global__ void __launch_bounds__(kMbThreads) matbatch_kernel(const uint8_t* __r
                                                                const ActBlock* __restrict__ act, int batch,
                                                                int in_dim, int out_dim, float* __restrict__ y,
                                                                int ldy) {
+    GNCX_TRACE_SCOPE(kTagMatbatch, out_dim);
     constexpr int UB = Fmt<T>::UB, NW = Fmt<T>::NW, E = Fmt<T>::E;
     constexpr int WS = (UB + 3) / 4 + 2;  // staged words per row (aligned cover + look-ahead)
     __shared__ __align__(16) uint32_t wsm[kMbRows * WS];

@@ -31,6 +31,7 @@
 #include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "trace.cuh"
 #include "tma.cuh"
 #include "units.cuh"
 
@@ -187,6 +188,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
                                                                     const ActBlock* __restrict__ act, int batch,
                                                                     int in_dim, int out_dim, float* __restrict__ y,
                                                                     int ldy, int32_t* err) {
+    GNCX_TRACE_SCOPE(kTagMatbatchTc, out_dim);
     constexpr int UB = TcFmt<T>::UB;
     constexpr int NQ = UB / 16;           // 16-byte pieces of a row's unit
     constexpr int NE = kTcEpiWarps * 32;  // epilogue threads

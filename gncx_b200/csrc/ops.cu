@@ -6,6 +6,7 @@
 #include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
+#include "trace.cuh"
 #include "launch.cuh"
 #include "norm.cuh"
 
@@ -115,6 +116,7 @@ __device__ __forceinline__ float dequant_elem(const uint8_t* row, int32_t type, 
 
 __global__ void dequant_kernel(const uint8_t* __restrict__ w, int32_t type, int32_t rows, int32_t n, float scale,
                                const int32_t* __restrict__ row_ids, float* __restrict__ out) {
+    GNCX_TRACE_SCOPE(kTagDequant, rows);
     pdl_launch_dependents();
     pdl_wait();  // row ids (the decode step's token) come from the preceding kernel
     const size_t rb = row_bytes(type, n);

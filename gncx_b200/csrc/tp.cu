@@ -18,6 +18,7 @@
 #include <string.h>
 
 #include "kernels.h"
+#include "trace.cuh"
 #include "launch.cuh"
 #include "tma.cuh"
 
@@ -57,6 +58,7 @@ struct GatherArgs {
 // same grid for the same gather, so when all CTAs are through, every peer's
 // slice has landed here.  No cross-CTA counter, one system fence per CTA.
 __global__ void __launch_bounds__(kTpThreads) tp_gather_kernel(const GatherArgs a) {
+    GNCX_TRACE_SCOPE(kTagTpGather, a.rows);
     pdl_launch_dependents();  // the next kernel may start streaming its weights
     pdl_wait();               // the slice comes from the preceding kernel
     const float* src = reinterpret_cast<const float*>(a.region[a.rank] + a.buf);
@@ -113,6 +115,7 @@ struct LlArgs {
 };
 
 __global__ void __launch_bounds__(kTpThreads) tp_ll_gather_kernel(const LlArgs a) {
+    GNCX_TRACE_SCOPE(kTagTpGatherLl, a.row_floats);
     pdl_launch_dependents();
     pdl_wait();  // this rank's slice comes from the preceding kernel
     __shared__ uint32_t s_ep;

@@ -145,7 +145,14 @@ enum {
 int32_t gncx_last_error(void);               /* first error since the last clear (sticky) */
 const char* gncx_last_error_message(void);
 void gncx_clear_error(void);
-int32_t gncx_sync(void);                     /* wait for queued work; returns and records its status */
+int32_t gncx_sync(void);
+/* Diagnostic builds only (libgncx_llm_core_trace.so; the product library
+ * returns GNCX_ERR_INVALID_ARG): from now on every kernel launch on the
+ * current device appends one 40-byte record per CTA -- grid id, kernel tag,
+ * an argument, CTA index, %globaltimer at entry and exit -- to the device
+ * buffer `records` (capacity records; `counter` is a device word the caller
+ * zeroes).  NULL, NULL stops recording.  No reference counterpart. */
+int32_t gncx_trace_enable(void* records, uint32_t* counter, uint32_t capacity);                     /* wait for queued work; returns and records its status */
 void gncx_set_stream(void* cuda_stream);     /* NULL = the library's own stream */
 void* gncx_get_stream(void);
 void gncx_set_synchronous(int32_t on);       /* 1 (default): reference-named calls wait before returning */

@@ -27,6 +27,30 @@ HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "_build" / "liboracle.so"
 REF_STRICT_SO = HERE / "_ref" / "libgncx_ref_strict.so"
 REF_NATIVE_SO = HERE / "_ref" / "libgncx_ref.so"
+REF_SPR_SO = HERE / "_ref" / "libgncx_ref_spr.so"
+# CPU flags a -march=sapphirerapids build may use in compiler-generated code
+_SPR_FLAGS = {"avx512f", "avx512dq", "avx512cd", "avx512bw", "avx512vl", "avx512ifma", "avx512vbmi", "avx512_vbmi2",
+              "avx512_vnni", "avx512_bitalg", "avx512_vpopcntdq", "avx512_bf16", "avx512_fp16", "amx_tile",
+              "amx_int8", "amx_bf16", "avx_vnni", "gfni", "vaes", "vpclmulqdq", "bmi2", "fma", "f16c", "movbe"}
+
+
+def _host_flags() -> set:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("flags"):
+                return set(line.split(":", 1)[1].split())
+    except OSError:
+        pass
+    return set()
+
+
+def timing_reference_so() -> Path:
+    """The reference build for timing on this host: the -march=sapphirerapids
+    one (what the shipped -march=native gives there) when the host has every
+    extension it may use, else the portable AVX2 one."""
+    if REF_SPR_SO.exists() and _SPR_FLAGS <= _host_flags():
+        return REF_SPR_SO
+    return REF_NATIVE_SO
 
 
 def reference_source() -> Path | None:
