@@ -28,16 +28,19 @@
 // kvh * kv_head_stride (the reference's [pos][n_kv][head_dim], or the engine's
 // head-major [n_kv][max_seq][head_dim]).
 #include <cuda_runtime.h>
+#include <stdlib.h>
 #include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
 #include "trace.cuh"
 #include "launch.cuh"
 #include "norm.cuh"
+#include "tma.cuh"
 
 namespace gncx {
 
-constexpr int kAttnThreads = 256;
+constexpr int kAttnThreads = 256;     // prefill / exact kernels
+constexpr int kAttnMaxThreads = 512;  // the split-KV partial kernel: 512 where head_dim <= 128
 constexpr int kMaxHeadDim = 256;
 constexpr int kRowPad = 4;    // floats of padding per staged K/V row
 constexpr int kScorePad = 8;  // floats of padding per score row
@@ -53,10 +56,10 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // Floats of the K/V staging area, which the position-group reduction of the
-// PV step reuses as scratch (kAttnThreads * 8 floats).
+// PV step reuses as scratch (up to kAttnMaxThreads * 8 floats).
 __host__ __device__ inline size_t attn_kv_floats(int hd, int chunk) {
     size_t n = (size_t)2 * chunk * (hd + kRowPad);
-    if ((size_t)kAttnThreads * 8 > n) n = (size_t)kAttnThreads * 8;
+    if ((size_t)kAttnMaxThreads * 8 > n) n = (size_t)kAttnMaxThreads * 8;
     return (n + 3) & ~(size_t)3;  // keeps the q rows that follow 16-byte aligned
 }
 
@@ -82,51 +85,73 @@ __device__ __forceinline__ float ld_l2(const float* p) {
     return v;
 }
 
-// Merge the n split records of heads h0 .. h0+G-1 of query z:
-// out = (sum_s o_s * e^(m_s-M)) / (sum_s l_s * e^(m_s-M) + 1e-12), serial in s.
-// `wsm` / `lsm` hold G*n floats each, `s_inv` G floats; called by whole CTAs.
-__device__ void attn_merge(const AttnArgs& a, int z, int h0, int G, int n, float* wsm, float* lsm, float* s_inv) {
+// Merge the n split records of head h of query z:
+// out = (sum_s o_s * e^(m_s-M)) / (sum_s l_s * e^(m_s-M) + 1e-12).  The split
+// sums are formed in parallel (the split-KV softmax is not in the reference's
+// serial order anyway): blockDim / head_dim groups of threads each take every
+// g-th split for one output column, then the groups' partial sums are added.
+// `wsm` / `lsm` hold n floats each, `osm` blockDim floats; whole CTAs call it.
+__device__ void attn_merge(const AttnArgs& a, int z, int h, int n, float* wsm, float* lsm, float* osm) {
     const int hd = a.hd;
     const size_t R = attn_record_floats(hd);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
-    for (int i = tid; i < G * n; i += nthr) {
-        const int g = i / n, s = i - g * n;
-        const float* rec = a.part + (((size_t)z * a.n_heads + h0 + g) * a.max_splits + s) * R;
-        wsm[i] = ld_l2(rec);
-        lsm[i] = ld_l2(rec + 1);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x, nwarps = nthr >> 5;
+    __shared__ float red[32];
+    __shared__ float s_max, s_inv;
+    const float* rec0 = a.part + ((size_t)z * a.n_heads + h) * a.max_splits * R;
+    float M = -INFINITY;
+    for (int s = tid; s < n; s += nthr) {
+        wsm[s] = ld_l2(rec0 + (size_t)s * R);
+        lsm[s] = ld_l2(rec0 + (size_t)s * R + 1);
+        M = fmaxf(M, wsm[s]);
+    }
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if (lane == 0) red[warp] = M;
+    __syncthreads();
+    if (tid == 0) {
+        float m = red[0];
+        for (int k = 1; k < nwarps; ++k) m = fmaxf(m, red[k]);
+        s_max = m;
     }
     __syncthreads();
-    for (int g = warp; g < G; g += nthr >> 5) {
-        float M = -INFINITY;
-        for (int s = lane; s < n; s += 32) M = fmaxf(M, wsm[g * n + s]);
-        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        for (int s = lane; s < n; s += 32) wsm[g * n + s] = exp_cr(fsub(wsm[g * n + s], M));
+    M = s_max;
+    float L = 0.0f;
+    for (int s = tid; s < n; s += nthr) {
+        const float wgt = exp_cr(fsub(wsm[s], M));
+        wsm[s] = wgt;
+        L = fadd(L, fmul(lsm[s], wgt));
     }
+    for (int o = 16; o > 0; o >>= 1) L = fadd(L, __shfl_xor_sync(0xffffffffu, L, o));
+    __syncthreads();  // red is reused
+    if (lane == 0) red[warp] = L;
     __syncthreads();
-    if (tid < G) {
-        float L = 0.0f;
-        for (int s = 0; s < n; ++s) L = fadd(L, fmul(lsm[tid * n + s], wsm[tid * n + s]));
-        s_inv[tid] = fdiv(1.0f, fadd(L, 1e-12f));
+    if (tid == 0) {
+        float l = 0.0f;
+        for (int k = 0; k < nwarps; ++k) l = fadd(l, red[k]);
+        s_inv = fdiv(1.0f, fadd(l, 1e-12f));
     }
-    __syncthreads();
-    for (int i = tid; i < G * hd; i += nthr) {
-        const int g = i / hd, d = i - g * hd;
-        const int h = h0 + g;
-        const float* rec = a.part + ((size_t)z * a.n_heads + h) * a.max_splits * R + 4 + d;
-        const float* w = wsm + g * n;
+    const int ng = nthr / hd > 0 ? nthr / hd : 1;
+    const int d = tid % hd, g = tid / hd;
+    if (g < ng && d < hd) {
+        const float* rec = rec0 + 4 + d;
         float o = 0.0f;
-        for (int s0 = 0; s0 < n; s0 += kMergeBatch) {
+        for (int s0 = g * kMergeBatch; s0 < n; s0 += ng * kMergeBatch) {
             float v[kMergeBatch];  // a batch of records in flight at once
 #pragma unroll
             for (int b = 0; b < kMergeBatch; ++b) v[b] = s0 + b < n ? ld_l2(rec + (size_t)(s0 + b) * R) : 0.0f;
 #pragma unroll
             for (int b = 0; b < kMergeBatch; ++b)
-                if (s0 + b < n) o = fadd(o, fmul(v[b], w[s0 + b]));
+                if (s0 + b < n) o = fadd(o, fmul(v[b], wsm[s0 + b]));
         }
-        o = fmul(o, s_inv[g]);
-        if (a.out) a.out[(size_t)z * a.out_stride + (size_t)h * hd + d] = o;
+        osm[g * hd + d] = o;
+    }
+    __syncthreads();
+    for (int i = tid; i < hd; i += nthr) {  // whole warps: hd % 32 == 0 when act is written
+        float o = osm[i];
+        for (int q = 1; q < ng; ++q) o = fadd(o, osm[q * hd + i]);
+        o = fmul(o, s_inv);
+        if (a.out) a.out[(size_t)z * a.out_stride + (size_t)h * hd + i] = o;
         if (a.act_out.blocks || a.act_out.staged)
-            act_out_store(a.act_out, o, a.n_heads * hd, (size_t)z, (h * hd + d) >> 5, d & 31);
+            act_out_store(a.act_out, o, a.n_heads * hd, (size_t)z, (h * hd + i) >> 5, i & 31);
     }
 }
 
@@ -249,8 +274,8 @@ __device__ __forceinline__ void warp_head_norm_rope(float* x, int hd, const floa
 }
 
 // Partial record per (query, head, split): [0] = max, [1] = sum of exp, [4..] = o[hd]
-template <bool VEC, bool SCORES_ONLY>
-__global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnArgs a) {
+template <bool VEC, bool SCORES_ONLY, int NT>
+__global__ void __launch_bounds__(NT) attn_partial_kernel(const AttnArgs a) {
     extern __shared__ __align__(16) uint8_t smraw[];
     GNCX_TRACE_SCOPE(kTagAttnPartial, gridDim.x);
     const int z = blockIdx.z;
@@ -277,6 +302,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
     const int lane = tid & 31, warp = tid >> 5;
     const size_t row0 = (size_t)(t0 + c0) * a.kv_pos_stride + (size_t)kvh * a.kv_head_stride;
     const size_t ps = (size_t)a.kv_pos_stride;
+    // with the fused post step the query's own row (the last of the window) is
+    // made here, not loaded
+    const int pn = t0 + len - 1 - (t0 + c0);  // the query's position within this chunk
+    const bool own_row = a.post_k && pn >= 0 && pn < cn;
+    const int n_load = own_row ? pn : cn;     // rows copied from the cache
 
     pdl_launch_dependents();
     // ---- stage K and V: rows written before the preceding kernel first (they
@@ -285,7 +315,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
     auto stage_rows = [&](int pa, int pb) {
         if (VEC) {
             // thread -> one 16-byte piece c of rows pa + p0, pa + p0 + step, ...
-            const int cpr = hd >> 2, step = kAttnThreads / cpr;
+            // (16-byte cp.async: per-row bulk copies measured slower -- the
+            // SM's copy engine serialises hundreds of 512-byte copies)
+            const int cpr = hd >> 2, step = NT / cpr;
             const int c = tid % cpr, p0 = tid / cpr;
             if (tid < step * cpr) {
                 for (int p = pa + p0; p < pb; p += step) {
@@ -295,7 +327,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
             }
             cp_async_commit();
         } else {
-            for (int i = tid; i < (pb - pa) * hd; i += kAttnThreads) {
+            for (int i = tid; i < (pb - pa) * hd; i += NT) {
                 const int p = pa + i / hd, d = i % hd;
                 ks[(size_t)p * rs + d] = a.kc[row0 + p * ps + d];
                 if (!SCORES_ONLY) vs[(size_t)p * rs + d] = a.vc[row0 + p * ps + d];
@@ -306,19 +338,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
     if (tid == 0) GNCX_TRACE_MARK(10, n_old);
     pdl_wait();
     if (tid == 0) GNCX_TRACE_MARK(11, 0);
-    // with the fused post step the query's own row (the last of the window) is
-    // made here, not loaded
-    const int pn = t0 + len - 1 - (t0 + c0);  // the query's position within this chunk
-    const bool own_row = a.post_k && pn >= 0 && pn < cn;
-    if (n_old < cn) stage_rows(n_old, own_row ? pn : cn);
+    if (n_old < n_load) stage_rows(n_old, n_load);
     const float* qz = a.q + (size_t)z * a.q_stride + (size_t)kvh * G * hd;
-    for (int i = tid; i < G * hd; i += kAttnThreads) qs[(size_t)(i / hd) * qrs + i % hd] = qz[i];
+    for (int i = tid; i < G * hd; i += NT) qs[(size_t)(i / hd) * qrs + i % hd] = qz[i];
     if (a.post_k) {
         const int pos = t0 + len - 1;
         if (own_row) {
             const float* kz = a.post_k + (size_t)kvh * hd;
             const float* vz = a.post_v + (size_t)kvh * hd;
-            for (int i = tid; i < hd; i += kAttnThreads) {
+            for (int i = tid; i < hd; i += NT) {
                 ks[(size_t)pn * rs + i] = kz[i];
                 const float v = vz[i];
                 if (!SCORES_ONLY) vs[(size_t)pn * rs + i] = v;
@@ -328,7 +356,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
         }
         __syncthreads();
         // warps 0..G-1: the group's q heads; warp G: the new K row
-        for (int task = warp; task < G + (own_row ? 1 : 0); task += kAttnThreads / 32) {
+        for (int task = warp; task < G + (own_row ? 1 : 0); task += NT / 32) {
             const bool isq = task < G;
             float* x = isq ? qs + (size_t)task * qrs : ks + (size_t)pn * rs;
             warp_head_norm_rope(x, hd, isq ? a.post_qn : a.post_kn, a.post_norm != 0, a.post_eps, a.rope_c, a.rope_s,
@@ -360,7 +388,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
 
     if (tid == 0) GNCX_TRACE_MARK(14, 0);
     // ---- per head: chunk max, exp (position-major copy for the PV), sum ----
-    for (int g = warp; g < G; g += kAttnThreads / 32) {
+    for (int g = warp; g < G; g += NT / 32) {
         float mx = -INFINITY;
         for (int p = lane; p < cn; p += 32) mx = fmaxf(mx, sc[g * sld + p]);
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -373,12 +401,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
         if (lane == 0) { red[2 * g] = mx; red[2 * g + 1] = sum; }
     }
-    for (int i = tid; i < cn * (G4 - G); i += kAttnThreads) es[(size_t)(i / (G4 - G)) * G4 + G + i % (G4 - G)] = 0.0f;
+    for (int i = tid; i < cn * (G4 - G); i += NT) es[(size_t)(i / (G4 - G)) * G4 + G + i % (G4 - G)] = 0.0f;
     __syncthreads();
 
     if (tid == 0) GNCX_TRACE_MARK(15, 0);
     // ---- o[g][d] = sum_p e[p][g] * v[p][d] ----
-    const int npg = kAttnThreads / hd > 0 ? kAttnThreads / hd : 1;
+    const int npg = NT / hd > 0 ? NT / hd : 1;
     const int d = tid % hd, pg = tid / hd;
     const bool active = pg < npg && d < hd && tid < npg * hd;
     for (int g0 = 0; g0 < G; g0 += kPvHeads) {
@@ -398,9 +426,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const AttnAr
 }
 
 // Merge the split records of one (query, head).
-__global__ void attn_combine_kernel(const AttnArgs a) {
-    extern __shared__ float wsm[];  // [max_splits] weights, then [max_splits] sums
-    __shared__ float s_inv[1];
+constexpr int kCombineThreads = 256;
+__global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(const AttnArgs a) {
+    extern __shared__ float wsm[];  // [max_splits] weights, [max_splits] sums, [kCombineThreads] partial outputs
     GNCX_TRACE_SCOPE(kTagAttnCombine, gridDim.x);
     pdl_launch_dependents();
     pdl_wait();
@@ -409,7 +437,7 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
     int t0, len;
     attn_window(a, z, t0, len);
     const int n = (len + a.chunk - 1) / a.chunk;
-    attn_merge(a, z, h, 1, n, wsm, wsm + a.max_splits, s_inv);
+    attn_merge(a, z, h, n, wsm, wsm + a.max_splits, wsm + 2 * a.max_splits);
 }
 
 // ---- causal prefill: one CTA per (chunk, KV head, tile of queries) ----
@@ -712,11 +740,20 @@ int attention_geometry_chunk(int32_t len, int32_t n_kv, int sm_count) {
     return c;
 }
 
+// 512 threads when head_dim <= 128 and the grid is at most two CTAs per SM
+// (decode at a few thousand positions: one score per thread for 128 positions
+// x 4 heads, four position groups in the PV; 2.26 vs 2.31 ms/token on the 8B
+// shape), else 256 (long windows: more resident CTAs per SM, 136 vs 148 us at
+// 32768 positions).
 template <bool VEC, bool SCORES_ONLY>
 static cudaError_t launch_partial(const AttnArgs& a, dim3 grid, size_t smem, cudaStream_t st) {
-    const cudaError_t e = set_smem_limit(attn_partial_kernel<VEC, SCORES_ONLY>, smem);
+    static const int force = getenv("GNCX_ATTN_THREADS") ? atoi(getenv("GNCX_ATTN_THREADS")) : 0;  // tuning override
+    const bool wide = force ? force == 512
+                            : a.hd <= 128 && (int64_t)grid.x * grid.y * grid.z <= 2 * (int64_t)device_info().sm_count;
+    auto k = wide ? attn_partial_kernel<VEC, SCORES_ONLY, 512> : attn_partial_kernel<VEC, SCORES_ONLY, 256>;
+    const cudaError_t e = set_smem_limit(k, smem);
     if (e != cudaSuccess) return e;
-    return launch_k(attn_partial_kernel<VEC, SCORES_ONLY>, grid, dim3(kAttnThreads), smem, st, a);
+    return launch_k(k, grid, dim3(wide ? 512 : 256), smem, st, a);
 }
 
 bool attention_shape_ok(int32_t n_heads, int32_t n_kv, int32_t hd) {
@@ -778,10 +815,11 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
         e = vec ? launch_partial<true, false>(a, grid, smem, st) : launch_partial<false, false>(a, grid, smem, st);
     }
     if (e != cudaSuccess) return kErrCuda;
-    const size_t csm = (size_t)a.max_splits * 8;
+    const size_t csm = (size_t)a.max_splits * 8 + kCombineThreads * 4;
     if (set_smem_limit(attn_combine_kernel, csm) != cudaSuccess) return kErrCuda;
-    return launch_k(attn_combine_kernel, dim3(a.n_heads, n_tok), dim3(128), csm, st, a) == cudaSuccess ? kOk
-                                                                                                    : kErrCuda;
+    return launch_k(attn_combine_kernel, dim3(a.n_heads, n_tok), dim3(kCombineThreads), csm, st, a) == cudaSuccess
+               ? kOk
+               : kErrCuda;
 }
 
 int32_t attention_scratch_records(int32_t pos, int32_t n_heads, int32_t window) {

@@ -26,6 +26,7 @@
 #include <fcntl.h>
 #include <math.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
@@ -183,6 +184,9 @@ struct Engine {
     int nh_l = 0, nkv_l = 0, qd_l = 0, kvd_l = 0, ffn_l = 0, dim_l = 0, voc0 = 0, voc_l = 0;
     size_t x_q = 0, x_p = 0, x_f = 0, x_l = 0;  // gather buffers (byte offsets in the exchange region)
     size_t ll_q = 0, ll_f = 0, ll_l = 0;        // one-row (decode) staging areas of the same gathers
+    size_t ll_p = 0;                             // one-row staging of the out-split attn_output / ffn_down
+    size_t ll_am = 0;                            // the greedy step's (value, id) swap: size x 16 bytes
+    bool tp_outsplit = false;  // decode splits attn_output / ffn_down by rows too (GNCX_TP_OUTSPLIT=1)
     int x_rows = 0;                              // rows each gather buffer holds
     const uint8_t* tok_embd = nullptr;
     int embd_type = 0;
@@ -227,7 +231,11 @@ struct Engine {
 
 // Positions per attention split in decode: 128 where the chunk's K/V rows fit
 // shared memory (head_dim <= 128; 8B shape: 2.16 vs 2.20 ms/token at 64), else 64.
-static int decode_chunk(int hd) { return hd <= 128 ? 128 : 64; }
+static int decode_chunk(int hd) {
+    static const int force = getenv("GNCX_ATTN_CHUNK") ? atoi(getenv("GNCX_ATTN_CHUNK")) : 0;  // tuning override
+    if (force == 32 || force == 64 || force == 128) return hd <= 128 || force < 128 ? force : 64;
+    return hd <= 128 ? 128 : 64;
+}
 static constexpr int kPrefillChunk = 64;   // positions per chunk of the causal prefill attention kernel
 static constexpr int kPrefillGroup = 256;  // prompt positions per attention launch in prefill
 static constexpr int kTpMaxRows = 4096;    // prompt rows a tensor-parallel prefill gathers at once
@@ -260,16 +268,30 @@ static int gather(Engine* e, size_t buf, int rows, int row_floats, int off, int 
 static int gather_row(Engine* e, int slot);
 
 // LM head over this rank's vocabulary rows of the staged act_d, then (tensor
-// parallel) the all-gather that gives every rank all logits.
-static int lm_head(Engine* e) {
+// parallel, when the caller needs every logit) the all-gather that gives
+// every rank all of them.
+static int lm_head(Engine* e, bool gather_logits = true) {
     const uint8_t* w = e->tok_embd + (size_t)e->voc0 * row_bytes(e->embd_type, e->dim);
     CK(gemv(e, w, e->embd_type, e->act_d, e->normed, e->dim, e->voc_l, e->logits + e->voc0, e->softcap));
-    return gather_row(e, 2);  // the logits slot of the one-row gathers
+    return gather_logits ? gather_row(e, 2) : kOk;  // the logits slot of the one-row gathers
 }
 
-// GEMV whose input is an fp32 vector (re-quantized inside the GEMV).
-static int gemv_x(Engine* e, const uint8_t* w, int t, const float* x, int in, int out, float* y, float cap = 0.0f) {
-    return gemv_launch(w, t, x, nullptr, in, out, y, cap, e->d_err, e->stream);
+
+// A decode GEMV whose output y (dim rows) is the residual of the next norm:
+// hidden += y, then RMSNorm with gains `norm_w` into the staged act_d (and
+// normed).  The norm is its own one-CTA kernel: under programmatic dependent
+// launch it is resident and waiting while the GEMV finishes, and the next
+// GEMV's CTAs stream their weights while it runs.  (Running the norm in the
+// GEMV's last CTA instead -- an arrival counter per launch -- measured 0.24
+// ms/token slower: every CTA's exit then waits for a fence and an atomic, so
+// the next kernel's CTAs start streaming later.)
+static int gemv_norm(Engine* e, const uint8_t* w, int t, const uint8_t* act, const float* x, int in, float* y,
+                     const float* norm_w) {
+    const int D = e->dim;
+    if (act && t != kBF16) CK(gemv_launch(w, t, nullptr, act, in, D, y, 0.0f, e->d_err, e->stream));
+    else CK(gemv_launch(w, t, x, nullptr, in, D, y, 0.0f, e->d_err, e->stream));
+    return add_norm_quant_launch(e->hidden, y, norm_w, 1, D, e->eps, ActOut{nullptr, e->act_d}, e->normed,
+                                 e->stream);
 }
 
 static int gather(Engine* e, size_t buf, int rows, int row_floats, int off, int len) {
@@ -277,7 +299,7 @@ static int gather(Engine* e, size_t buf, int rows, int row_floats, int off, int 
 }
 
 // Decode's one-row gathers: attention output, GLU output, logits.
-enum LlSlot { kLlAttn = 0, kLlGlu = 1, kLlLogits = 2 };
+enum LlSlot { kLlAttn = 0, kLlGlu = 1, kLlLogits = 2, kLlProj = 3 };  // slot kTpLlSlots - 1: the argmax swap
 static int gather_row(Engine* e, int slot) {
     TpSlices sl{};
     const int n = e->tp.size;
@@ -286,10 +308,12 @@ static int gather_row(Engine* e, int slot) {
     for (int q = 0; q < n; ++q) {
         if (slot == kLlAttn) { sl.off[q] = q * e->qd_l; sl.len[q] = e->qd_l; }
         else if (slot == kLlGlu) { sl.off[q] = q * e->ffn_l; sl.len[q] = e->ffn_l; }
+        else if (slot == kLlProj) { sl.off[q] = q * e->dim_l; sl.len[q] = e->dim_l; }
         else { int v0, v1; split_rows(e->vocab, n, q, 4, v0, v1); sl.off[q] = v0; sl.len[q] = v1 - v0; }
     }
     if (slot == kLlAttn) { buf = e->x_q; ll = e->ll_q; row = e->q_dim; }
     else if (slot == kLlGlu) { buf = e->x_f; ll = e->ll_f; row = e->ffn; }
+    else if (slot == kLlProj) { buf = e->x_p; ll = e->ll_p; row = e->dim; }
     else { buf = e->x_l; ll = e->ll_l; row = e->vocab; }
     return tp_gather_ll_launch(e->tp, buf, ll, row, sl, slot, e->d_err, e->stream);
 }
@@ -304,13 +328,15 @@ static int decode_step(Engine* e, bool sample, double penalty) {
     const bool tp = e->tp.size > 1;
     const int rk = e->tp.rank;
     float* gq = tp ? tp_buffer(e->tp, e->x_q) : nullptr;  // attention output (gathered)
-    float* gp = e->proj;  // attn_output / ffn_down result (every rank computes all of it)
     float* gf = tp ? tp_buffer(e->tp, e->x_f) : nullptr;  // GLU output (gathered)
     CK(dequant_launch(e->tok_embd, e->embd_type, 1, D, e->embd_scale, &e->st->token, e->hidden, s));
+    // layer 0's attention norm; every later norm runs in the epilogue of the
+    // GEMV whose output it adds into the residual stream
+    CK(add_norm_quant_launch(e->hidden, nullptr, e->L[0].attn_norm, 1, D, e->eps, ActOut{nullptr, e->act_d},
+                             e->normed, s));
     for (int l = 0; l < e->n_layers; ++l) {
         const LayerW& w = e->L[l];
-        CK(add_norm_quant_launch(e->hidden, l == 0 ? nullptr : gp, w.attn_norm, 1, D, e->eps,
-                                 ActOut{nullptr, e->act_d}, e->normed, s));
+        const float* next_norm = l + 1 < e->n_layers ? e->L[l + 1].attn_norm : e->out_norm;
         if (w.qkv_fused) {
             CK(gemv(e, w.wq, w.tq, e->act_d, e->normed, D, qkv_w, e->qkv));
         } else {
@@ -360,13 +386,20 @@ static int decode_step(Engine* e, bool sample, double penalty) {
         a.scores = e->scores;
         a.score_cap = e->max_splits * decode_chunk(e->hd);
         CK(attention_run(a, 1, s));
-        if (tp) {  // gather the heads, then the whole attn_output on every rank
+        if (tp && e->tp_outsplit) {  // gather the heads, this rank's attn_output rows, gather those
             CK(gather_row(e, kLlAttn));
-            CK(gemv_x(e, w.wo, w.to, gq, QD, D, e->proj));
+            float* gpb = tp_buffer(e->tp, e->x_p);
+            CK(gemv_launch(w.wo + (size_t)rk * e->dim_l * row_bytes(w.to, QD), w.to, gq, nullptr, QD, e->dim_l,
+                           gpb + (size_t)rk * e->dim_l, 0.0f, e->d_err, s));
+            CK(gather_row(e, kLlProj));
+            CK(add_norm_quant_launch(e->hidden, gpb, w.ffn_norm, 1, D, e->eps, ActOut{nullptr, e->act_d}, e->normed,
+                                     s));
+        } else if (tp) {  // gather the heads, then the whole attn_output on every rank
+            CK(gather_row(e, kLlAttn));
+            CK(gemv_norm(e, w.wo, w.to, nullptr, gq, QD, e->proj, w.ffn_norm));
         } else {
-            CK(gemv(e, w.wo, w.to, e->act_q, nullptr, QD, D, e->proj));
+            CK(gemv_norm(e, w.wo, w.to, e->act_q, nullptr, QD, e->proj, w.ffn_norm));
         }
-        CK(add_norm_quant_launch(e->hidden, gp, w.ffn_norm, 1, D, e->eps, ActOut{nullptr, e->act_d}, e->normed, s));
         if (w.gu_fused) {
             CK(gemv(e, w.wg, w.tg, e->act_d, e->normed, D, 2 * fl, e->gu));
         } else {
@@ -377,13 +410,30 @@ static int decode_step(Engine* e, bool sample, double penalty) {
             CK(glu_quant_launch(e->gu, e->gu + fl, 2 * fl, fl, 1, e->arch == 2, ActOut{nullptr, nullptr}, s,
                                 gf + (size_t)rk * fl, F));
             CK(gather_row(e, kLlGlu));
-            CK(gemv_x(e, w.wd, w.td, gf, F, D, e->proj));  // the whole ffn_down on every rank
+            if (e->tp_outsplit) {  // this rank's ffn_down rows, then every rank gathers them
+                float* gpb = tp_buffer(e->tp, e->x_p);
+                CK(gemv_launch(w.wd + (size_t)rk * e->dim_l * row_bytes(w.td, F), w.td, gf, nullptr, F, e->dim_l,
+                               gpb + (size_t)rk * e->dim_l, 0.0f, e->d_err, s));
+                CK(gather_row(e, kLlProj));
+                CK(add_norm_quant_launch(e->hidden, gpb, next_norm, 1, D, e->eps, ActOut{nullptr, e->act_d},
+                                         e->normed, s));
+            } else {
+                CK(gemv_norm(e, w.wd, w.td, nullptr, gf, F, e->proj, next_norm));  // the whole ffn_down on every rank
+            }
         } else {
             CK(glu_quant_launch(e->gu, e->gu + F, 2 * F, F, 1, e->arch == 2, ActOut{nullptr, e->act_f}, s));
-            CK(gemv(e, w.wd, w.td, e->act_f, nullptr, F, D, e->proj));
+            CK(gemv_norm(e, w.wd, w.td, e->act_f, nullptr, F, e->proj, next_norm));
         }
     }
-    CK(add_norm_quant_launch(e->hidden, gp, e->out_norm, 1, D, e->eps, ActOut{nullptr, e->act_d}, e->normed, s));
+    if (sample && tp) {
+        // each rank takes the penalized maximum of its vocabulary slice and the
+        // ranks swap (value, id) pairs: no logit crosses NVLink
+        CK(lm_head(e, false));
+        int32_t n_parts = 0;
+        CK(argmax_partials_launch(e->logits + e->voc0, e->voc_l, e->voc0, e->st, penalty, e->am_scratch, &n_parts, s));
+        CK(tp_argmax_state_launch(e->tp, e->ll_am, e->am_scratch, n_parts, e->st, e->out_ids, 1, e->d_err, s));
+        return kOk;
+    }
     CK(lm_head(e));
     if (sample) CK(argmax_state_launch(e->logits, e->vocab, e->st, penalty, e->out_ids, 1, e->am_scratch, s));
     return kOk;
@@ -771,7 +821,9 @@ static int engine_load(Engine* e, const char* path, int max_seq, int tp_rank, in
         e->ll_q = e->x_l + (tp > 1 ? (size_t)e->vocab * 4 : 0);
         e->ll_f = e->ll_q + T * e->q_dim * 8;
         e->ll_l = e->ll_f + T * F * 8;
-        const int st = tp_alloc(e->tp, tp_rank, tp, e->ll_l + T * e->vocab * 8);
+        e->ll_p = e->ll_l + T * e->vocab * 8;
+        e->ll_am = (e->ll_p + T * D * 8 + 15) & ~(size_t)15;
+        const int st = tp_alloc(e->tp, tp_rank, tp, e->ll_am + T * 16);
         if (st != kOk) return st;
     }
     if (tp > 1) {
@@ -790,6 +842,7 @@ static int engine_load(Engine* e, const char* path, int max_seq, int tp_rank, in
     CU(cudaMalloc(&e->am_scratch, argmax_state_scratch_bytes()));
     CU(cudaMalloc(&e->d_err, 4));
     CU(cudaMemset(e->d_err, 0, 4));
+
     e->out_cap = max_seq + 1;
     CU(cudaMalloc(&e->out_ids, (size_t)e->out_cap * 4));
     for (auto& ev : e->ev) CU(cudaEventCreate(&ev));
@@ -854,6 +907,7 @@ void* gncx_engine_create_tp(const char* gguf_path, int32_t max_seq_len, int32_t 
         return nullptr;
     }
     Engine* e = new Engine();
+    if (const char* v = getenv("GNCX_TP_OUTSPLIT")) e->tp_outsplit = atoi(v) != 0;
     if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) {
         delete e;
         return nullptr;

@@ -10,6 +10,7 @@
 //   * penalized greedy argmax -> decode state update (:1229-1311), so the token
 //     loop runs from device memory under one captured CUDA graph per token.
 #include <cuda_runtime.h>
+#include <stdlib.h>
 #include "act.cuh"
 #include "common.cuh"
 #include "kernels.h"
@@ -274,7 +275,7 @@ int glu_quant_launch(const float* g, const float* u, int32_t stride, int32_t ffn
 // first maximum wins) feeding generate (:1276-1311): the chosen token becomes
 // the next input, joins the penalty window and the output; EOS stops.
 constexpr int kAmThreads = 256;
-constexpr int kAmBlocks = 148;
+constexpr int kAmBlocks = kArgmaxParts;
 
 struct Best { double v; int i; };
 __device__ __forceinline__ Best pick(Best a, Best b) {
@@ -297,8 +298,10 @@ __device__ Best am_block_best(Best p) {
     return p;
 }
 
-__global__ void am_state_stage1(const float* __restrict__ logits, int vocab, const DecodeState* st, double penalty,
-                                double* part_v, int* part_i) {
+// logits[0 .. vocab) are the vocabulary ids idx0 .. idx0 + vocab (a tensor-
+// parallel rank's slice); the partial results carry global ids.
+__global__ void am_state_stage1(const float* __restrict__ logits, int vocab, int idx0, const DecodeState* st,
+                                double penalty, double* part_v, int* part_i) {
     GNCX_TRACE_SCOPE(kTagArgmax1, vocab);
     pdl_launch_dependents();
     pdl_wait();  // the logits come from the preceding kernel
@@ -310,7 +313,7 @@ __global__ void am_state_stage1(const float* __restrict__ logits, int vocab, con
     __syncthreads();
     const int n = st->n_all < kRecentWindow ? st->n_all : kRecentWindow;
     for (int k = threadIdx.x; k < n; k += blockDim.x) {
-        const int t = st->ring[k];
+        const int t = st->ring[k] - idx0;
         if (t >= lo && t < hi) atomicOr(&pen[(t - lo) >> 5], 1u << ((t - lo) & 31));
     }
     __syncthreads();
@@ -318,7 +321,7 @@ __global__ void am_state_stage1(const float* __restrict__ logits, int vocab, con
     for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         double v = (double)logits[i];
         if ((pen[(i - lo) >> 5] >> ((i - lo) & 31)) & 1u) v = v > 0.0 ? __ddiv_rn(v, penalty) : __dmul_rn(v, penalty);
-        if (v > b.v) { b.v = v; b.i = i; }
+        if (v > b.v) { b.v = v; b.i = idx0 + i; }
     }
     b = am_block_best(b);
     if (threadIdx.x == 0) { part_v[blockIdx.x] = b.v; part_i[blockIdx.x] = b.i; }
@@ -350,6 +353,20 @@ __global__ void am_state_stage2(const double* part_v, const int* part_i, int n, 
 
 size_t argmax_state_scratch_bytes() { return (size_t)kAmBlocks * (sizeof(double) + sizeof(int)); }
 
+int argmax_partials_launch(const float* logits, int32_t vocab, int32_t idx0, const DecodeState* st, double penalty,
+                           void* scratch, int32_t* n_parts, cudaStream_t s) {
+    if (!logits || !st || !scratch || vocab <= 0 || idx0 < 0) return kErrInvalidArg;
+    double* pv = reinterpret_cast<double*>(scratch);
+    int* pi = reinterpret_cast<int*>(pv + kAmBlocks);
+    const int blocks = vocab < kAmBlocks * 64 ? (vocab + 63) / 64 : kAmBlocks;
+    const int per = (vocab + blocks - 1) / blocks;
+    *n_parts = blocks;
+    return launch_k(am_state_stage1, dim3(blocks), dim3(kAmThreads), (size_t)((per + 31) / 32) * 4, s, logits, vocab,
+                    idx0, st, penalty, pv, pi) == cudaSuccess
+               ? kOk
+               : kErrCuda;
+}
+
 int argmax_state_launch(const float* logits, int32_t vocab, DecodeState* st, double penalty, int32_t* out_ids,
                         int advance_pos, void* scratch, cudaStream_t s) {
     if (!logits || !st || !out_ids || !scratch || vocab <= 0) return kErrInvalidArg;
@@ -357,8 +374,8 @@ int argmax_state_launch(const float* logits, int32_t vocab, DecodeState* st, dou
     int* pi = reinterpret_cast<int*>(pv + kAmBlocks);
     const int blocks = vocab < kAmBlocks * 64 ? (vocab + 63) / 64 : kAmBlocks;
     const int per = (vocab + blocks - 1) / blocks;
-    if (launch_k(am_state_stage1, dim3(blocks), dim3(kAmThreads), (size_t)((per + 31) / 32) * 4, s, logits, vocab, st,
-                 penalty, pv, pi) != cudaSuccess ||
+    if (launch_k(am_state_stage1, dim3(blocks), dim3(kAmThreads), (size_t)((per + 31) / 32) * 4, s, logits, vocab, 0,
+                 st, penalty, pv, pi) != cudaSuccess ||
         launch_k(am_state_stage2, dim3(1), dim3(kAmThreads), 0, s, pv, pi, blocks, st, out_ids, advance_pos) !=
             cudaSuccess)
         return kErrCuda;

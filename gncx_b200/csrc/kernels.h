@@ -168,7 +168,12 @@ int qkv_post_launch(float* qkv, int32_t row_stride, int32_t rows, int32_t nh, in
 // re-quantized `act` and/or fp32 `out` (row r at out + r * out_stride).
 int glu_quant_launch(const float* g, const float* u, int32_t stride, int32_t ffn, int32_t rows, bool gelu,
                      ActOut act, cudaStream_t st, float* out = nullptr, int32_t out_stride = 0);
+constexpr int kArgmaxParts = 148;  // partial maxima of stage 1: doubles [kArgmaxParts], then ints
 size_t argmax_state_scratch_bytes();
+// Stage 1 only, over logits of the vocabulary ids idx0 .. idx0 + vocab: the
+// per-block penalized maxima (global ids) into `scratch`; *n_parts blocks.
+int argmax_partials_launch(const float* logits, int32_t vocab, int32_t idx0, const DecodeState* st, double penalty,
+                           void* scratch, int32_t* n_parts, cudaStream_t s);
 int argmax_state_launch(const float* logits, int32_t vocab, DecodeState* st, double penalty, int32_t* out_ids,
                         int advance_pos, void* scratch, cudaStream_t s);
 
@@ -184,7 +189,7 @@ constexpr size_t kTpCtlBytes = 4096;
 constexpr int kTpEpochs = kTpMaxRanks * kTpMaxCtas;
 constexpr int kTpInfo = kTpEpochs + kTpMaxCtas;  // 5 words: magic, bytes (lo, hi), rank, size
 constexpr uint32_t kTpMagic = 0x58544e47u;
-constexpr int kTpLlSlots = 4;
+constexpr int kTpLlSlots = 5;
 constexpr int kTpLlEpochs = 640;  // word offset: [kTpLlSlots][kTpMaxCtas] epochs of the one-row gather
 static_assert(kTpInfo + 5 <= kTpLlEpochs && (kTpLlEpochs + kTpLlSlots * kTpMaxCtas) * 4 <= (int)kTpCtlBytes,
               "control words fit");
@@ -220,6 +225,15 @@ struct TpSlices {
 // slot keeps its own epochs; the same slot must always have the same shape).
 int tp_gather_ll_launch(const TpComm& c, size_t buf, size_t ll, int32_t row_floats, const TpSlices& sl, int32_t slot,
                         int32_t* err, cudaStream_t st);
+// Tensor-parallel greedy step: each rank has the penalized maxima of its
+// vocabulary slice (argmax_partials_launch into `scratch`, n_parts of them);
+// the ranks swap their best (value, id) -- 16 bytes each, at byte offset
+// `stage` (size x 16 bytes) of every region's data area -- and every rank
+// applies the overall best (larger value, then lower id: the first maximum of
+// the whole vocabulary) to its decode state exactly as argmax_state_launch
+// does.  Replaces an all-gather of every logit.
+int tp_argmax_state_launch(const TpComm& c, size_t stage, const void* scratch, int32_t n_parts, DecodeState* st,
+                           int32_t* out_ids, int advance_pos, int32_t* err, cudaStream_t s);
 
 // ---- embedding ----
 int embed_launch(const uint8_t* tensor, int32_t type, const int32_t* tokens, int32_t n_tokens, int32_t dim,

@@ -76,13 +76,16 @@ __device__ __forceinline__ float rms_inv(const float* xs, int n, float eps) {
 
 // The same factor from precomputed squares stored lane-major: sq[j * n4 + k]
 // = x[4k+j]^2 (n = 4 * n4, n4 a multiple of 4, sq 16-byte aligned).  Lanes 0-3
-// of warp 0 run the four chains with vector loads well ahead of the adds.
+// of warp 0 run the four chains with vector loads.
 __device__ __forceinline__ float rms_inv_sq(const float* sq, int n4, float eps) {
     __shared__ float s_inv;
     const int tid = threadIdx.x;
     if (tid < 32) {
         float acc = 0.0f;
         if (tid < 4) {
+            // a plain unrolled loop: ~5.4 cycles per element on B200, against
+            // ~8 for loads pinned ahead with volatile asm and ~4.2 (the fadd
+            // latency) with the values already in registers
             const float4* p = reinterpret_cast<const float4*>(sq + (size_t)tid * n4);
 #pragma unroll 8
             for (int i = 0; i < (n4 >> 2); ++i) {

@@ -142,6 +142,7 @@ __global__ void __launch_bounds__(kTpThreads) tp_ll_gather_kernel(const LlArgs a
             asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst), "l"(w) : "memory");
         }
     }
+    if (threadIdx.x == 0) GNCX_TRACE_MARK(50, 0);  // sends issued
     // receive: poll this rank's staging rows until each peer value carries the epoch
     if (*(volatile int32_t*)a.err != 0) return;  // a rank already gave up: do not wait again
     const unsigned long long t0 = global_ns();
@@ -163,9 +164,124 @@ __global__ void __launch_bounds__(kTpThreads) tp_ll_gather_kernel(const LlArgs a
             row[o + j] = __uint_as_float((uint32_t)w);
         }
     }
+    if (threadIdx.x == 0) GNCX_TRACE_MARK(51, 0);  // every peer value of this thread's share arrived
+}
+
+// ---- the greedy step over a split vocabulary ----
+constexpr int kAmSlot = kTpLlSlots - 1;  // epoch slot of the (value, id) swap
+struct AmArgs {
+    uint8_t* region[kTpMaxRanks];
+    int rank, size;
+    size_t stage;  // data-area byte offset of size x 16-byte entries {word0: id | epoch << 32, word1: value}
+    const double* part_v;
+    const int* part_i;
+    int n;
+    DecodeState* st;
+    int32_t* out_ids;
+    int advance_pos;
+    int32_t* err;
+};
+
+__device__ __forceinline__ bool am_better(double v, int i, double bv, int bi) {
+    return v > bv || (v == bv && i < bi);  // the first maximum wins (lua/gncx_streamer.lua:1229-1273)
+}
+
+__global__ void __launch_bounds__(kTpThreads) tp_argmax_state_kernel(const AmArgs a) {
+    GNCX_TRACE_SCOPE(kTagArgmax2, a.n);
+    pdl_launch_dependents();
+    pdl_wait();  // the partial maxima come from the preceding kernel
+    __shared__ double sv[kTpThreads / 32];
+    __shared__ int si[kTpThreads / 32];
+    double bv = -1e30;
+    int bi = 0;
+    for (int k = threadIdx.x; k < a.n; k += blockDim.x)
+        if (am_better(a.part_v[k], a.part_i[k], bv, bi)) { bv = a.part_v[k]; bi = a.part_i[k]; }
+    for (int o = 16; o > 0; o >>= 1) {
+        const double v = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int i = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (am_better(v, i, bv, bi)) { bv = v; bi = i; }
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    for (int k = 1; k < kTpThreads / 32; ++k)
+        if (am_better(sv[k], si[k], bv, bi)) { bv = sv[k]; bi = si[k]; }
+    // swap: the value first, a system fence, then the (id, epoch) word the peers poll
+    uint32_t* ctl = reinterpret_cast<uint32_t*>(a.region[a.rank]);
+    uint32_t* epw = ctl + kTpLlEpochs + kAmSlot * kTpMaxCtas;
+    const uint32_t ep = *epw + 1u;
+    *epw = ep;
+    for (int q = 0; q < a.size; ++q) {
+        if (q == a.rank) continue;
+        uint64_t* dst = reinterpret_cast<uint64_t*>(a.region[q] + kTpCtlBytes + a.stage) + 2 * a.rank;
+        asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst + 1), "l"((uint64_t)__double_as_longlong(bv))
+                     : "memory");
+    }
+    __threadfence_system();
+    for (int q = 0; q < a.size; ++q) {
+        if (q == a.rank) continue;
+        uint64_t* dst = reinterpret_cast<uint64_t*>(a.region[q] + kTpCtlBytes + a.stage) + 2 * a.rank;
+        const uint64_t w0 = ((uint64_t)ep << 32) | (uint32_t)bi;
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(w0) : "memory");
+    }
+    if (*(volatile int32_t*)a.err != 0) return;  // a rank already gave up: do not wait again
+    const unsigned long long t0 = global_ns();
+    const uint64_t* mine = reinterpret_cast<const uint64_t*>(a.region[a.rank] + kTpCtlBytes + a.stage);
+    for (int q = 0; q < a.size; ++q) {
+        if (q == a.rank) continue;
+        uint64_t w0;
+        for (;;) {
+            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(w0) : "l"(mine + 2 * q) : "memory");
+            if ((uint32_t)(w0 >> 32) == ep) break;
+            if (global_ns() - t0 > kTpWaitNs) {
+                record_error(a.err, kErrTimeout);
+                return;
+            }
+        }
+        uint64_t w1;
+        asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w1) : "l"(mine + 2 * q + 1) : "memory");
+        const double v = __longlong_as_double((long long)w1);
+        const int i = (int)(uint32_t)w0;
+        if (am_better(v, i, bv, bi)) { bv = v; bi = i; }
+    }
+    // the decode state update of argmax_state_launch (generate, :1276-1311)
+    DecodeState* st = a.st;
+    if (!st->done) {
+        const int next = bi;
+        if (next == st->eos) {
+            st->done = 1;
+        } else {
+            if (st->n_out < st->max_out) a.out_ids[st->n_out] = next;
+            st->n_out += 1;
+            st->ring[st->n_all % kRecentWindow] = next;
+            st->n_all += 1;
+            st->token = next;
+            if (a.advance_pos) st->pos += 1;
+            if (st->n_out >= st->max_out) st->done = 1;
+        }
+    }
 }
 
 }  // namespace
+
+int tp_argmax_state_launch(const TpComm& c, size_t stage, const void* scratch, int32_t n_parts, DecodeState* st,
+                           int32_t* out_ids, int advance_pos, int32_t* err, cudaStream_t s) {
+    if (!c.connected || !scratch || !st || !out_ids || !err || n_parts <= 0 || n_parts > kArgmaxParts || (stage & 15))
+        return kErrInvalidArg;
+    AmArgs a{};
+    for (int q = 0; q < kTpMaxRanks; ++q) a.region[q] = c.region[q];
+    a.rank = c.rank;
+    a.size = c.size;
+    a.stage = stage;
+    a.part_v = reinterpret_cast<const double*>(scratch);
+    a.part_i = reinterpret_cast<const int*>(a.part_v + kArgmaxParts);
+    a.n = n_parts;
+    a.st = st;
+    a.out_ids = out_ids;
+    a.advance_pos = advance_pos;
+    a.err = err;
+    return launch_k(tp_argmax_state_kernel, dim3(1), dim3(kTpThreads), 0, s, a) == cudaSuccess ? kOk : kErrCuda;
+}
 
 int tp_gather_ll_launch(const TpComm& c, size_t buf, size_t ll, int32_t row_floats, const TpSlices& sl, int32_t slot,
                         int32_t* err, cudaStream_t st) {

@@ -23,7 +23,7 @@ enum TraceTag : uint32_t {
 
 struct TraceRec {
     unsigned long long grid, t0, t1;
-    uint32_t tag, aux, cta, pad;  // pad: 0 = a CTA's span (thread 0), 1 = an instant mark
+    uint32_t tag, aux, cta, pad;  // pad: odd (1) = an instant mark; even = a CTA span, SM cycles x 2
 };
 static_assert(sizeof(TraceRec) == 40, "trace record layout");
 
@@ -73,19 +73,23 @@ __device__ __forceinline__ void trace_fill(TraceRec& r, uint32_t tag, uint32_t a
 // flushes the CTA's span record and its instant marks when it leaves.
 struct TraceScope {
     unsigned long long t0;
+    long long c0;  // SM cycles at entry: the span record's pad carries the cycles spent
     uint32_t tag, aux;
     __device__ TraceScope(uint32_t tg, uint32_t ax) : tag(tg), aux(ax) {
         t0 = trace_clock();
+        c0 = clock64();
         if (threadIdx.x == 0) *trace_mark_count() = 0;
         __syncthreads();
     }
     __device__ ~TraceScope() {
         if (threadIdx.x != 0 || !g_trace_rec) return;
         const unsigned long long t1 = trace_clock();
+        const long long c1 = clock64();
         const unsigned nm = min(*(volatile unsigned*)trace_mark_count(), (unsigned)kTraceMarks);
         const unsigned i = atomicAdd(g_trace_n, 1u + nm);
         if (i + nm >= g_trace_cap) return;
         trace_fill(g_trace_rec[i], tag, aux, t0, t1, 0);
+        g_trace_rec[i].pad = (uint32_t)((c1 - c0) << 1);  // even: a span (cycles x 2); marks carry 1
         for (unsigned k = 0; k < nm; ++k) g_trace_rec[i + 1 + k] = trace_marks()[k];
     }
 };

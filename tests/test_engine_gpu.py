@@ -76,6 +76,26 @@ def test_tiny_model_stream(tmp_path, oracle_model_cls, wtype):
         assert len(set(want)) > 20  # a diverse stream
 
 
+@pytest.mark.parametrize("dim", [1024, 2048, 4096])
+def test_model_widths(tmp_path, oracle_model_cls, dim):
+    """Each hidden width the decode norm kernel specialises (1024, 2048, 4096):
+    prefill and every forward_token's logits against the reference in exact
+    mode, and the device-driven greedy stream."""
+    from gncx_b200.streamer import GNCXStreamer
+    hp = dict(n_layers=2, dim=dim, n_heads=dim // 128, n_kv=dim // 256, head_dim=128, ffn=512, vocab=3000, eps=1e-6,
+              rope_base=1e6)
+    path = gguf.write_random_model(tmp_path / "w.gguf", hp, seed=dim, wtype=Q6_K)
+    prompt = np.random.default_rng(dim).integers(0, hp["vocab"], 21).tolist()
+    ref = oracle_model_cls(path, 64)
+    toks, ref_logits = _reference_steps(ref, prompt, 16)
+    ref.close()
+    with GNCXStreamer(path, max_seq_len=64, exact_attention=True) as eng:
+        errs, _ = _teacher_forced(eng, prompt, toks, ref_logits)
+        assert errs.max() <= LOGIT_TOL, errs
+        got = eng.generate_ids(prompt, 16, 1.15, eos_id=-1)
+    assert got == toks
+
+
 @pytest.mark.parametrize("wtype", [Q4_K, Q6_K])
 def test_tiny_model_fast_attention(tmp_path, oracle_model_cls, wtype):
     """Split-KV softmax mode: logits within tolerance at every step."""

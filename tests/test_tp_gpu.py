@@ -38,10 +38,10 @@ def _port():
     return p
 
 
-def _launch(n, args, timeout=300):
+def _launch(n, args, timeout=300, extra_env=None):
     """Run under torch.distributed.run in a session of its own, so that on a
     timeout the launcher and all its ranks end together."""
-    env = dict(os.environ, PYTHONPATH=str(ROOT), NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, PYTHONPATH=str(ROOT), NCCL_NVLS_ENABLE="0", **(extra_env or {}))
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}", "--master-addr",
            "127.0.0.1", "--master-port", str(_port()), *args]
     p = subprocess.Popen(cmd, cwd=ROOT, env=env, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True,
@@ -54,11 +54,11 @@ def _launch(n, args, timeout=300):
     return subprocess.CompletedProcess(cmd, p.returncode, out, err)
 
 
-def _tp_run(tmp_path, model, n, exact):
-    out = tmp_path / f"tp{n}_{int(exact)}.npz"
+def _tp_run(tmp_path, model, n, exact, outsplit=False):
+    out = tmp_path / f"tp{n}_{int(exact)}_{int(outsplit)}.npz"
     args = ["-m", "gncx_b200.tp_run", str(model), "--prompt-len", "37", "--steps", "5", "--new", "24", "--seed", "3",
             "--out", str(out)] + (["--exact"] if exact else [])
-    r = _launch(n, args)
+    r = _launch(n, args, extra_env={"GNCX_TP_OUTSPLIT": "1"} if outsplit else None)
     assert r.returncode == 0, (r.stdout[-4000:], r.stderr[-4000:])
     z = np.load(out)
     info = json.loads(str(z["info"]))
@@ -66,12 +66,16 @@ def _tp_run(tmp_path, model, n, exact):
     return z["logits"], z["ids"]
 
 
-@pytest.mark.parametrize("wtype,exact", [(Q4_K, True), (Q8_0, False)])
-def test_tp2_matches_one_gpu(tmp_path, wtype, exact):
+@pytest.mark.parametrize("wtype,exact,outsplit", [(Q4_K, True, False), (Q8_0, False, False), (Q4_K, True, True)])
+def test_tp2_matches_one_gpu(tmp_path, wtype, exact, outsplit):
+    """Logits of the prefill and of every forward step, and the greedy stream
+    (each rank's penalized maximum over its vocabulary slice, swapped as
+    (value, id) pairs), equal the 1-GPU engine's; also with attn_output and
+    ffn_down split by rows in decode (GNCX_TP_OUTSPLIT=1)."""
     _need_gpus(2)
     model = gguf.write_random_model(tmp_path / "tiny.gguf", TINY, seed=5, wtype=wtype)
     l1, i1 = _tp_run(tmp_path, model, 1, exact)
-    l2, i2 = _tp_run(tmp_path, model, 2, exact)
+    l2, i2 = _tp_run(tmp_path, model, 2, exact, outsplit)
     assert np.all(np.isfinite(l1)) and len(i1) == 24
     assert np.array_equal(l1, l2)
     assert np.array_equal(i1, i2)
