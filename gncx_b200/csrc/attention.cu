@@ -273,6 +273,69 @@ __device__ __forceinline__ void warp_head_norm_rope(float* x, int hd, const floa
     __syncwarp();
 }
 
+// The per-head gains and this position's rope factors of one warp's head,
+// loaded into registers before the kernel's dependency wait (the gains are
+// weights; the rope table is fixed; the position was set before the step).
+constexpr int kPostMaxW = kMaxHeadDim / 32, kPostMaxR = kMaxHeadDim / 64;
+struct HeadPost {
+    float w[kPostMaxW];
+    float c[kPostMaxR], s[kPostMaxR];
+};
+__device__ __forceinline__ void head_post_load(HeadPost& hp, int hd, const float* __restrict__ w,
+                                               const float* __restrict__ ct, const float* __restrict__ st, int pos,
+                                               int lane) {
+    const int half = hd >> 1;
+#pragma unroll
+    for (int m = 0; m < kPostMaxW; ++m) {
+        const int i = lane + 32 * m;
+        hp.w[m] = (w && i < hd) ? __ldg(w + i) : 1.0f;
+    }
+#pragma unroll
+    for (int m = 0; m < kPostMaxR; ++m) {
+        const int i = lane + 32 * m;
+        hp.c[m] = i < half ? __ldg(ct + (size_t)pos * half + i) : 0.0f;
+        hp.s[m] = i < half ? __ldg(st + (size_t)pos * half + i) : 0.0f;
+    }
+}
+// warp_head_norm_rope with the operands of head_post_load (same arithmetic).
+__device__ __forceinline__ void warp_head_norm_rope_pf(float* x, int hd, const HeadPost& hp, bool has_w,
+                                                       bool do_norm, float eps, int lane) {
+    if (do_norm) {
+        const float acc = lane < 4 ? lane_sumsq(x, lane, hd >> 2) : 0.0f;
+        const float a1 = __shfl_sync(0xffffffffu, acc, 1);
+        const float a2 = __shfl_sync(0xffffffffu, acc, 2);
+        const float a3 = __shfl_sync(0xffffffffu, acc, 3);
+        float inv = 0.0f;
+        if (lane == 0) {
+            const double s = __dadd_rn(__dadd_rn(__dadd_rn((double)acc, (double)a1), (double)a2), (double)a3);
+            const float ms = __double2float_rn(__ddiv_rn(s, (double)hd));
+            inv = fdiv(1.0f, __fsqrt_rn(fadd(ms, eps)));
+        }
+        inv = __shfl_sync(0xffffffffu, inv, 0);
+#pragma unroll
+        for (int m = 0; m < kPostMaxW; ++m) {
+            const int i = lane + 32 * m;
+            if (i < hd) {
+                const float v = fmul(x[i], inv);
+                x[i] = has_w ? fmul(v, hp.w[m]) : v;
+            }
+        }
+        __syncwarp();
+    }
+    const int half = hd >> 1;
+#pragma unroll
+    for (int m = 0; m < kPostMaxR; ++m) {
+        const int i = lane + 32 * m;
+        if (i < half) {
+            const float c = hp.c[m], s = hp.s[m];
+            const float x1 = x[i], x2 = x[i + half];
+            x[i] = fsub(fmul(x1, c), fmul(x2, s));
+            x[i + half] = fadd(fmul(x2, c), fmul(x1, s));
+        }
+    }
+    __syncwarp();
+}
+
 // Partial record per (query, head, split): [0] = max, [1] = sum of exp, [4..] = o[hd]
 template <bool VEC, bool SCORES_ONLY, int NT>
 __global__ void __launch_bounds__(NT) attn_partial_kernel(const AttnArgs a) {
@@ -335,6 +398,16 @@ __global__ void __launch_bounds__(NT) attn_partial_kernel(const AttnArgs a) {
         }
     };
     if (n_old > 0) stage_rows(0, n_old);
+    // the post step's gains and rope factors, before the dependency wait: warp
+    // `task` < G norms and rotates q head `task`, warp G the new K row
+    HeadPost hp;
+    const int post_pos = t0 + len - 1;
+    const int n_post = a.post_k ? G + (own_row ? 1 : 0) : 0;
+    // (split-KV only: in exact mode, whose scores-only CTAs end right after the
+    // post step, loading these early measured slower: 3.92 vs 3.38 ms/token)
+    const bool post_pf = !SCORES_ONLY && n_post <= NT / 32;
+    if (warp < n_post && post_pf)
+        head_post_load(hp, hd, warp < G ? a.post_qn : a.post_kn, a.rope_c, a.rope_s, post_pos, lane);
     if (tid == 0) GNCX_TRACE_MARK(10, n_old);
     pdl_wait();
     if (tid == 0) GNCX_TRACE_MARK(11, 0);
@@ -359,8 +432,12 @@ __global__ void __launch_bounds__(NT) attn_partial_kernel(const AttnArgs a) {
         for (int task = warp; task < G + (own_row ? 1 : 0); task += NT / 32) {
             const bool isq = task < G;
             float* x = isq ? qs + (size_t)task * qrs : ks + (size_t)pn * rs;
-            warp_head_norm_rope(x, hd, isq ? a.post_qn : a.post_kn, a.post_norm != 0, a.post_eps, a.rope_c, a.rope_s,
-                                pos, lane);
+            if (post_pf)
+                warp_head_norm_rope_pf(x, hd, hp, (isq ? a.post_qn : a.post_kn) != nullptr, a.post_norm != 0,
+                                       a.post_eps, lane);
+            else
+                warp_head_norm_rope(x, hd, isq ? a.post_qn : a.post_kn, a.post_norm != 0, a.post_eps, a.rope_c,
+                                    a.rope_s, pos, lane);
             if (!isq)
                 for (int i = lane; i < hd; i += 32)
                     const_cast<float*>(a.kc)[(size_t)pos * ps + (size_t)kvh * a.kv_head_stride + i] = x[i];
