@@ -353,6 +353,67 @@ def attention_sweep(torch, lib, P, reps: int = 20) -> dict:
     return res
 
 
+def attention_kernel_sweep(torch, lib, P, reps: int = 5) -> dict:
+    """The same attention steps without host API time: one CUDA graph per
+    configuration holds back-to-back gncx_mqa_attention_step_ext calls (KV
+    write, split-KV partial, merge), each on its own copy of the cache (copies
+    totalling >= 2x L2, so every step streams its window from HBM), replayed
+    `reps` times; time per step = replay time / steps."""
+    nh, nkv, hd = 32, 8, 128
+    scale = float(np.float32(1.0 / np.sqrt(hd)))
+    peak = float(measured_peaks().get("hbm_gbs", 6650.0))
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    outer = torch.cuda.current_stream()
+    g0 = torch.Generator(device="cuda")
+    g0.manual_seed(13)
+    res = {}
+    for ctx, win in ((512, 0), (4096, 0), (32768, 0), (32768, 4096)):
+        span = min(ctx, win) if win > 0 else ctx
+        kv_bytes = 2 * ctx * nkv * hd * 4
+        copies = max(2, -(-2 * l2 // (2 * span * nkv * hd * 4)))
+        copies = min(copies, max(2, (24 << 30) // kv_bytes))  # stay within a few GB of the device
+        caches = [(torch.randn(ctx * nkv * hd, device="cuda", generator=g0),
+                   torch.randn(ctx * nkv * hd, device="cuda", generator=g0)) for _ in range(copies)]
+        q = torch.randn(nh * hd, device="cuda", generator=g0)
+        k = torch.randn(nkv * hd, device="cuda", generator=g0)
+        v = torch.randn(nkv * hd, device="cuda", generator=g0)
+        out = torch.empty(nh * hd, device="cuda")
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(outer)
+        with torch.cuda.stream(s):
+            lib.gncx_set_stream(ctypes.c_void_p(s.cuda_stream))
+            kc, vc = caches[0]
+            lib.gncx_mqa_attention_step_ext(P(q), P(k), P(v), P(kc), P(vc), ctx - 1, nh, nkv, hd, scale, win, 1,
+                                            P(out))  # workspace and attributes set up outside the capture
+            s.synchronize()
+            with torch.cuda.graph(g, stream=s):
+                for kc, vc in caches:
+                    lib.gncx_mqa_attention_step_ext(P(q), P(k), P(v), P(kc), P(vc), ctx - 1, nh, nkv, hd, scale,
+                                                    win, 1, P(out))
+        lib.gncx_set_stream(ctypes.c_void_p(outer.cuda_stream))
+        from gncx_b200 import core
+        core.check(lib)
+        g.replay()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(outer)
+            g.replay()
+            b.record(outer)
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b) / copies)
+        ms = statistics.median(times)
+        nbytes = 2 * span * nkv * hd * 4 + 2 * nkv * hd * 4 + 2 * nh * hd * 4
+        gbs = nbytes / (ms / 1e3) / 1e9
+        res[f"ctx {ctx}" + (f" window {win}" if win else "")] = {"us": ms * 1e3, "GB/s": gbs, "frac": gbs / peak,
+                                                                 "steps": copies}
+        del g, caches
+        torch.cuda.empty_cache()
+    return res
+
+
 def decode_bench(args, torch) -> dict:
     """Benchmark configuration 5: random-init 8B-shaped Qwen3 decoder (Q4_K
     weights, Q6_K tied head), 2048-token seeded prompt prefilled through the
@@ -648,6 +709,10 @@ def run_gpu(args) -> None:
                 line["attention"] = attention_sweep(torch, lib, P)
             except Exception as exc:  # reported; the GEMV numbers stand
                 line["attention"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+            try:
+                line["attention_kernel_only"] = attention_kernel_sweep(torch, lib, P)
+            except Exception as exc:  # reported; the GEMV numbers stand
+                line["attention_kernel_only"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
         if tp_decode is not None:
             line["decode"] = tp_decode
         elif not args.no_decode:
@@ -672,7 +737,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the per-format sweep table")
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B-shape decode/prefill measurement")
-    ap.add_argument("--model", default="qwen3-8b", choices=["qwen3-8b", "qwen3-0.6b"])
+    ap.add_argument("--model", default="qwen3-8b", choices=["qwen3-8b", "qwen3-0.6b", "qwen3-8b-2l"],
+                    help="qwen3-8b-2l: the 8B layer shape with two layers, for kernel profiling captures")
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--new-tokens", type=int, default=512)
     ap.add_argument("--seed", type=int, default=0)

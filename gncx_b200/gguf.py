@@ -192,6 +192,10 @@ CONFIGS = {
     # 8B shape (benchmark configuration 5)
     "qwen3-8b": dict(n_layers=36, dim=4096, n_heads=32, n_kv=8, head_dim=128, ffn=12288, vocab=151936,
                      eps=1e-6, rope_base=1e6),
+    # the 8B layer shape with two layers: profiling captures of single decode
+    # kernels (a few hundred MB on the device instead of ~5 GB)
+    "qwen3-8b-2l": dict(n_layers=2, dim=4096, n_heads=32, n_kv=8, head_dim=128, ffn=12288, vocab=151936,
+                        eps=1e-6, rope_base=1e6),
 }
 
 
