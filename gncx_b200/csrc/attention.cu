@@ -191,6 +191,42 @@ __device__ __forceinline__ void chunk_scores(const float* ks, int rs, const floa
     }
 }
 
+// The same scores from unpadded K rows (rows `hd` floats apart, as one bulk
+// copy lands them): eight lanes share one (position, head) dot, lane j
+// running the reference's chain j (d = 8m + j) with the query values in its
+// registers, then the fold ((c0+c4)+(c1+c5))+((c2+c6)+(c3+c7)) by shuffles.
+// The four (position, head) pairs of a warp are the G heads of G == 4 / 2 / 1
+// consecutive... pairs in (position, head) order, so a warp reads at most
+// 4 / G different K rows per step (the same row for G == 4).  hd % 8 == 0,
+// hd <= 128, G in {1, 2, 4}; the warps of the CTA take every NW-th group of
+// four pairs.
+template <class Store>
+__device__ __forceinline__ void chunk_scores_warp(const float* ks, int hd, const float* qs, int qrs, int G, int cn,
+                                                  Store store) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int s = lane >> 3, j = lane & 7, nm = hd >> 3;
+    const int g = s % G;  // this lane's head: the same for every group a warp takes (4 % G == 0)
+    float qv[16];
+#pragma unroll
+    for (int m = 0; m < 16; ++m) qv[m] = m < nm ? qs[(size_t)g * qrs + 8 * m + j] : 0.0f;
+    for (int pair0 = 4 * warp; pair0 < G * cn; pair0 += 4 * nw) {
+        const int pair = pair0 + s;
+        const int p = pair / G;
+        const bool ok = pair < G * cn;
+        const float* kr = ks + (size_t)(ok ? p : 0) * hd + j;
+        float c = 0.0f;
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+            if (m < nm) c = fadd(c, fmul(qv[m], kr[8 * m]));
+        const float c4 = __shfl_down_sync(0xffffffffu, c, 4);   // lanes j < 4: c_j + c_{j+4}
+        const float t = fadd(c, c4);
+        const float t1 = __shfl_down_sync(0xffffffffu, t, 1);   // lanes 0, 2: (c0+c4)+(c1+c5), (c2+c6)+(c3+c7)
+        const float u = fadd(t, t1);
+        const float u2 = __shfl_down_sync(0xffffffffu, u, 2);
+        if (ok && j == 0) store(g, p, fadd(u, u2));
+    }
+}
+
 constexpr int kPvHeads = 8;  // query heads accumulated per pass over V
 
 // acc[i] += sum over this thread's positions p = pg, pg + npg, ... of
@@ -337,7 +373,15 @@ __device__ __forceinline__ void warp_head_norm_rope_pf(float* x, int hd, const H
 }
 
 // Partial record per (query, head, split): [0] = max, [1] = sum of exp, [4..] = o[hd]
-template <bool VEC, bool SCORES_ONLY, int NT>
+// BULK (split-KV, head-major cache: a chunk of one head is contiguous): K and
+// V of the chunk arrive as one bulk copy (TMA) each into unpadded rows,
+// completing on s_bar[0] / s_bar[1], and the scores use the warp-per-dot
+// mapping that is conflict-free on unpadded rows.
+// POST (split-KV decode with the fused Q/K post step): the post step's gains
+// and rope factors are loaded into registers before the dependency wait (a
+// separate instantiation: the registers would lower the occupancy of the
+// long-window drop-in launches, which have no post step).
+template <bool VEC, bool SCORES_ONLY, int NT, bool BULK, bool POST>
 __global__ void __launch_bounds__(NT) attn_partial_kernel(const AttnArgs a) {
     extern __shared__ __align__(16) uint8_t smraw[];
     GNCX_TRACE_SCOPE(kTagAttnPartial, gridDim.x);
@@ -353,7 +397,7 @@ __global__ void __launch_bounds__(NT) attn_partial_kernel(const AttnArgs a) {
     const int G4 = (G + 3) & ~3;
     const int kvh = blockIdx.y;
     const int cn = min(chunk, len - c0);
-    const int rs = hd + kRowPad;
+    const int rs = BULK ? hd : hd + kRowPad;
     float* ks = reinterpret_cast<float*>(smraw);                                  // [chunk][rs]
     float* vs = ks + (size_t)chunk * rs;                                           // [chunk][rs]
     const int qrs = attn_q_stride(hd), sld = chunk + kScorePad;
@@ -370,13 +414,31 @@ __global__ void __launch_bounds__(NT) attn_partial_kernel(const AttnArgs a) {
     const int pn = t0 + len - 1 - (t0 + c0);  // the query's position within this chunk
     const bool own_row = a.post_k && pn >= 0 && pn < cn;
     const int n_load = own_row ? pn : cn;     // rows copied from the cache
+    __shared__ __align__(8) uint64_t s_bar[2];
+    if (BULK) {
+        if (tid == 0) {
+            mbar_init(&s_bar[0], 1);
+            mbar_init(&s_bar[1], 1);
+            fence_barrier_init();
+            const uint32_t bytes = (uint32_t)n_load * (uint32_t)hd * 4u;
+            mbar_arrive_expect_tx(&s_bar[0], bytes);
+            mbar_arrive_expect_tx(&s_bar[1], bytes);
+        }
+        __syncthreads();
+    }
 
     pdl_launch_dependents();
     // ---- stage K and V: rows written before the preceding kernel first (they
     // may stream in while it finishes), the rest after the dependency wait ----
     const int n_old = a.prefetch_old ? max(0, min(cn, (t0 + len - 1) - (t0 + c0))) : 0;
     auto stage_rows = [&](int pa, int pb) {
-        if (VEC) {
+        if (BULK) {
+            if (tid == 0 && pb > pa) {
+                const uint32_t bytes = (uint32_t)(pb - pa) * (uint32_t)hd * 4u;
+                bulk_g2s(ks + (size_t)pa * hd, a.kc + row0 + (size_t)pa * ps, bytes, &s_bar[0]);
+                bulk_g2s(vs + (size_t)pa * hd, a.vc + row0 + (size_t)pa * ps, bytes, &s_bar[1]);
+            }
+        } else if (VEC) {
             // thread -> one 16-byte piece c of rows pa + p0, pa + p0 + step, ...
             // (16-byte cp.async: per-row bulk copies measured slower -- the
             // SM's copy engine serialises hundreds of 512-byte copies)
@@ -400,14 +462,15 @@ __global__ void __launch_bounds__(NT) attn_partial_kernel(const AttnArgs a) {
     if (n_old > 0) stage_rows(0, n_old);
     // the post step's gains and rope factors, before the dependency wait: warp
     // `task` < G norms and rotates q head `task`, warp G the new K row
-    HeadPost hp;
-    const int post_pos = t0 + len - 1;
-    const int n_post = a.post_k ? G + (own_row ? 1 : 0) : 0;
     // (split-KV only: in exact mode, whose scores-only CTAs end right after the
     // post step, loading these early measured slower: 3.92 vs 3.38 ms/token)
-    const bool post_pf = !SCORES_ONLY && n_post <= NT / 32;
-    if (warp < n_post && post_pf)
-        head_post_load(hp, hd, warp < G ? a.post_qn : a.post_kn, a.rope_c, a.rope_s, post_pos, lane);
+    HeadPost hp;
+    const int n_post = a.post_k ? G + (own_row ? 1 : 0) : 0;
+    const bool post_pf = POST && !SCORES_ONLY && n_post <= NT / 32;
+    if constexpr (POST) {
+        if (warp < n_post && post_pf)
+            head_post_load(hp, hd, warp < G ? a.post_qn : a.post_kn, a.rope_c, a.rope_s, t0 + len - 1, lane);
+    }
     if (tid == 0) GNCX_TRACE_MARK(10, n_old);
     pdl_wait();
     if (tid == 0) GNCX_TRACE_MARK(11, 0);
@@ -432,7 +495,7 @@ __global__ void __launch_bounds__(NT) attn_partial_kernel(const AttnArgs a) {
         for (int task = warp; task < G + (own_row ? 1 : 0); task += NT / 32) {
             const bool isq = task < G;
             float* x = isq ? qs + (size_t)task * qrs : ks + (size_t)pn * rs;
-            if (post_pf)
+            if (POST && post_pf)
                 warp_head_norm_rope_pf(x, hd, hp, (isq ? a.post_qn : a.post_kn) != nullptr, a.post_norm != 0,
                                        a.post_eps, lane);
             else
@@ -444,7 +507,11 @@ __global__ void __launch_bounds__(NT) attn_partial_kernel(const AttnArgs a) {
         }
     }
     if (tid == 0) GNCX_TRACE_MARK(12, 0);
-    if (VEC) cp_async_wait<0>();
+    if (BULK) {
+        if (!mbar_wait(&s_bar[0], 0)) record_error(a.err, kErrTimeout);
+    } else if (VEC) {
+        cp_async_wait<0>();
+    }
     __syncthreads();
     if (tid == 0) GNCX_TRACE_MARK(13, 0);
 
@@ -459,7 +526,11 @@ __global__ void __launch_bounds__(NT) attn_partial_kernel(const AttnArgs a) {
     }
     {
         const float scale = a.scale;
-        chunk_scores(ks, rs, qs, qrs, G, hd, cn, [&](int g, int p, float dot) { sc[g * sld + p] = fmul(dot, scale); });
+        if (BULK)
+            chunk_scores_warp(ks, hd, qs, qrs, G, cn, [&](int g, int p, float dot) { sc[g * sld + p] = fmul(dot, scale); });
+        else
+            chunk_scores(ks, rs, qs, qrs, G, hd, cn,
+                         [&](int g, int p, float dot) { sc[g * sld + p] = fmul(dot, scale); });
     }
     __syncthreads();
 
@@ -482,6 +553,7 @@ __global__ void __launch_bounds__(NT) attn_partial_kernel(const AttnArgs a) {
     __syncthreads();
 
     if (tid == 0) GNCX_TRACE_MARK(15, 0);
+    if (BULK && !mbar_wait(&s_bar[1], 0)) record_error(a.err, kErrTimeout);
     // ---- o[g][d] = sum_p e[p][g] * v[p][d] ----
     const int npg = NT / hd > 0 ? NT / hd : 1;
     const int d = tid % hd, pg = tid / hd;
@@ -827,7 +899,24 @@ static cudaError_t launch_partial(const AttnArgs& a, dim3 grid, size_t smem, cud
     static const int force = getenv("GNCX_ATTN_THREADS") ? atoi(getenv("GNCX_ATTN_THREADS")) : 0;  // tuning override
     const bool wide = force ? force == 512
                             : a.hd <= 128 && (int64_t)grid.x * grid.y * grid.z <= 2 * (int64_t)device_info().sm_count;
-    auto k = wide ? attn_partial_kernel<VEC, SCORES_ONLY, 512> : attn_partial_kernel<VEC, SCORES_ONLY, 256>;
+    // one bulk copy per chunk for K and for V where a chunk of a head is
+    // contiguous (the engine's head-major cache), split-KV mode
+    static const bool no_bulk = getenv("GNCX_ATTN_NO_BULK") != nullptr;  // tuning override
+    const int G = a.n_heads / a.n_kv;
+    const bool bulk = !no_bulk && VEC && !SCORES_ONLY && a.kv_pos_stride == a.hd && a.hd % 8 == 0 && a.hd <= 128 &&
+                      (G == 1 || G == 2 || G == 4) && (((uintptr_t)a.kc | (uintptr_t)a.vc) & 15) == 0 &&
+                      (a.kv_head_stride % 4) == 0;
+    constexpr bool kSplit = VEC && !SCORES_ONLY;  // the instantiations with bulk / post variants
+    const bool post = kSplit && a.post_k != nullptr;
+    void (*k)(const AttnArgs) = nullptr;
+    if (bulk && post) k = wide ? attn_partial_kernel<VEC, SCORES_ONLY, 512, kSplit, kSplit>
+                               : attn_partial_kernel<VEC, SCORES_ONLY, 256, kSplit, kSplit>;
+    else if (bulk) k = wide ? attn_partial_kernel<VEC, SCORES_ONLY, 512, kSplit, false>
+                            : attn_partial_kernel<VEC, SCORES_ONLY, 256, kSplit, false>;
+    else if (post) k = wide ? attn_partial_kernel<VEC, SCORES_ONLY, 512, false, kSplit>
+                            : attn_partial_kernel<VEC, SCORES_ONLY, 256, false, kSplit>;
+    else k = wide ? attn_partial_kernel<VEC, SCORES_ONLY, 512, false, false>
+                  : attn_partial_kernel<VEC, SCORES_ONLY, 256, false, false>;
     const cudaError_t e = set_smem_limit(k, smem);
     if (e != cudaSuccess) return e;
     return launch_k(k, grid, dim3(wide ? 512 : 256), smem, st, a);
