@@ -17,7 +17,7 @@ CSRC = HERE / "csrc"
 OUT_DIR = HERE / "_build"
 LIB = HERE / "libgncx_llm_core.so"
 
-SOURCES = ["gemv.cu", "matbatch.cu", "matbatch_tc.cu", "attention.cu", "ops.cu", "fused.cu", "capi.cu", "engine.cu", "noalloc.cu",
+SOURCES = ["gemv.cu", "matbatch.cu", "matbatch_tc.cu", "attention.cu", "ops.cu", "fused.cu", "capi.cu", "engine.cu", "noalloc.cu", "decode_step.cu",
            "tp.cu"]
 
 NVCC_FLAGS = [

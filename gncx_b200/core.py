@@ -126,6 +126,7 @@ _SIGS = {
     "gncx_engine_generate": (c_int32, [c_void_p, POINTER(c_int32), c_int32, c_int32, c_double, c_int32,
                                        POINTER(c_int32)]),
     "gncx_engine_timing": (c_int32, [c_void_p, POINTER(c_double), POINTER(c_double), POINTER(c_int32)]),
+    "gncx_engine_decode_path": (c_int32, [c_void_p]),
 }
 
 _lib = None

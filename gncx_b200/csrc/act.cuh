@@ -121,7 +121,9 @@ __device__ __forceinline__ void act_quant_quarter(const float (&v)[8], bool ok, 
 // quantize one 32-input block (8 inputs each).  A thread's loads for up to
 // eight blocks are issued before any of them is quantized, so a long x costs
 // one L2 round trip per eight blocks, not one per block.  Must be called by a
-// multiple of 32 threads, all of them.
+// multiple of 32 threads, all of them.  CG: x was written by other CTAs of the
+// running kernel, so it is read from L2 (ld.global.cg), never from L1.
+template <bool CG = false>
 __device__ __forceinline__ void stage_act_fp32(const float* __restrict__ x, int in_dim, int8_t* qs, float4* rec,
                                                int tid, int nthreads) {
     constexpr int K = 8;
@@ -138,13 +140,13 @@ __device__ __forceinline__ void stage_act_fp32(const float* __restrict__ x, int 
             if (it0 + k < iters && b < nb) {
                 const float* src = x + (size_t)b * 32 + q4 * 8;
                 if (vec) {
-                    const float4 t0 = reinterpret_cast<const float4*>(src)[0];
-                    const float4 t1 = reinterpret_cast<const float4*>(src)[1];
+                    const float4 t0 = CG ? __ldcg(reinterpret_cast<const float4*>(src)) : reinterpret_cast<const float4*>(src)[0];
+                    const float4 t1 = CG ? __ldcg(reinterpret_cast<const float4*>(src) + 1) : reinterpret_cast<const float4*>(src)[1];
                     v[k][0] = t0.x; v[k][1] = t0.y; v[k][2] = t0.z; v[k][3] = t0.w;
                     v[k][4] = t1.x; v[k][5] = t1.y; v[k][6] = t1.z; v[k][7] = t1.w;
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) v[k][i] = src[i];
+                    for (int i = 0; i < 8; ++i) v[k][i] = CG ? __ldcg(src + i) : src[i];
                 }
             } else {
 #pragma unroll

@@ -227,6 +227,14 @@ struct Engine {
     size_t pf_score_cap = 0;
     ActBlock *pf_act = nullptr, *pf_actq = nullptr, *pf_actf = nullptr;
     size_t pf_part_floats = 0;
+    // persistent decode step (decode_step.cu): one launch for the layer stack
+    bool step_ok = false;
+    StepPlan step{};
+    StepLayer* step_layers = nullptr;
+    float *step_attn = nullptr, *step_proj = nullptr, *step_glu = nullptr, *step_part = nullptr;
+    float* step_scores = nullptr;
+    unsigned* step_sync = nullptr;
+    size_t step_sync_bytes = 0;
 };
 
 // Positions per attention split in decode: 128 where the chunk's K/V rows fit
@@ -318,6 +326,24 @@ static int gather_row(Engine* e, int slot) {
     return tp_gather_ll_launch(e->tp, buf, ll, row, sl, slot, e->d_err, e->stream);
 }
 
+// The LM head over the final norm in act_d and, if `sample`, the penalized
+// greedy argmax that appends the next token and advances the position.
+static int lm_head_and_sample(Engine* e, bool sample, double penalty) {
+    cudaStream_t s = e->stream;
+    if (sample && e->tp.size > 1) {
+        // each rank takes the penalized maximum of its vocabulary slice and the
+        // ranks swap (value, id) pairs: no logit crosses NVLink
+        CK(lm_head(e, false));
+        int32_t n_parts = 0;
+        CK(argmax_partials_launch(e->logits + e->voc0, e->voc_l, e->voc0, e->st, penalty, e->am_scratch, &n_parts, s));
+        CK(tp_argmax_state_launch(e->tp, e->ll_am, e->am_scratch, n_parts, e->st, e->out_ids, 1, e->d_err, s));
+        return kOk;
+    }
+    CK(lm_head(e));
+    if (sample) CK(argmax_state_launch(e->logits, e->vocab, e->st, penalty, e->out_ids, 1, e->am_scratch, s));
+    return kOk;
+}
+
 // One decode step: forward(st->token at st->pos) and, if `sample`, the
 // penalized argmax that appends the next token and advances the position.
 static int decode_step(Engine* e, bool sample, double penalty) {
@@ -330,6 +356,14 @@ static int decode_step(Engine* e, bool sample, double penalty) {
     float* gq = tp ? tp_buffer(e->tp, e->x_q) : nullptr;  // attention output (gathered)
     float* gf = tp ? tp_buffer(e->tp, e->x_f) : nullptr;  // GLU output (gathered)
     CK(dequant_launch(e->tok_embd, e->embd_type, 1, D, e->embd_scale, &e->st->token, e->hidden, s));
+    if (e->step_ok && !tp) {
+        // the whole layer stack as one persistent kernel; its counters start at zero
+        StepPlan plan = e->step;
+        plan.exact = e->exact ? 1 : 0;
+        CU(cudaMemsetAsync(e->step_sync, 0, e->step_sync_bytes, s));
+        CK(decode_step_launch(plan, s));
+        return lm_head_and_sample(e, sample, penalty);
+    }
     // layer 0's attention norm; every later norm runs in the epilogue of the
     // GEMV whose output it adds into the residual stream
     CK(add_norm_quant_launch(e->hidden, nullptr, e->L[0].attn_norm, 1, D, e->eps, ActOut{nullptr, e->act_d},
@@ -425,18 +459,7 @@ static int decode_step(Engine* e, bool sample, double penalty) {
             CK(gemv_norm(e, w.wd, w.td, e->act_f, nullptr, F, e->proj, next_norm));
         }
     }
-    if (sample && tp) {
-        // each rank takes the penalized maximum of its vocabulary slice and the
-        // ranks swap (value, id) pairs: no logit crosses NVLink
-        CK(lm_head(e, false));
-        int32_t n_parts = 0;
-        CK(argmax_partials_launch(e->logits + e->voc0, e->voc_l, e->voc0, e->st, penalty, e->am_scratch, &n_parts, s));
-        CK(tp_argmax_state_launch(e->tp, e->ll_am, e->am_scratch, n_parts, e->st, e->out_ids, 1, e->d_err, s));
-        return kOk;
-    }
-    CK(lm_head(e));
-    if (sample) CK(argmax_state_launch(e->logits, e->vocab, e->st, penalty, e->out_ids, 1, e->am_scratch, s));
-    return kOk;
+    return lm_head_and_sample(e, sample, penalty);
 }
 
 static int ensure_prefill(Engine* e, int B) {
@@ -633,6 +656,8 @@ static int tp_share(int nh, int nkv, int hd, int dim, int ffn, int vocab, int tp
     if (sh.voc <= 0) { err = "vocabulary too small for the tensor parallel size"; return kErrInvalidArg; }
     return kOk;
 }
+
+static int setup_step(Engine* e);
 
 // Load: read hyper-parameters, lay this rank's share of the tensors out in one
 // device arena, upload.
@@ -847,6 +872,73 @@ static int engine_load(Engine* e, const char* path, int max_seq, int tp_rank, in
     CU(cudaMalloc(&e->out_ids, (size_t)e->out_cap * 4));
     for (auto& ev : e->ev) CU(cudaEventCreate(&ev));
     (void)layer_or_null;
+    return setup_step(e);
+}
+
+// Plan the persistent decode step for this model (one GPU; q/k/v and gate/up
+// each stored as one matrix).  Models it does not cover keep the per-kernel
+// decode, which GNCX_DECODE_PERSISTENT selects for every model when 0.
+static int setup_step(Engine* e) {
+    e->step_ok = false;
+    if (e->tp.size > 1) return kOk;
+    const char* env = getenv("GNCX_DECODE_PERSISTENT");
+    if (!env || atoi(env) == 0) return kOk;
+    StepPlan p{};
+    std::vector<StepLayer> hl(e->n_layers);
+    for (int l = 0; l < e->n_layers; ++l) {
+        const LayerW& w = e->L[l];
+        if (!w.qkv_fused || !w.gu_fused) return kOk;
+        StepLayer& s = hl[l];
+        s.wqkv = w.wq; s.wo = w.wo; s.wg = w.wg; s.wu = w.wu; s.wd = w.wd;
+        s.tqkv = w.tq; s.to = w.to; s.tgu = w.tg; s.td = w.td;
+        s.attn_norm = w.attn_norm; s.ffn_norm = w.ffn_norm; s.q_norm = w.q_norm; s.k_norm = w.k_norm;
+        s.kc = w.kc; s.vc = w.vc;
+    }
+    p.n_layers = e->n_layers;
+    p.dim = e->dim;
+    p.nh = e->nh;
+    p.nkv = e->nkv;
+    p.hd = e->hd;
+    p.qd = e->q_dim;
+    p.kvd = e->kv_dim;
+    p.ffn = e->ffn;
+    p.max_seq = e->max_seq;
+    p.eps = e->eps;
+    p.scale = e->attn_scale;
+    p.qk_norm = e->qk_norm ? 1 : 0;
+    p.gelu = e->arch == 2 ? 1 : 0;
+    p.ahead = 192 * 1024;
+    if (const char* v = getenv("GNCX_STEP_AHEAD")) p.ahead = atoi(v);  // tuning override (bytes)
+    if (decode_step_plan(p, hl.data(), device_info().max_smem_optin) != kOk) return kOk;
+    const size_t R = (size_t)attn_record_floats(e->hd);
+    e->step_sync_bytes = decode_step_sync_words(e->n_layers) * 4;
+    CU(cudaMalloc(&e->step_layers, hl.size() * sizeof(StepLayer)));
+    CU(cudaMemcpy(e->step_layers, hl.data(), hl.size() * sizeof(StepLayer), cudaMemcpyHostToDevice));
+    CU(cudaMalloc(&e->step_attn, (size_t)e->q_dim * 4));
+    CU(cudaMalloc(&e->step_proj, (size_t)e->dim * 4));
+    CU(cudaMalloc(&e->step_glu, (size_t)e->ffn * 4));
+    CU(cudaMalloc(&e->step_part, (size_t)e->nh * p.max_splits * R * 4));
+    CU(cudaMalloc(&e->step_scores, (size_t)e->nh * p.score_stride * 4));
+    CU(cudaMalloc(&e->step_sync, e->step_sync_bytes));
+    p.layers = e->step_layers;
+    p.rope_c = e->rope_c;
+    p.rope_s = e->rope_s;
+    p.out_norm = e->out_norm;
+    p.st = e->st;
+    p.hidden = e->hidden;
+    p.normed = e->normed;
+    p.act_out = e->act_d;
+    p.qkv = e->qkv;
+    p.attn = e->step_attn;
+    p.proj_o = e->proj;
+    p.proj_d = e->step_proj;
+    p.glu = e->step_glu;
+    p.part = e->step_part;
+    p.scores = e->step_scores;
+    p.sync = e->step_sync;
+    p.err = e->d_err;
+    e->step = p;
+    e->step_ok = true;
     return kOk;
 }
 
@@ -856,7 +948,9 @@ static void engine_free(Engine* e) {
     if (e->graph) cudaGraphExecDestroy(e->graph);
     void* bufs[] = {e->scores, e->pf_scores, e->arena, e->kv, e->rope_c, e->rope_s, e->hidden, e->normed, e->proj, e->qkv, e->gu, e->logits_own,
                     e->act_d, e->act_q, e->act_f, e->part, e->st, e->am_scratch, e->d_err, e->out_ids, e->ids_dev,
-                    e->pf_h, e->pf_p, e->pf_qkv, e->pf_gu, e->pf_part, e->pf_act, e->pf_actq, e->pf_actf};
+                    e->pf_h, e->pf_p, e->pf_qkv, e->pf_gu, e->pf_part, e->pf_act, e->pf_actq, e->pf_actf,
+                    e->step_layers, e->step_attn, e->step_proj, e->step_glu, e->step_part, e->step_scores,
+                    e->step_sync};
     for (void* b : bufs)
         if (b) cudaFree(b);
     tp_free(e->tp);
@@ -1062,6 +1156,8 @@ int32_t gncx_engine_generate(void* h, const int32_t* prompt, int32_t n_prompt, i
     e->decode_steps = max_new - 1;
     return n_out;
 }
+
+int32_t gncx_engine_decode_path(void* h) { return h && static_cast<Engine*>(h)->step_ok ? 1 : 0; }
 
 // Device time of the last prefill and decode loop (ms) and the decode step count.
 int32_t gncx_engine_timing(void* h, double* prefill_ms, double* decode_ms, int32_t* decode_steps) {

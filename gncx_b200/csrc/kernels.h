@@ -177,6 +177,61 @@ int argmax_partials_launch(const float* logits, int32_t vocab, int32_t idx0, con
 int argmax_state_launch(const float* logits, int32_t vocab, DecodeState* st, double penalty, int32_t* out_ids,
                         int advance_pos, void* scratch, cudaStream_t s);
 
+// ---- persistent decode step (decode_step.cu) ----
+// One decode token's layer stack as one persistent kernel (one CTA per SM,
+// cooperative launch); single GPU, weights Q4_0 / Q8_0 / Q4_K / Q6_K with
+// q/k/v and gate/up each stored as one matrix of one type.
+constexpr int kStepMaxDim = 4096;       // hidden size (the residual stream lives in registers)
+constexpr int kStepStageBytes = 37120;  // one ring stage: 16 Q4_K rows of 4096 inputs + alignment slack
+constexpr int kStepMaxStages = 8;
+constexpr int kStepSyncWords = 32;      // counters per layer (phases, then per-KV-head words)
+struct StepLayer {
+    const uint8_t* wqkv;  // q, k, v rows back to back
+    const uint8_t* wo;
+    const uint8_t* wg;    // gate rows
+    const uint8_t* wu;    // up rows
+    const uint8_t* wd;
+    int tqkv, to, tgu, td;
+    const float* attn_norm;
+    const float* ffn_norm;
+    const float* q_norm;  // may be null
+    const float* k_norm;
+    float* kc;            // head-major cache [n_kv][max_seq][head_dim]
+    float* vc;
+};
+struct StepPlan {
+    const StepLayer* layers;  // device array [n_layers]
+    int n_layers, dim, nh, nkv, hd, qd, kvd, ffn, max_seq;
+    float eps, scale;
+    int qk_norm, gelu;
+    int exact;                // 1: attention in the reference's serial order (needs exact_ok)
+    const float* rope_c;
+    const float* rope_s;
+    const float* out_norm;
+    const DecodeState* st;    // the token's position
+    float* hidden;            // in: the token's embedding row; out: the final residual stream
+    float* normed;            // out: the final RMSNorm (fp32)
+    uint8_t* act_out;         // out: the same, staged act-Q8 for the LM head
+    float* qkv;               // [qd + 2 kvd]
+    float* attn;              // [qd]
+    float* proj_o;            // [dim]
+    float* proj_d;            // [dim]
+    float* glu;               // [ffn]
+    float* part;              // split-KV records [nh][max_splits][hd + 4]
+    float* scores;            // exact mode: scores, then softmax weights [nh][score_stride]
+    unsigned* sync;           // decode_step_sync_words(n_layers) words, zero before every launch
+    int32_t* err;
+    int ahead;                // bytes of L2 prefetch a CTA keeps ahead of its copies
+    // set by decode_step_plan
+    int chunk, max_splits, stage_bytes, stages, max_terms, exact_ok;
+    int score_stride;         // max_seq rounded up to a multiple of 4
+};
+// Checks the shapes and formats and fills the geometry fields; kOk when the
+// persistent kernel can run this model within max_smem bytes per CTA.
+int decode_step_plan(StepPlan& p, const StepLayer* host_layers, int max_smem);
+size_t decode_step_sync_words(int n_layers);
+int decode_step_launch(const StepPlan& p, cudaStream_t st);
+
 // ---- tensor parallelism (tp.cu) ----
 // One exchange region per rank: kTpCtlBytes of control words, then the gather
 // buffers at byte offsets chosen by the caller.  Control words: flags

@@ -123,6 +123,10 @@ class GNCXStreamer:
             self._check(-n)
         return list(out[:n])
 
+    def persistent_decode(self) -> bool:
+        """True when decode steps run as one persistent kernel per token."""
+        return self.lib.gncx_engine_decode_path(self.handle) == 1
+
     def timing(self) -> dict:
         p, d, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_int32()
         self.lib.gncx_engine_timing(self.handle, ctypes.byref(p), ctypes.byref(d), ctypes.byref(n))

@@ -251,6 +251,10 @@ int32_t gncx_engine_generate(void* engine, const int32_t* prompt, int32_t n_prom
                              double repeat_penalty, int32_t eos, int32_t* out_ids);
 /* Device time (ms) of the last prefill and decode loop, and the decode step count. */
 int32_t gncx_engine_timing(void* engine, double* prefill_ms, double* decode_ms, int32_t* decode_steps);
+/* Which kernels run a decode step (no counterpart in the reference): 1 = the
+ * whole layer stack as one persistent kernel (one GPU, a model whose shapes
+ * and formats it covers); 0 = one kernel per GEMV / norm / attention step. */
+int32_t gncx_engine_decode_path(void* engine);
 
 /* Tensor parallel over the GPUs of one box (no counterpart in the reference),
  * one process per GPU, each on its own current device.  Rank r of tp_size
