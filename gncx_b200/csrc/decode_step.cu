@@ -53,6 +53,7 @@
 #include "kernels.h"
 #include "norm.cuh"
 #include "tma.cuh"
+#include "trace.cuh"
 #include "units.cuh"
 
 namespace gncx {
@@ -60,7 +61,6 @@ namespace gncx {
 constexpr int kStepCW = 8;                  // compute warps
 constexpr int kStepCT = kStepCW * 32;       // compute threads
 constexpr int kStepThreads = kStepCT + 32;  // + the producer warp
-constexpr int kStepMaxUnits = kStepCT;      // 256-input units per GEMV tile: one per compute thread
 constexpr int kStepHPass = 8 * kStepCT;     // residual elements per register pass (8 per thread)
 constexpr int kStepMaxPasses = kStepMaxDim / kStepHPass;
 static_assert(kStepMaxPasses * kStepHPass == kStepMaxDim, "residual passes");
@@ -77,20 +77,30 @@ constexpr int kPvChunk = 256;   // exact mode: positions staged per PV step
 constexpr int kSmBlock = 512;   // exact mode: exp values staged per serial-sum block
 
 // ---------------------------------------------------------------- geometry
-// Whole rows per tile of a matrix with `in` inputs: at most one unit per
-// compute thread and the rows' bytes (+ alignment slack) within a stage;
-// `pair` tiles hold that many gate rows and as many up rows.
-__host__ __device__ inline int step_tile_rows(int type, int in, int stage_bytes, bool pair) {
+// A GEMV tile is kStepCW x (rows per warp) whole consecutive rows; within a
+// warp, `lpr` lanes share a row (lane j owns units j and j + lpr, as in the
+// per-kernel GEMV), so a warp finishes its rows on its own -- no barrier of
+// the compute warps per tile.
+__host__ __device__ inline int step_lpr(int upr) {
+    int l = 1;
+    while (l < 32 && 2 * l < upr) l <<= 1;
+    return l;
+}
+
+// Rows each compute warp takes per tile (gate/up: gate rows plus as many up
+// rows), limited by the lanes and by the tile fitting one stage; 0 when the
+// row does not fit.
+__host__ __device__ inline int step_warp_rows(int type, int in, int stage_bytes, bool pair) {
     const int upr = in / 256;
+    const int lpr = step_lpr(upr);
+    if (2 * lpr < upr) return 0;  // more than 16384 inputs
     const size_t rb = row_bytes(type, in);
-    int r;
+    int r = 32 / lpr;
     if (pair) {
-        r = (kStepMaxUnits / 2) / upr;
-        const int fit = (int)(((size_t)stage_bytes - 96) / (2 * rb));
-        r = r < fit ? r : fit;
+        const int fit = 2 * (int)(((size_t)stage_bytes - 96) / (2 * rb * kStepCW));
+        r = (r < fit ? r : fit) & ~1;
     } else {
-        r = kStepMaxUnits / upr;
-        const int fit = (int)(((size_t)stage_bytes - 32) / rb);
+        const int fit = (int)(((size_t)stage_bytes - 32) / (rb * kStepCW));
         r = r < fit ? r : fit;
     }
     return r;
@@ -117,7 +127,7 @@ struct StepSmem {
     uint64_t* empty;
     int8_t* qs;       // staged act-Q8 of the current GEMV input
     float4* rec;
-    float* red;       // [2][kStepMaxUnits * max_terms] unit terms awaiting the serial row sums
+    float* red;       // [kStepCW][64 * max_terms] unit terms awaiting the serial row sums
     float* scratch;   // norm squares / attention work area (union)
     uint8_t* ring;
 };
@@ -125,7 +135,8 @@ struct StepSmem {
 __host__ __device__ inline size_t step_act_bytes(int max_in) {
     return ((size_t)max_in + (size_t)(max_in / 32) * 16 + 127) & ~(size_t)127;
 }
-__host__ __device__ inline size_t step_red_bytes(int max_terms) { return (size_t)2 * kStepMaxUnits * max_terms * 4; }
+// A warp's rows cover at most 32 lanes x 2 units: 64 units of terms.
+__host__ __device__ inline size_t step_red_bytes(int max_terms) { return (size_t)kStepCW * 64 * max_terms * 4; }
 
 // Floats of the split-KV work area for G query heads per KV head.
 __host__ __device__ inline size_t step_attn_floats(int G, int hd, int chunk, int max_splits) {
@@ -159,13 +170,13 @@ __host__ __device__ inline size_t step_scratch_bytes(const StepPlan& p) {
 
 __host__ __device__ inline size_t step_smem_bytes(const StepPlan& p) {
     return 256 + step_act_bytes(step_max_in(p)) + step_red_bytes(p.max_terms) + step_scratch_bytes(p) +
-           (size_t)p.stages * p.stage_bytes;
+           (size_t)kStepStages * p.stage_bytes;
 }
 
 __device__ inline StepSmem step_carve(uint8_t* base, const StepPlan& p) {
     StepSmem s;
     s.full = reinterpret_cast<uint64_t*>(base);
-    s.empty = s.full + kStepMaxStages;
+    s.empty = s.full + kStepStages;
     uint8_t* q = base + 256;
     const int max_in = step_max_in(p);
     s.qs = reinterpret_cast<int8_t*>(q);
@@ -180,16 +191,6 @@ __device__ inline StepSmem step_carve(uint8_t* base, const StepPlan& p) {
 }
 
 // ---------------------------------------------------------------- the work list
-// One ring entry: up to two byte ranges (a gate/up tile has two), each copied
-// as its 16-byte-aligned superset; range 1 lands at stage offset `off1`.
-struct StepEntry {
-    const uint8_t* src0;
-    uint32_t n0;
-    const uint8_t* src1;
-    uint32_t n1;
-    uint32_t off1;
-};
-
 // Per-token geometry every thread derives from the plan.
 struct StepGeo {
     int G;          // CTAs
@@ -198,10 +199,6 @@ struct StepGeo {
     int n_split;    // attention chunks
     int n_items;    // attention chunk items: chunks x KV heads
 };
-
-__device__ __forceinline__ int step_mine(int n_total, const StepGeo& g) {
-    return n_total > g.cta ? (n_total - g.cta + g.G - 1) / g.G : 0;
-}
 
 __device__ __forceinline__ int step_rows_of(const StepPlan& p, int ph) {
     switch (ph) {
@@ -236,57 +233,8 @@ __device__ __forceinline__ const uint8_t* step_w_of(const StepLayer& L, int ph) 
     }
 }
 
-// Tiles of a GEMV phase.
-__device__ __forceinline__ int step_tiles(const StepPlan& p, const StepLayer& L, int ph, int& rows) {
-    rows = step_tile_rows(step_type_of(L, ph), step_in_of(p, ph), p.stage_bytes, ph == kPhGu);
-    const int n = step_rows_of(p, ph);
-    return (n + rows - 1) / rows;
-}
-
-// Ring entries per attention chunk item: K and V (split-KV) or K only (exact
-// mode, whose PV step loads V itself).
-__device__ __forceinline__ int step_attn_per_item(const StepPlan& p) { return p.exact ? 1 : 2; }
-
-// Ring entries of this CTA in phase `ph` of a layer.
-__device__ __forceinline__ int step_entries(const StepPlan& p, const StepLayer& L, const StepGeo& g, int ph) {
-    if (ph == kPhAttn) return step_attn_per_item(p) * step_mine(g.n_items, g);
-    int rows;
-    return step_mine(step_tiles(p, L, ph, rows), g);
-}
-
-__device__ StepEntry step_describe(const StepPlan& p, const StepLayer& L, const StepGeo& g, int ph, int k) {
-    StepEntry e{nullptr, 0u, nullptr, 0u, 0u};
-    if (ph == kPhAttn) {
-        const int per = step_attn_per_item(p);
-        const int item = g.cta + (k / per) * g.G;
-        const bool is_v = per == 2 && (k & 1);
-        const int split = item / p.nkv, kvh = item - split * p.nkv;
-        const int c0 = split * p.chunk;
-        // the chunk holding the token's own position loads the rows below it;
-        // its own row is made in the kernel
-        const int n_load = c0 + p.chunk > g.pos ? g.pos - c0 : p.chunk;
-        const float* cache = is_v ? L.vc : L.kc;
-        e.src0 = reinterpret_cast<const uint8_t*>(cache + ((size_t)kvh * p.max_seq + c0) * p.hd);
-        e.n0 = (uint32_t)n_load * (uint32_t)p.hd * 4u;
-        return e;
-    }
-    int rows;
-    step_tiles(p, L, ph, rows);
-    const int tile = g.cta + k * g.G;
-    const int r0 = tile * rows;
-    const int n_rows = step_rows_of(p, ph);
-    const int nr = min(rows, n_rows - r0);
-    const int type = step_type_of(L, ph);
-    const size_t rb = row_bytes(type, step_in_of(p, ph));
-    e.src0 = step_w_of(L, ph) + (size_t)r0 * rb;
-    e.n0 = (uint32_t)((size_t)nr * rb);
-    if (ph == kPhGu) {
-        e.src1 = L.wu + (size_t)r0 * rb;
-        e.n1 = e.n0;
-        e.off1 = (uint32_t)step_pair_offset(rows, rb);
-    }
-    return e;
-}
+// Index of a GEMV phase in the layer's tile geometry.
+__device__ __forceinline__ int step_gi(int ph) { return ph == kPhQkv ? 0 : ph - 1; }
 
 __device__ __forceinline__ uint32_t span16(const uint8_t* src, uint32_t n) {
     if (n == 0) return 0;
@@ -295,36 +243,13 @@ __device__ __forceinline__ uint32_t span16(const uint8_t* src, uint32_t n) {
     return (uint32_t)(e - a);
 }
 
-struct StepCursor {
-    int l, ph, k, n;  // layer, phase, entry within the phase, entries in the phase
+// The producer's position in the ring: the stage to fill next and how many
+// times the ring has wrapped (the empty barrier's phase to wait for).
+struct StepRing {
+    int s = 0;
+    uint32_t round = 0;
+    int n = 0;  // entries issued
 };
-
-__device__ void step_settle(const StepPlan& p, const StepGeo& g, StepCursor& c) {
-    while (c.l < p.n_layers) {
-        if (c.k < c.n) return;
-        c.k = 0;
-        if (++c.ph == kPhCount) {
-            c.ph = 0;
-            ++c.l;
-            if (c.l >= p.n_layers) return;
-        }
-        const StepLayer L = p.layers[c.l];
-        c.n = step_entries(p, L, g, c.ph);
-    }
-}
-
-__device__ StepCursor step_first(const StepPlan& p, const StepGeo& g) {
-    StepCursor c{0, 0, 0, 0};
-    const StepLayer L = p.layers[0];
-    c.n = step_entries(p, L, g, 0);
-    step_settle(p, g, c);
-    return c;
-}
-
-__device__ __forceinline__ void step_next(const StepPlan& p, const StepGeo& g, StepCursor& c) {
-    ++c.k;
-    step_settle(p, g, c);
-}
 
 // ---------------------------------------------------------------- synchronisation
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(kStepCT) : "memory"); }
@@ -352,6 +277,10 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
 }
 __device__ __forceinline__ int ld_volatile_i32(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 
+// Spinning threads look at the abort flag (a global word every CTA's threads
+// would otherwise hammer) and their deadline only once per this many cycles.
+constexpr long long kPollCycles = 16384;
+
 // Thread 0 of the compute warps publishes this CTA's part of a phase (after
 // the barrier every compute thread's stores of it are ordered before).
 __device__ __forceinline__ void step_signal(unsigned* ctr, int tid) {
@@ -369,9 +298,13 @@ __device__ bool step_wait(const unsigned* ctr, unsigned target, int* abort_flag,
     int ok = 1;
     if (tid == 0 && ld_acquire_u32(ctr) < target) {
         const long long t0 = clock64();
+        long long next = t0 + kPollCycles;
         while (ld_acquire_u32(ctr) < target) {
+            const long long now = clock64();
+            if (now < next) continue;
+            next = now + kPollCycles;
             if (ld_volatile_i32(abort_flag)) { ok = 0; break; }
-            if (clock64() - t0 > kWaitCycles) {
+            if (now - t0 > kWaitCycles) {
                 record_error(err, kErrTimeout);
                 atomicExch(abort_flag, 1);
                 ok = 0;
@@ -389,15 +322,92 @@ __device__ bool step_wait(const unsigned* ctr, unsigned target, int* abort_flag,
 __device__ __forceinline__ void step_stage_wait(uint64_t* bar, uint32_t parity, int* abort_flag, int32_t* err) {
     if (mbar_try_wait(bar, parity)) return;
     const long long t0 = clock64();
+    long long next = t0 + kPollCycles;
     while (!mbar_try_wait(bar, parity)) {
+        const long long now = clock64();
+        if (now < next) continue;
+        next = now + kPollCycles;
         if (ld_volatile_i32(abort_flag)) return;
-        if (clock64() - t0 > kWaitCycles) {
+        if (now - t0 > kWaitCycles) {
             record_error(err, kErrTimeout);
             atomicExch(abort_flag, 1);
             return;
         }
     }
 }
+
+// ---------------------------------------------------------------- timeline marks
+// Diagnostic builds (-DGNCX_TRACE) record, per CTA and layer, %globaltimer at
+// the phase boundaries of the compute warps (thread 0) into the trace buffer:
+// one block of records per CTA, reserved with one atomic at kernel start.
+constexpr int kStepMarks = 16;
+constexpr int kStepTraceEntries = 2048;  // ring entries per CTA traced (producer and consumer)
+#ifdef GNCX_TRACE
+__device__ TraceRec* step_trace_block(unsigned n) {
+    if (!g_trace_rec) return nullptr;
+    const unsigned i = atomicAdd(g_trace_n, n);
+    return i + n <= g_trace_cap ? g_trace_rec + i : nullptr;
+}
+__device__ __forceinline__ TraceRec*& step_cblk() {
+    __shared__ TraceRec* blk;
+    return blk;
+}
+#define STEP_CUSE(idx, t0v)                                  \
+    do {                                                     \
+        if (threadIdx.x == 0) STEP_ENTRY_REC(step_cblk(), kTagStepUse, (idx), (t0v)); \
+    } while (0)
+#define STEP_ENTRY_DECL(name) TraceRec* name = nullptr
+#define STEP_ENTRY_INIT(name) name = step_trace_block(kStepTraceEntries)
+#define STEP_ENTRY_T0(v) const unsigned long long v = trace_clock()
+#define STEP_ENTRY_REC(blk, tag, idx, t0v)                                                      \
+    do {                                                                                        \
+        if ((blk) && (idx) < kStepTraceEntries) {                                               \
+            const unsigned long long t1_ = trace_clock();                                       \
+            trace_fill((blk)[idx], (tag), (uint32_t)(idx), (t0v), t1_, 0);                      \
+        }                                                                                       \
+    } while (0)
+#define STEP_TRACE_DECL TraceRec* tblk = nullptr
+#define STEP_TRACE_INIT(nl)                                                   \
+    do {                                                                      \
+        if (tid == 0 && g_trace_rec) {                                        \
+            const unsigned n_ = (unsigned)(nl) * kStepMarks;                  \
+            const unsigned i_ = atomicAdd(g_trace_n, n_);                     \
+            if (i_ + n_ <= g_trace_cap) tblk = g_trace_rec + i_;              \
+        }                                                                     \
+    } while (0)
+#define STEP_MARK(m, l)                                                                                  \
+    do {                                                                                                 \
+        if (tblk) {                                                                                      \
+            const unsigned long long t_ = trace_clock();                                                 \
+            trace_fill(tblk[(l) * kStepMarks + (m)], kTagStep, (uint32_t)((m) | ((l) << 8)), t_, t_, 1); \
+        }                                                                                                \
+    } while (0)
+#else
+#define STEP_TRACE_DECL \
+    do {                \
+    } while (0)
+#define STEP_TRACE_INIT(nl) \
+    do {                    \
+    } while (0)
+#define STEP_MARK(m, l) \
+    do {                \
+    } while (0)
+#define STEP_ENTRY_DECL(name) \
+    do {                      \
+    } while (0)
+#define STEP_ENTRY_INIT(name) \
+    do {                      \
+    } while (0)
+#define STEP_ENTRY_T0(v) \
+    do {                 \
+    } while (0)
+#define STEP_ENTRY_REC(blk, tag, idx, t0v) \
+    do {                                   \
+    } while (0)
+#define STEP_CUSE(idx, t0v) \
+    do {                    \
+    } while (0)
+#endif
 
 // ---------------------------------------------------------------- residual stream + RMSNorm
 struct StepResid {
@@ -439,7 +449,7 @@ __device__ __forceinline__ void step_add_residual(StepResid& r, const float* y, 
 // lanes over x[4k+j]^2 combined in double (csrc/gncx_llm_kernels.cpp:789-840),
 // then y = (x * inv) * w quantized per 32 inputs (:955-995).  Same arithmetic
 // as add_norm_quant_row_kernel.
-__device__ void step_norm_quant(const StepResid& r, const float (&g)[kStepMaxPasses][8], int dim, float eps,
+__device__ __noinline__ void step_norm_quant(const StepResid& r, const float (&g)[kStepMaxPasses][8], int dim, float eps,
                                 const StepSmem& sm, float* normed, int tid) {
     __shared__ float s_inv;
     float* sq = sm.scratch;  // [4][dim/4]
@@ -524,26 +534,36 @@ __device__ void step_norm_quant(const StepResid& r, const float (&g)[kStepMaxPas
     cbar();
 }
 
+// act-Q8 staging of an fp32 vector other CTAs wrote (one shared copy, as above).
+__device__ __noinline__ void step_stage_act(const float* x, int n, const StepSmem& sm, int tid) {
+    stage_act_fp32<true>(x, n, sm.qs, sm.rec, tid, kStepCT);
+    cbar();
+}
+
 // ---------------------------------------------------------------- GEMV tiles
+// This lane's units (j and j + lpr) of the row at `rowp` in a stage, their
+// terms parked in the row's slots of the warp's term area.
 template <int T>
-__device__ __forceinline__ void step_units(const uint8_t* r0p, const uint8_t* r1p, int split, int rb, int nr, int upr,
-                                           const ActView& av, float* red, int tid) {
+__device__ __forceinline__ void step_lane_units(const uint8_t* rowp, int j, int lpr, int upr, const ActView& av,
+                                                float* terms) {
     constexpr int UB = Fmt<T>::UB, NW = Fmt<T>::NW, E = Fmt<T>::E;
-    if (tid < nr * upr) {
-        const int r = tid / upr, u = tid - r * upr;
-        const uint8_t* rp = r < split ? r0p + (size_t)r * rb : r1p + (size_t)(r - split) * rb;
-        uint32_t w[NW];
-        load_unit_smem<NW, T != kQ6_K>(rp + (size_t)u * UB, w);
-        float t[E];
-        unit_terms<T>(w, UnitAct{av, u}, t);
-        float* dst = red + (size_t)tid * E;
-        if constexpr (E % 4 == 0) {
 #pragma unroll
-            for (int e = 0; e < E; e += 4)
-                *reinterpret_cast<float4*>(dst + e) = make_float4(t[e], t[e + 1], t[e + 2], t[e + 3]);
-        } else {
+    for (int k = 0; k < 2; ++k) {
+        const int u = j + k * lpr;
+        if (u < upr) {
+            uint32_t w[NW];
+            load_unit_smem<NW, T != kQ6_K>(rowp + (size_t)u * UB, w);
+            float t[E];
+            unit_terms<T>(w, UnitAct{av, u}, t);
+            float* dst = terms + (size_t)u * E;
+            if constexpr (E % 4 == 0) {
 #pragma unroll
-            for (int e = 0; e < E; ++e) dst[e] = t[e];
+                for (int e = 0; e < E; e += 4)
+                    *reinterpret_cast<float4*>(dst + e) = make_float4(t[e], t[e + 1], t[e + 2], t[e + 3]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < E; ++e) dst[e] = t[e];
+            }
         }
     }
 }
@@ -567,58 +587,70 @@ __host__ __device__ __forceinline__ int type_terms(int t) { return (t == kQ4_0 |
 
 // One GEMV phase of this CTA: tiles cta, cta + G, ... of the matrix, outputs
 // to y (rows) -- or, for the gate/up phase, glu(gate row, up row) to y.
-__device__ void step_gemv_phase(const StepPlan& p, const StepLayer& L, const StepGeo& g, int ph, const StepSmem& sm,
-                                int& item, int& red_buf, float* y, int* abort_flag, int tid) {
-    const int lane = tid & 31;
-    int rows;
-    const int n_tiles = step_tiles(p, L, ph, rows);
-    const int type = step_type_of(L, ph);
-    const int in = step_in_of(p, ph);
-    const int upr = in / 256;
-    const size_t rb = row_bytes(type, in);
+// Each warp takes its rows of a tile and finishes them alone: units into its
+// term area, the stage released, then each row's first lane adds the row's
+// terms in unit order (and, for gate/up, takes the up row's sum from the
+// lane that formed it).  FMT: the one format of every matrix, or 0.
+//
+// Not inlined: the four GEMV phases of a layer share one copy of this code,
+// which stays in the instruction caches across phases (inlined copies, one
+// per call site, were fetched cold at the start of every phase).
+template <int FMT>
+__device__ __noinline__ void step_gemv_phase(const StepPlan& p, const StepLayer& L, const StepGeo& g, int ph, const StepSmem& sm,
+                                int& item, float* y, int* abort_flag, int tid) {
+    const int lane = tid & 31, warp = tid >> 5;
+    const int gi = step_gi(ph);
+    const int rows = L.rows[gi];
+    const int wr = L.wrows[gi];
+    const int n_tiles = L.tiles[gi];
+    const int type = FMT ? FMT : step_type_of(L, ph);
+    const int upr = step_in_of(p, ph) / 256;
+    const int lpr = step_lpr(upr);
+    const size_t rb = (size_t)L.rbytes[gi];
     const int n_rows = step_rows_of(p, ph);
     const int E = type_terms(type);
     const ActView av{sm.qs, sm.rec};
     const uint8_t* w = step_w_of(L, ph);
     const bool pair = ph == kPhGu;
+    const int rloc = lane / lpr, j = lane - rloc * lpr;
+    const int hp = pair ? wr / 2 : wr;         // output rows of this warp per tile
+    const bool up = pair && rloc >= hp;         // this lane's row is an up row
+    const int orow = warp * hp + (up ? rloc - hp : rloc);  // output row within the tile
+    float* terms = sm.red + (size_t)warp * 64 * p.max_terms + (size_t)rloc * upr * E;
     for (int tile = g.cta; tile < n_tiles; tile += g.G, ++item) {
-        const int s = item % p.stages;
-        const uint32_t par = (uint32_t)(item / p.stages) & 1u;
+        const int s = item & (kStepStages - 1);
+        const uint32_t par = (uint32_t)(item / kStepStages) & 1u;
+        STEP_ENTRY_T0(ct0);
         step_stage_wait(&sm.full[s], par, abort_flag, p.err);
+        STEP_CUSE(item, ct0);
         const int r0 = tile * rows;
         const int nr = min(rows, n_rows - r0);
-        uint8_t* stage = sm.ring + (size_t)s * p.stage_bytes;
-        const uint8_t* src0 = w + (size_t)r0 * rb;
-        const uint8_t* r0p = stage + ((uintptr_t)src0 & 15);
-        const uint8_t* r1p = r0p;
-        int split = nr;
-        int nr_all = nr;
-        if (pair) {
-            const uint8_t* src1 = L.wu + (size_t)r0 * rb;
-            r1p = stage + step_pair_offset(rows, rb) + ((uintptr_t)src1 & 15);
-            nr_all = 2 * nr;
-        }
-        float* red = sm.red + (size_t)red_buf * kStepMaxUnits * p.max_terms;
-        switch (type) {
-            case kQ4_K: step_units<kQ4_K>(r0p, r1p, split, (int)rb, nr_all, upr, av, red, tid); break;
-            case kQ6_K: step_units<kQ6_K>(r0p, r1p, split, (int)rb, nr_all, upr, av, red, tid); break;
-            case kQ4_0: step_units<kQ4_0>(r0p, r1p, split, (int)rb, nr_all, upr, av, red, tid); break;
-            default: step_units<kQ8_0>(r0p, r1p, split, (int)rb, nr_all, upr, av, red, tid); break;
+        const bool valid = rloc < wr && orow < nr;
+        const uint8_t* stage = sm.ring + (size_t)s * p.stage_bytes;
+        const uint8_t* src = (up ? L.wu : w) + (size_t)r0 * rb;
+        const uint8_t* rowp = stage + (up ? L.pair_off : 0) + ((uintptr_t)src & 15) + (size_t)orow * rb;
+        if (valid) {
+            if constexpr (FMT != 0) {
+                step_lane_units<FMT>(rowp, j, lpr, upr, av, terms);
+            } else {
+                switch (type) {
+                    case kQ4_K: step_lane_units<kQ4_K>(rowp, j, lpr, upr, av, terms); break;
+                    case kQ6_K: step_lane_units<kQ6_K>(rowp, j, lpr, upr, av, terms); break;
+                    case kQ4_0: step_lane_units<kQ4_0>(rowp, j, lpr, upr, av, terms); break;
+                    default: step_lane_units<kQ8_0>(rowp, j, lpr, upr, av, terms); break;
+                }
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[s]);
-        cbar();
-        const int nt = upr * E;
-        if (tid < nr) {
-            if (pair) {
-                const float gv = step_row_sum(red + (size_t)tid * nt, nt);
-                const float uv = step_row_sum(red + (size_t)(nr + tid) * nt, nt);
-                y[r0 + tid] = p.gelu ? geglu1(gv, uv) : swiglu1(gv, uv);
-            } else {
-                y[r0 + tid] = step_row_sum(red + (size_t)tid * nt, nt);
-            }
+        const float acc = (valid && j == 0) ? step_row_sum(terms, upr * E) : 0.0f;
+        if (pair) {
+            const float uacc = __shfl_down_sync(0xffffffffu, acc, hp * lpr);
+            if (valid && j == 0 && !up) y[r0 + orow] = p.gelu ? geglu1(acc, uacc) : swiglu1(acc, uacc);
+        } else if (valid && j == 0) {
+            y[r0 + orow] = acc;
         }
-        red_buf ^= 1;
+        __syncwarp();  // the term area is rewritten by the next tile
     }
 }
 
@@ -629,8 +661,10 @@ __device__ void step_gemv_phase(const StepPlan& p, const StepLayer& L, const Ste
 // token's own position -- the new K row made in the stage (normed, rotated)
 // and the new K and V rows written to the cache.  Returns the K stage.
 __device__ __forceinline__ float* step_chunk_prologue(const StepPlan& p, const StepLayer& L, const StepGeo& g,
-                                                      int kvh, int pn, bool own, float* qs, int qrs, int sK,
-                                                      uint32_t parK, const StepSmem& sm, int* abort_flag, int tid) {
+                                                      int kvh, int pn, bool own, float* qs, int qrs, int kitem,
+                                                      const StepSmem& sm, int* abort_flag, int tid) {
+    const int sK = kitem & (kStepStages - 1);
+    const uint32_t parK = (uint32_t)(kitem / kStepStages) & 1u;
     const int lane = tid & 31, warp = tid >> 5;
     const int hd = p.hd;
     const int G = p.nh / p.nkv;
@@ -642,7 +676,9 @@ __device__ __forceinline__ float* step_chunk_prologue(const StepPlan& p, const S
         __syncwarp();
         warp_head_norm_rope(x, hd, L.q_norm, p.qk_norm != 0, p.eps, p.rope_c, p.rope_s, g.pos, lane);
     }
+    STEP_ENTRY_T0(ct0);
     step_stage_wait(&sm.full[sK], parK, abort_flag, p.err);
+    STEP_CUSE(kitem, ct0);
     float* ks = reinterpret_cast<float*>(sm.ring + (size_t)sK * p.stage_bytes);
     const int kw = G % kStepCW;  // the warp that makes the new K row
     if (own && warp == kw) {
@@ -700,12 +736,12 @@ __device__ void step_attn_item(const StepPlan& p, const StepLayer& L, const Step
     const int npg = kStepCT / hd;
     float* wsm = pvs + (size_t)npg * kPvHeads * hd;  // [G][max_splits]
     float* lsm = wsm + (size_t)G * p.max_splits;     // [G][max_splits]
-    const int sK = item % p.stages;
-    const uint32_t parK = (uint32_t)(item / p.stages) & 1u;
-    const int sV = (item + 1) % p.stages;
-    const uint32_t parV = (uint32_t)((item + 1) / p.stages) & 1u;
+    const int sK = item & (kStepStages - 1);
+    const int vitem = item + 1;
+    const int sV = vitem & (kStepStages - 1);
+    const uint32_t parV = (uint32_t)(vitem / kStepStages) & 1u;
+    float* ks = step_chunk_prologue(p, L, g, kvh, pn, own, qs, qrs, item, sm, abort_flag, tid);
     item += 2;
-    float* ks = step_chunk_prologue(p, L, g, kvh, pn, own, qs, qrs, sK, parK, sm, abort_flag, tid);
     float* vs = reinterpret_cast<float*>(sm.ring + (size_t)sV * p.stage_bytes);
     cbar();
     {
@@ -731,7 +767,9 @@ __device__ void step_attn_item(const StepPlan& p, const StepLayer& L, const Step
         if (lane == 0) { red2[2 * gg] = mx; red2[2 * gg + 1] = sum; }
     }
     for (int i = tid; i < cn * (G4 - G); i += kStepCT) es[(size_t)(i / (G4 - G)) * G4 + G + i % (G4 - G)] = 0.0f;
+    STEP_ENTRY_T0(vt0);
     step_stage_wait(&sm.full[sV], parV, abort_flag, p.err);
+    STEP_CUSE(vitem, vt0);
     if (own) {
         const float* vsrc = p.qkv + p.qd + p.kvd + (size_t)kvh * hd;
         for (int i = tid; i < hd; i += kStepCT) vs[(size_t)pn * hd + i] = __ldcg(vsrc + i);
@@ -864,10 +902,9 @@ __device__ void step_exact_scores_item(const StepPlan& p, const StepLayer& L, co
     const bool own = pn < cn;
     const int qrs = hd + 4;
     float* qs = sm.scratch;  // [G][qrs]
-    const int sK = item % p.stages;
-    const uint32_t parK = (uint32_t)(item / p.stages) & 1u;
+    const int sK = item & (kStepStages - 1);
+    float* ks = step_chunk_prologue(p, L, g, kvh, pn, own, qs, qrs, item, sm, abort_flag, tid);
     item += 1;
-    float* ks = step_chunk_prologue(p, L, g, kvh, pn, own, qs, qrs, sK, parK, sm, abort_flag, tid);
     cbar();
     {
         const float scale = p.scale;
@@ -945,7 +982,95 @@ __device__ void step_exact_pv_item(const StepPlan& p, const StepLayer& L, const 
     if (chain) p.attn[(size_t)(kvh * G + w) * hd + d0 + c] = acc;
 }
 
+// ---------------------------------------------------------------- the producer
+// One ring entry: wait until the stage is free, then one bulk copy per byte
+// range (each range's 16-byte-aligned superset; range 1 at stage offset
+// off1).  False when the wait gave up (the CTA is aborting).
+__device__ __forceinline__ bool step_issue(const StepSmem& sm, const StepPlan& p, StepRing& rg, const uint8_t* src0,
+                                           uint32_t n0, const uint8_t* src1, uint32_t n1, uint32_t off1,
+                                           int* abort_flag) {
+    const int s = rg.s;
+    if (rg.round > 0) {
+        const uint32_t par = (rg.round - 1) & 1u;
+        if (!mbar_try_wait(&sm.empty[s], par)) {
+            const long long t0 = clock64();
+            long long next = t0 + kPollCycles;
+            while (!mbar_try_wait(&sm.empty[s], par)) {
+                const long long now = clock64();
+                if (now < next) continue;
+                next = now + kPollCycles;
+                if (ld_volatile_i32(abort_flag)) return false;
+                if (now - t0 > kWaitCycles) {
+                    record_error(p.err, kErrTimeout);
+                    atomicExch(abort_flag, 1);
+                    return false;
+                }
+            }
+        }
+    }
+    const uint32_t b0 = span16(src0, n0), b1 = span16(src1, n1);
+    uint8_t* stage = sm.ring + (size_t)s * p.stage_bytes;
+    mbar_arrive_expect_tx(&sm.full[s], b0 + b1);
+    if (b0) bulk_g2s(stage, reinterpret_cast<const void*>((uintptr_t)src0 & ~(uintptr_t)15), b0, &sm.full[s]);
+    if (b1) bulk_g2s(stage + off1, reinterpret_cast<const void*>((uintptr_t)src1 & ~(uintptr_t)15), b1, &sm.full[s]);
+    ++rg.n;
+    if (++rg.s == kStepStages) {
+        rg.s = 0;
+        ++rg.round;
+    }
+    return true;
+}
+
+// The CTA's tiles of one GEMV phase of layer L.
+__device__ __forceinline__ bool step_issue_gemv(const StepSmem& sm, const StepPlan& p, const StepLayer& L,
+                                                const StepGeo& g, int ph, StepRing& rg, int* abort_flag) {
+    const int gi = step_gi(ph);
+    const int rows = L.rows[gi];
+    const size_t rb = (size_t)L.rbytes[gi];
+    const int n_rows = step_rows_of(p, ph);
+    const uint8_t* w = step_w_of(L, ph);
+    const bool pair = ph == kPhGu;
+    for (int tile = g.cta; tile < L.tiles[gi]; tile += g.G) {
+        const int r0 = tile * rows;
+        const uint32_t n = (uint32_t)((size_t)min(rows, n_rows - r0) * rb);
+        if (!step_issue(sm, p, rg, w + (size_t)r0 * rb, n, pair ? L.wu + (size_t)r0 * rb : nullptr, pair ? n : 0u,
+                        (uint32_t)L.pair_off, abort_flag))
+            return false;
+    }
+    return true;
+}
+
+// The producer warp's lane 0: every ring entry of the CTA, in the order the
+// compute warps consume them.  Returns after every copy it issued has landed.
+template <bool EXACT>
+__device__ void step_producer(const StepSmem& sm, const StepPlan& p, const StepGeo& g, int* abort_flag) {
+    StepRing rg;
+    bool ok = true;
+    for (int l = 0; l < p.n_layers && ok; ++l) {
+        const StepLayer L = p.layers[l];
+        ok = step_issue_gemv(sm, p, L, g, kPhQkv, rg, abort_flag);
+        for (int it = g.cta; it < g.n_items && ok; it += g.G) {
+            const int split = it / p.nkv, kvh = it - split * p.nkv;
+            const int c0 = split * p.chunk;
+            // the chunk holding the token's own position loads the rows below
+            // it; its own row is made in the kernel
+            const uint32_t n = (uint32_t)(c0 + p.chunk > g.pos ? g.pos - c0 : p.chunk) * (uint32_t)p.hd * 4u;
+            const size_t off = ((size_t)kvh * p.max_seq + c0) * p.hd;
+            ok = step_issue(sm, p, rg, reinterpret_cast<const uint8_t*>(L.kc + off), n, nullptr, 0u, 0u, abort_flag);
+            if (!EXACT && ok)
+                ok = step_issue(sm, p, rg, reinterpret_cast<const uint8_t*>(L.vc + off), n, nullptr, 0u, 0u, abort_flag);
+        }
+        ok = ok && step_issue_gemv(sm, p, L, g, kPhO, rg, abort_flag);
+        ok = ok && step_issue_gemv(sm, p, L, g, kPhGu, rg, abort_flag);
+        ok = ok && step_issue_gemv(sm, p, L, g, kPhDown, rg, abort_flag);
+    }
+    // every copy issued has landed before the CTA may exit
+    for (int k = rg.n > kStepStages ? rg.n - kStepStages : 0; k < rg.n; ++k)
+        if (!mbar_wait(&sm.full[k % kStepStages], (uint32_t)(k / kStepStages) & 1u)) record_error(p.err, kErrTimeout);
+}
+
 // ---------------------------------------------------------------- the kernel
+template <bool EXACT, int FMT>
 __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const StepPlan p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const StepSmem sm = step_carve(smem, p);
@@ -960,7 +1085,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     g.n_split = (g.len + p.chunk - 1) / p.chunk;
     g.n_items = g.n_split * p.nkv;
     if (tid == 0) {
-        for (int i = 0; i < p.stages; ++i) {
+        for (int i = 0; i < kStepStages; ++i) {
             mbar_init(&sm.full[i], 1);
             mbar_init(&sm.empty[i], kStepCW);
         }
@@ -969,63 +1094,16 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
     __syncthreads();
 
     if (warp == kStepCW) {
-        // ---------------- producer: the CTA's weight tiles and K/V chunks, in order ----------------
-        if (lane != 0) return;
-        StepCursor c = step_first(p, g);
-        StepCursor pf = c;
-        uint32_t ahead = 0;
-        int item = 0;
-        const uint32_t want_ahead = (uint32_t)p.ahead;
-        while (c.l < p.n_layers) {
-            if (want_ahead) {
-                while (pf.l < p.n_layers && ahead < want_ahead) {
-                    const StepLayer Lp = p.layers[pf.l];
-                    const StepEntry e = step_describe(p, Lp, g, pf.ph, pf.k);
-                    const uint32_t b0 = span16(e.src0, e.n0), b1 = span16(e.src1, e.n1);
-                    if (b0) bulk_prefetch_l2(reinterpret_cast<const void*>((uintptr_t)e.src0 & ~(uintptr_t)15), b0);
-                    if (b1) bulk_prefetch_l2(reinterpret_cast<const void*>((uintptr_t)e.src1 & ~(uintptr_t)15), b1);
-                    ahead += b0 + b1;
-                    step_next(p, g, pf);
-                }
-            }
-            const StepLayer L = p.layers[c.l];
-            const StepEntry e = step_describe(p, L, g, c.ph, c.k);
-            const int s = item % p.stages;
-            const int use = item / p.stages;
-            if (use > 0) {
-                const uint32_t par = (uint32_t)(use - 1) & 1u;
-                bool ok = mbar_try_wait(&sm.empty[s], par);
-                if (!ok) {
-                    const long long t0 = clock64();
-                    while (!(ok = mbar_try_wait(&sm.empty[s], par))) {
-                        if (ld_volatile_i32(abort_flag)) break;
-                        if (clock64() - t0 > kWaitCycles) {
-                            record_error(p.err, kErrTimeout);
-                            atomicExch(abort_flag, 1);
-                            break;
-                        }
-                    }
-                }
-                if (!ok) break;
-            }
-            const uint32_t b0 = span16(e.src0, e.n0), b1 = span16(e.src1, e.n1);
-            uint8_t* stage = sm.ring + (size_t)s * p.stage_bytes;
-            mbar_arrive_expect_tx(&sm.full[s], b0 + b1);
-            if (b0) bulk_g2s(stage, reinterpret_cast<const void*>((uintptr_t)e.src0 & ~(uintptr_t)15), b0, &sm.full[s]);
-            if (b1)
-                bulk_g2s(stage + e.off1, reinterpret_cast<const void*>((uintptr_t)e.src1 & ~(uintptr_t)15), b1,
-                         &sm.full[s]);
-            if (want_ahead) ahead = ahead > b0 + b1 ? ahead - (b0 + b1) : 0;
-            ++item;
-            step_next(p, g, c);
-        }
-        // every copy issued has landed before the CTA may exit
-        for (int k = item > p.stages ? item - p.stages : 0; k < item; ++k)
-            if (!mbar_wait(&sm.full[k % p.stages], (uint32_t)(k / p.stages) & 1u)) record_error(p.err, kErrTimeout);
+        if (lane == 0) step_producer<EXACT>(sm, p, g, abort_flag);
         return;
     }
 
     // ---------------- compute warps ----------------
+    STEP_TRACE_DECL;
+    STEP_TRACE_INIT(p.n_layers);
+#ifdef GNCX_TRACE
+    if (tid == 0) step_cblk() = step_trace_block(kStepTraceEntries);
+#endif
     StepResid r;
     const int dim = p.dim;
 #pragma unroll
@@ -1038,7 +1116,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             h[0] = a.x; h[1] = a.y; h[2] = a.z; h[3] = a.w; h[4] = b.x; h[5] = b.y; h[6] = b.z; h[7] = b.w;
         }
     }
-    int item = 0, red_buf = 0;
+    int item = 0;
     float gn[kStepMaxPasses][8];
     const unsigned G = (unsigned)g.G;
     const int n_pv = p.nkv * (p.hd / kPvCols);  // exact mode PV items
@@ -1046,19 +1124,24 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         const StepLayer L = p.layers[l];
         unsigned* sy = p.sync + (size_t)l * kStepSyncWords;
         // ---- residual add (the previous layer's ffn_down) + attention RMSNorm
+        STEP_MARK(0, l);
         step_load_gains(L.attn_norm, dim, tid, gn);
         if (l > 0) {
             if (!step_wait(p.sync + (size_t)(l - 1) * kStepSyncWords + kSyDown, G, abort_flag, p.err, tid)) return;
             step_add_residual(r, p.proj_d, dim, tid);
         }
+        STEP_MARK(1, l);
         step_norm_quant(r, gn, dim, p.eps, sm, nullptr, tid);
+        STEP_MARK(2, l);
         // ---- QKV GEMV
-        step_gemv_phase(p, L, g, kPhQkv, sm, item, red_buf, p.qkv, abort_flag, tid);
+        step_gemv_phase<FMT>(p, L, g, kPhQkv, sm, item, p.qkv, abort_flag, tid);
         step_signal(&sy[kSyQkv], tid);
+        STEP_MARK(3, l);
         // ---- attention
         if (!step_wait(&sy[kSyQkv], G, abort_flag, p.err, tid)) return;
+        STEP_MARK(4, l);
         unsigned attn_target = (unsigned)p.nkv;
-        if (!p.exact) {
+        if constexpr (!EXACT) {
             for (int it = g.cta; it < g.n_items; it += g.G) step_attn_item(p, L, g, it, sm, item, sy, abort_flag, tid);
         } else {
             for (int it = g.cta; it < g.n_items; it += g.G)
@@ -1073,25 +1156,32 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             }
             attn_target = (unsigned)n_pv;
         }
+        STEP_MARK(5, l);
         // ---- O GEMV on the re-quantized attention output
         if (!step_wait(&sy[kSyAttn], attn_target, abort_flag, p.err, tid)) return;
-        stage_act_fp32<true>(p.attn, p.qd, sm.qs, sm.rec, tid, kStepCT);
-        cbar();
-        step_gemv_phase(p, L, g, kPhO, sm, item, red_buf, p.proj_o, abort_flag, tid);
+        STEP_MARK(6, l);
+        step_stage_act(p.attn, p.qd, sm, tid);
+        STEP_MARK(12, l);
+        step_gemv_phase<FMT>(p, L, g, kPhO, sm, item, p.proj_o, abort_flag, tid);
         step_signal(&sy[kSyO], tid);
+        STEP_MARK(7, l);
         // ---- residual add + ffn RMSNorm
         step_load_gains(L.ffn_norm, dim, tid, gn);
         if (!step_wait(&sy[kSyO], G, abort_flag, p.err, tid)) return;
+        STEP_MARK(8, l);
         step_add_residual(r, p.proj_o, dim, tid);
         step_norm_quant(r, gn, dim, p.eps, sm, nullptr, tid);
+        STEP_MARK(9, l);
         // ---- gate/up GEMV with the GLU in its epilogue
-        step_gemv_phase(p, L, g, kPhGu, sm, item, red_buf, p.glu, abort_flag, tid);
+        step_gemv_phase<FMT>(p, L, g, kPhGu, sm, item, p.glu, abort_flag, tid);
         step_signal(&sy[kSyGu], tid);
+        STEP_MARK(10, l);
         // ---- ffn_down on the re-quantized GLU output
         if (!step_wait(&sy[kSyGu], G, abort_flag, p.err, tid)) return;
-        stage_act_fp32<true>(p.glu, p.ffn, sm.qs, sm.rec, tid, kStepCT);
-        cbar();
-        step_gemv_phase(p, L, g, kPhDown, sm, item, red_buf, p.proj_d, abort_flag, tid);
+        STEP_MARK(11, l);
+        step_stage_act(p.glu, p.ffn, sm, tid);
+        STEP_MARK(13, l);
+        step_gemv_phase<FMT>(p, L, g, kPhDown, sm, item, p.proj_d, abort_flag, tid);
         step_signal(&sy[kSyDown], tid);
     }
     // ---- final residual add + output norm: CTA 0 writes the LM head's input
@@ -1126,7 +1216,7 @@ static bool fmt_ok(int t, int in) {
     return row_bytes(t, in) % 16 == 0 || t == kQ6_K;
 }
 
-int decode_step_plan(StepPlan& p, const StepLayer* host_layers, int max_smem) {
+int decode_step_plan(StepPlan& p, StepLayer* host_layers, int max_smem) {
     if (p.n_layers <= 0 || p.dim <= 0 || p.dim > kStepMaxDim || p.dim % 256 || p.nh <= 0 || p.nkv <= 0 ||
         p.nh % p.nkv || p.max_seq <= 0)
         return kErrInvalidArg;
@@ -1142,16 +1232,25 @@ int decode_step_plan(StepPlan& p, const StepLayer* host_layers, int max_smem) {
     p.exact_ok = 1;
     p.score_stride = (p.max_seq + 3) & ~3;
     int max_terms = 1;
+    bool all_q4k = true;
     for (int l = 0; l < p.n_layers; ++l) {
-        const StepLayer& L = host_layers[l];
+        StepLayer& L = host_layers[l];
         const int ts[4] = {L.tqkv, L.to, L.tgu, L.td};
         const int ins[4] = {p.dim, p.qd, p.dim, p.ffn};
+        const int outs[4] = {p.qd + 2 * p.kvd, p.dim, p.ffn, p.dim};
         for (int i = 0; i < 4; ++i) {
             if (!fmt_ok(ts[i], ins[i])) return kErrInvalidArg;
-            if (step_tile_rows(ts[i], ins[i], p.stage_bytes, i == 2) < 1) return kErrCapacity;
+            const int wr = step_warp_rows(ts[i], ins[i], p.stage_bytes, i == 2);
+            if (wr < (i == 2 ? 2 : 1)) return kErrCapacity;
+            L.wrows[i] = i == 2 ? wr / 2 * 2 : wr;
+            L.rows[i] = kStepCW * (i == 2 ? wr / 2 : wr);
+            L.tiles[i] = (outs[i] + L.rows[i] - 1) / L.rows[i];
+            L.rbytes[i] = (int)row_bytes(ts[i], ins[i]);
             const int e = type_terms(ts[i]);
             max_terms = e > max_terms ? e : max_terms;
+            all_q4k = all_q4k && ts[i] == kQ4_K;
         }
+        L.pair_off = step_pair_offset(L.rows[2], (size_t)L.rbytes[2]);
         // the 16-byte unit loads of the aligned formats need 16-byte aligned rows
         const uintptr_t ptrs[5] = {(uintptr_t)L.wqkv, (uintptr_t)L.wo, (uintptr_t)L.wg, (uintptr_t)L.wu,
                                    (uintptr_t)L.wd};
@@ -1161,18 +1260,17 @@ int decode_step_plan(StepPlan& p, const StepLayer* host_layers, int max_smem) {
         if (((uintptr_t)L.kc | (uintptr_t)L.vc) % 16) return kErrUnaligned;
     }
     p.max_terms = max_terms;
-    for (int s = kStepMaxStages; s >= 2; --s) {
-        p.stages = s;
-        if (step_smem_bytes(p) <= (size_t)max_smem) return kOk;
-    }
-    return kErrCapacity;
+    p.all_q4k = all_q4k ? 1 : 0;
+    return step_smem_bytes(p) <= (size_t)max_smem ? kOk : kErrCapacity;
 }
 
 size_t decode_step_sync_words(int n_layers) { return (size_t)(n_layers + 1) * kStepSyncWords; }
 
-int decode_step_launch(const StepPlan& p, cudaStream_t st) {
+template <bool EXACT, int FMT>
+static int step_launch_t(const StepPlan& p, cudaStream_t st) {
+    auto k = decode_step_kernel<EXACT, FMT>;
     const size_t smem = step_smem_bytes(p);
-    if (set_smem_limit(decode_step_kernel, smem) != cudaSuccess) return kErrCuda;
+    if (set_smem_limit(k, smem) != cudaSuccess) return kErrCuda;
     const DeviceInfo& dev = device_info();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(dev.sm_count);
@@ -1184,7 +1282,12 @@ int decode_step_launch(const StepPlan& p, cudaStream_t st) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, decode_step_kernel, p) == cudaSuccess ? kOk : kErrCuda;
+    return cudaLaunchKernelEx(&cfg, k, p) == cudaSuccess ? kOk : kErrCuda;
+}
+
+int decode_step_launch(const StepPlan& p, cudaStream_t st) {
+    if (p.exact) return p.all_q4k ? step_launch_t<true, kQ4_K>(p, st) : step_launch_t<true, 0>(p, st);
+    return p.all_q4k ? step_launch_t<false, kQ4_K>(p, st) : step_launch_t<false, 0>(p, st);
 }
 
 }  // namespace gncx

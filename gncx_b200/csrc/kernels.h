@@ -182,8 +182,8 @@ int argmax_state_launch(const float* logits, int32_t vocab, DecodeState* st, dou
 // cooperative launch); single GPU, weights Q4_0 / Q8_0 / Q4_K / Q6_K with
 // q/k/v and gate/up each stored as one matrix of one type.
 constexpr int kStepMaxDim = 4096;       // hidden size (the residual stream lives in registers)
-constexpr int kStepStageBytes = 37120;  // one ring stage: 16 Q4_K rows of 4096 inputs + alignment slack
-constexpr int kStepMaxStages = 8;
+constexpr int kStepStageBytes = 73856;  // one ring stage: 32 Q4_K rows of 4096 inputs + alignment slack
+constexpr int kStepStages = 2;
 constexpr int kStepSyncWords = 32;      // counters per layer (phases, then per-KV-head words)
 struct StepLayer {
     const uint8_t* wqkv;  // q, k, v rows back to back
@@ -198,6 +198,13 @@ struct StepLayer {
     const float* k_norm;
     float* kc;            // head-major cache [n_kv][max_seq][head_dim]
     float* vc;
+    // tile geometry of the four GEMVs (q/k/v, attn_output, gate/up, ffn_down),
+    // filled in by decode_step_plan
+    int rows[4];          // rows per tile (gate/up: gate rows, with as many up rows)
+    int wrows[4];         // rows per compute warp (gate/up: gate rows, with as many up rows)
+    int tiles[4];
+    int rbytes[4];        // bytes per row
+    int pair_off;         // gate/up: stage offset of the up rows
 };
 struct StepPlan {
     const StepLayer* layers;  // device array [n_layers]
@@ -223,12 +230,12 @@ struct StepPlan {
     int32_t* err;
     int ahead;                // bytes of L2 prefetch a CTA keeps ahead of its copies
     // set by decode_step_plan
-    int chunk, max_splits, stage_bytes, stages, max_terms, exact_ok;
+    int chunk, max_splits, stage_bytes, max_terms, exact_ok, all_q4k;
     int score_stride;         // max_seq rounded up to a multiple of 4
 };
 // Checks the shapes and formats and fills the geometry fields; kOk when the
 // persistent kernel can run this model within max_smem bytes per CTA.
-int decode_step_plan(StepPlan& p, const StepLayer* host_layers, int max_smem);
+int decode_step_plan(StepPlan& p, StepLayer* host_layers, int max_smem);
 size_t decode_step_sync_words(int n_layers);
 int decode_step_launch(const StepPlan& p, cudaStream_t st);
 

@@ -19,6 +19,9 @@ enum TraceTag : uint32_t {
     kTagGemv = 1, kTagGemvBf16, kTagMatbatch, kTagMatbatchTc, kTagAttnPartial, kTagAttnCombine, kTagAttnPrefill,
     kTagAttnExactSoftmax, kTagAttnExactPv, kTagAddNormQuant, kTagAddNormQuantRow, kTagQkvPost, kTagGluQuant,
     kTagArgmax1, kTagArgmax2, kTagDequant, kTagActQuant, kTagActStage, kTagTpGather, kTagTpGatherLl, kTagOther,
+    kTagStep,  // the persistent decode step's phase marks: aux = mark | layer << 8
+    kTagStepIssue,  // its producer, per ring entry: t0 before the slot wait, t1 after the copy is issued
+    kTagStepUse,    // its compute warps, per ring entry: t0 before the stage wait, t1 when the data is there
 };
 
 struct TraceRec {
