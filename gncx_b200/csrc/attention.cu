@@ -476,6 +476,141 @@ __global__ void __launch_bounds__(NT) attn_partial_kernel(const AttnArgs a) {
     }
 }
 
+// ---- long windows: one CTA per (range of chunks, KV head) streams its chunks ----
+// A CTA walks kStreamChunk-position chunks of its KV head through two
+// shared-memory buffers (cp.async: chunk j + 2 is in flight while chunk j is
+// scored and summed) and keeps an online softmax per query head -- running
+// maximum m, sum l and unnormalised output o, rescaled by e^(m_old - m_new)
+// when a chunk raises the maximum -- so loading and computing overlap inside
+// the CTA and the merge sees one record per CTA instead of one per chunk.
+// Records {m, l, -, -, o[hd]} like the split-KV partial kernel's; split-KV
+// softmax mode (sums in a different order from the reference's serial ones,
+// outputs within ~1e-6 relative).  Rows are unpadded (kv rows of head_dim
+// floats), scored with eight lanes per dot.
+constexpr int kStreamThreads = 256;
+constexpr int kStreamChunk = 32;
+constexpr int kStreamCtasPerSm = 3;  // resident together, so one CTA's loads and latency overlap the others'
+
+__host__ __device__ inline size_t attn_stream_smem_bytes(int G, int hd) {
+    const int G4 = (G + 3) & ~3;
+    return ((size_t)4 * kStreamChunk * hd                      // K and V, two buffers each
+            + (size_t)G * attn_q_stride(hd)                    // q heads
+            + (size_t)G * (kStreamChunk + kScorePad)           // scores
+            + (size_t)kStreamChunk * G4                        // exp, position-major
+            + (size_t)4 * G) * 4;                              // m, l, correction per head
+}
+
+__global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_kernel(const AttnArgs a, int cpp) {
+    extern __shared__ __align__(16) uint8_t smraw[];
+    GNCX_TRACE_SCOPE(kTagAttnPartial, gridDim.x);
+    pdl_launch_dependents();
+    pdl_wait();
+    const int hd = a.hd;
+    const int G = a.n_heads / a.n_kv, G4 = (G + 3) & ~3;
+    const int part = blockIdx.x, kvh = blockIdx.y;
+    int t0, len;
+    attn_window(a, 0, t0, len);
+    const int n_chunks = (len + kStreamChunk - 1) / kStreamChunk;
+    const int j0 = part * cpp, j1 = min(n_chunks, j0 + cpp);
+    if (j0 >= j1) return;  // uniform per CTA
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = kStreamThreads / 32;
+    float* kb = reinterpret_cast<float*>(smraw);                  // [2][chunk][hd]
+    float* vb = kb + (size_t)2 * kStreamChunk * hd;               // [2][chunk][hd]
+    const int qrs = attn_q_stride(hd), sld = kStreamChunk + kScorePad;
+    float* qs = vb + (size_t)2 * kStreamChunk * hd;               // [G][qrs]
+    float* sc = qs + (size_t)G * qrs;                              // [G][sld]
+    float* es = sc + (size_t)G * sld;                              // [chunk][G4]
+    float* st = es + (size_t)kStreamChunk * G4;                    // [G]{m, l, corr, -}
+    const size_t ps = (size_t)a.kv_pos_stride;
+    const float* kbase = a.kc + (size_t)t0 * ps + (size_t)kvh * a.kv_head_stride;
+    const float* vbase = a.vc + (size_t)t0 * ps + (size_t)kvh * a.kv_head_stride;
+    const int cpr = hd >> 2;  // 16-byte pieces per row
+    auto issue = [&](int j) {
+        const int c0 = j * kStreamChunk;
+        const int cn = min(kStreamChunk, len - c0);
+        float* kd = kb + (size_t)(j & 1) * kStreamChunk * hd;
+        float* vd = vb + (size_t)(j & 1) * kStreamChunk * hd;
+        for (int i = tid; i < cn * cpr; i += kStreamThreads) {
+            const int pp = i / cpr, c = i - pp * cpr;
+            cp_async16(kd + (size_t)pp * hd + 4 * c, kbase + (size_t)(c0 + pp) * ps + 4 * c);
+            cp_async16(vd + (size_t)pp * hd + 4 * c, vbase + (size_t)(c0 + pp) * ps + 4 * c);
+        }
+        cp_async_commit();
+    };
+    issue(j0);
+    if (j0 + 1 < j1) issue(j0 + 1);
+    const float* qz = a.q + (size_t)kvh * G * hd;
+    for (int i = tid; i < G * hd; i += kStreamThreads) qs[(size_t)(i / hd) * qrs + i % hd] = qz[i];
+    if (tid < G) { st[4 * tid] = -INFINITY; st[4 * tid + 1] = 0.0f; }
+    // PV mapping: thread (d, position group pg) accumulates column d of every head
+    const int npg = kStreamThreads / hd;
+    const int d = tid % hd, pg = tid / hd;
+    float acc[kPvHeads];
+#pragma unroll
+    for (int i = 0; i < kPvHeads; ++i) acc[i] = 0.0f;
+    const float scale = a.scale;
+    for (int j = j0; j < j1; ++j) {
+        if (j + 1 < j1) cp_async_wait<1>(); else cp_async_wait<0>();
+        __syncthreads();  // chunk j landed for every thread; qs / stats written
+        const int c0 = j * kStreamChunk;
+        const int cn = min(kStreamChunk, len - c0);
+        const float* ks = kb + (size_t)(j & 1) * kStreamChunk * hd;
+        const float* vs = vb + (size_t)(j & 1) * kStreamChunk * hd;
+        chunk_scores_warp(ks, hd, qs, qrs, G, cn, NW, [&](int g, int pp, float dot) { sc[g * sld + pp] = fmul(dot, scale); });
+        __syncthreads();
+        for (int g = warp; g < G; g += NW) {
+            float mx = -INFINITY;
+            for (int pp = lane; pp < cn; pp += 32) mx = fmaxf(mx, sc[g * sld + pp]);
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float m_old = st[4 * g];
+            const float m_new = fmaxf(m_old, mx);
+            float sum = 0.0f;
+            for (int pp = lane; pp < cn; pp += 32) {
+                const float e = exp_cr(fsub(sc[g * sld + pp], m_new));
+                es[(size_t)pp * G4 + g] = e;
+                sum += e;
+            }
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) {
+                const float corr = exp_cr(fsub(m_old, m_new));  // 0 for the first chunk (m_old = -inf)
+                st[4 * g] = m_new;
+                st[4 * g + 1] = fadd(fmul(st[4 * g + 1], corr), sum);
+                st[4 * g + 2] = corr;
+            }
+        }
+        for (int i = tid; i < cn * (G4 - G); i += kStreamThreads)
+            es[(size_t)(i / (G4 - G)) * G4 + G + i % (G4 - G)] = 0.0f;
+        __syncthreads();
+        if (pg < npg) {
+#pragma unroll
+            for (int i = 0; i < kPvHeads; ++i)
+                if (i < G) acc[i] = fmul(acc[i], st[4 * i + 2]);
+            chunk_pv(vs, hd, es, G4, 0, G, cn, d, pg, npg, acc);
+        }
+        __syncthreads();  // buffer j & 1 is free again
+        if (j + 2 < j1) issue(j + 2);
+    }
+    // sum the position groups' partial outputs (through the K buffers) and
+    // write this CTA's record of every head of the group
+    float* scr = kb;  // [npg][kPvHeads][hd] <= 2 * kStreamChunk * hd floats
+    if (pg < npg) {
+#pragma unroll
+        for (int i = 0; i < kPvHeads; ++i)
+            if (i < G) scr[((size_t)pg * kPvHeads + i) * hd + d] = acc[i];
+    }
+    __syncthreads();
+    const size_t R = attn_record_floats(hd);
+    for (int t = tid; t < G * hd; t += kStreamThreads) {
+        const int i = t / hd, dd = t - i * hd;
+        float v = scr[(size_t)i * hd + dd];
+        for (int q = 1; q < npg; ++q) v += scr[((size_t)q * kPvHeads + i) * hd + dd];
+        float* rec = a.part + ((size_t)(kvh * G + i) * a.max_splits + part) * R;
+        rec[4 + dd] = v;
+        if (dd == 0) { rec[0] = st[4 * i]; rec[1] = st[4 * i + 1]; }
+    }
+}
+
 // Merge the split records of one (query, head).
 constexpr int kCombineThreads = 256;
 __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(const AttnArgs a) {
@@ -864,6 +999,39 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
         return kOk;  // the PV kernel also wrote act_out
     }
     const int Gq = a.n_heads / a.n_kv;
+    // One query over a long window (the drop-in step at thousands of
+    // positions): the streaming kernel, one CTA per (range of chunks, KV head),
+    // kStreamCtasPerSm resident per SM, when there are at least two chunks per CTA.
+    bool stream = false;
+    AttnArgs sa = a;
+    dim3 sgrid;
+    int cpp = 0;
+    size_t ssm = 0;
+    if (n_tok == 1 && !a.post_k && vec && a.hd % 8 == 0 && a.hd <= 128 && (kStreamThreads % a.hd) == 0 &&
+        (Gq == 1 || Gq == 2 || Gq == 4) && !getenv("GNCX_ATTN_NO_STREAM")) {
+        int t0s, lens;
+        if (a.pos_dev) {
+            lens = 0;  // the position lives on the device: the chunked kernel sizes itself at run time
+        } else {
+            t0s = a.window > 0 ? (a.pos0 - a.window + 1 > 0 ? a.pos0 - a.window + 1 : 0) : 0;
+            lens = a.pos0 + 1 - t0s;
+        }
+        const int n_chunks = (lens + kStreamChunk - 1) / kStreamChunk;
+        int parts = kStreamCtasPerSm * dev.sm_count / a.n_kv;
+        if (parts < 1) parts = 1;
+        ssm = attn_stream_smem_bytes(Gq, a.hd);
+        if (lens > 0 && n_chunks >= 2 * parts && ssm <= (size_t)dev.max_smem_optin) {
+            cpp = (n_chunks + parts - 1) / parts;
+            parts = (n_chunks + cpp - 1) / cpp;
+            if ((int64_t)parts <= a.max_splits) {  // one record per CTA fits the caller's record space
+                stream = true;
+                sgrid = dim3(parts, a.n_kv, 1);
+                sa.chunk = cpp * kStreamChunk;  // the merge's "split": one CTA's range of positions
+                sa.max_splits = a.max_splits;
+                if (set_smem_limit(attn_stream_kernel, ssm) != cudaSuccess) return kErrCuda;
+            }
+        }
+    }
     if (n_tok > 1 && vec && a.window == 0 && a.chunk == kPfChunk && (a.hd == 128 || a.hd == 64) &&
         kPfRows % Gq == 0 && Gq <= kPfRows && attn_prefill_smem_bytes(a.hd) <= (size_t)dev.max_smem_optin) {
         // query-tiled causal prefill; score_cap carries the query count
@@ -879,13 +1047,16 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
             if (set_smem_limit(attn_prefill_kernel<64>, psm) != cudaSuccess) return kErrCuda;
             e = launch_k(attn_prefill_kernel<64>, pgrid, dim3(kAttnThreads), psm, st, b);
         }
+    } else if (stream) {
+        e = launch_k(attn_stream_kernel, sgrid, dim3(kStreamThreads), ssm, st, sa, cpp);
     } else {
         e = vec ? launch_partial<true, false>(a, grid, smem, st) : launch_partial<false, false>(a, grid, smem, st);
     }
     if (e != cudaSuccess) return kErrCuda;
-    const size_t csm = (size_t)a.max_splits * 8 + kCombineThreads * 4;
+    const AttnArgs& ca = stream ? sa : a;
+    const size_t csm = (size_t)ca.max_splits * 8 + kCombineThreads * 4;
     if (set_smem_limit(attn_combine_kernel, csm) != cudaSuccess) return kErrCuda;
-    return launch_k(attn_combine_kernel, dim3(a.n_heads, n_tok), dim3(kCombineThreads), csm, st, a) == cudaSuccess
+    return launch_k(attn_combine_kernel, dim3(a.n_heads, n_tok), dim3(kCombineThreads), csm, st, ca) == cudaSuccess
                ? kOk
                : kErrCuda;
 }

@@ -11,8 +11,7 @@
 // reference).
 //
 // CTA tile: 128 weight rows (TMEM lanes) x 32 tokens (TMEM columns), the
-// whole reduction dimension streamed one 256-input unit at a time through a
-// two-stage shared-memory ring:
+// whole reduction dimension streamed one 256-input unit at a time:
 //   * loader warps (4): each thread unpacks one row's unit (nibbles / int8
 //     quants) into int8 K-major core matrices (8 rows x 16 bytes) and its
 //     per-block scales; they also stage the tokens' int8 quants and scales;
@@ -20,13 +19,18 @@
 //     TMEM (8 x 32 columns) and commits them to mbarriers;
 //   * epilogue warps (8): warp w reads TMEM lanes 32(w%4).. (its rows) and
 //     16 of the 32 token columns, one block at a time, and accumulates the
-//     block terms.
-// The loaders fetch the next unit's weight bytes while unpacking the current
-// one and copy token quants with cp.async.
-// Units alternate between the two stages and the two TMEM halves, so the
-// tensor cores, the loaders and the epilogue overlap.  Every wait is bounded;
-// on a timeout the kernel records an error, skips the remaining work and
-// still releases TMEM.
+//     block terms.  The independent products of two tokens go through one
+//     packed `mul.rn.f32x2`; every sum stays a scalar __fadd_rn / __fsub_rn
+//     (a packed product feeding a packed sum may be fused into an FMA, which
+//     would not round like the reference).
+// The operand tiles (A, B) sit in a two-stage ring the MMA releases as soon
+// as it has read them; the scales sit in a separate four-stage ring the
+// epilogue releases, so the loaders run up to three units ahead of the
+// epilogue.  The loaders fetch the next unit's weight bytes while unpacking
+// the current one and copy token quants with cp.async.  Units alternate
+// between the two TMEM halves, so the tensor cores, the loaders and the
+// epilogue overlap.  Every wait is bounded; on a timeout the kernel records an
+// error, skips the remaining work and still releases TMEM.
 #include <cuda_runtime.h>
 #include "act.cuh"
 #include "common.cuh"
@@ -45,13 +49,19 @@ constexpr int kTcLoadWarps = 4;
 constexpr int kTcThreads = (kTcEpiWarps + kTcLoadWarps + 1) * 32;
 constexpr int kTcMmaWarp = kTcEpiWarps + kTcLoadWarps;
 
-// shared memory per stage
+// shared memory: operand stages (A + B tiles, free once the unit's MMAs have
+// read them) and scale stages (per-block weight and token scales, free once
+// the epilogue has applied them) in separate rings, so the loaders can run
+// kTcScaleStages - 1 units ahead of the epilogue
 constexpr int kTcA = 16 * 16 * 128;     // 16 K-chunks x 16 row groups x (8 rows x 16 B)
 constexpr int kTcB = 16 * 4 * 128;      // 16 K-chunks x 4 token groups x (8 tokens x 16 B)
 constexpr int kTcWS = 8 * kTcM * 8;     // per block, per row: float2
-constexpr int kTcAS = 8 * kTcN * 8;     // per block and token {d_a, sum q} (Q4_K: per chunk {lo, hi} pairs)
-constexpr int kTcStage = kTcA + kTcB + kTcWS + kTcAS;
-constexpr int kTcSmem = 2 * kTcStage + 128;
+constexpr int kTcAS = 8 * kTcN * 8;     // per block and token {d_a, sum q}, token pairs side by side
+constexpr int kTcOpStage = kTcA + kTcB;
+constexpr int kTcScStage = kTcWS + kTcAS;
+constexpr int kTcOpStages = 2;
+constexpr int kTcScaleStages = 4;
+constexpr int kTcSmem = kTcOpStages * kTcOpStage + kTcScaleStages * kTcScStage + 256;
 // More than half of an SM's shared memory, so one CTA per SM owns all of TMEM.
 constexpr int kTcSmemAlloc = kTcSmem > 120 * 1024 ? kTcSmem : 120 * 1024;
 
@@ -183,6 +193,27 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&v)[16]) {
         : "r"(taddr));
 }
 
+// Two fp32 values as one packed operand, and back.
+__device__ __forceinline__ unsigned long long pk2(float a, float b) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void upk2(unsigned long long v, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+// Two independent IEEE round-to-nearest products in one instruction.  Only
+// products go through the packed form: a packed product feeding a packed add
+// or subtract may be fused into a packed FMA by the backend (measured: the
+// all-packed epilogue differed from the scalar one in 64 % of outputs, the
+// packed-product form in none), so every sum stays a scalar __fadd_rn /
+// __fsub_rn, which is never contracted.
+__device__ __forceinline__ unsigned long long mul2_rn(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm volatile("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 template <int T>
 __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_t* __restrict__ w, size_t rb,
                                                                     const ActBlock* __restrict__ act, int batch,
@@ -194,12 +225,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
     constexpr int NE = kTcEpiWarps * 32;  // epilogue threads
     constexpr int NL = kTcLoadWarps * 32; // loader threads
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kTcStage);
-    uint64_t* empty = full + 2;
-    uint64_t* accf = full + 4;
-    uint64_t* acce = full + 6;
-    uint64_t* done = full + 8;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(full + 10);
+    uint8_t* sc_base = smem + kTcOpStages * kTcOpStage;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sc_base + kTcScaleStages * kTcScStage);  // operands loaded
+    uint64_t* empty = full + kTcOpStages;       // operands consumed by the MMAs
+    uint64_t* sfull = empty + kTcOpStages;      // scales written
+    uint64_t* sempty = sfull + kTcScaleStages;  // scales applied by the epilogue
+    uint64_t* accf = sempty + kTcScaleStages;
+    uint64_t* acce = accf + 2;
+    uint64_t* done = acce + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     __shared__ int abort_flag;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -208,9 +242,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
     const int upr = in_dim >> 8, nb = in_dim >> 5;
 
     if (tid == 0) {
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kTcOpStages; ++i) {
             mbar_init(&full[i], NL);
-            mbar_init(&empty[i], 1 + NE);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < kTcScaleStages; ++i) {
+            mbar_init(&sfull[i], NL);
+            mbar_init(&sempty[i], NE);
+        }
+        for (int i = 0; i < 2; ++i) {
             mbar_init(&accf[i], 1);
             mbar_init(&acce[i], NE);
         }
@@ -229,10 +269,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    auto stage_a = [&](int s) { return smem + s * kTcStage; };
-    auto stage_b = [&](int s) { return smem + s * kTcStage + kTcA; };
-    auto stage_ws = [&](int s) { return reinterpret_cast<float2*>(smem + s * kTcStage + kTcA + kTcB); };
-    auto stage_as = [&](int s) { return smem + s * kTcStage + kTcA + kTcB + kTcWS; };
+    auto stage_a = [&](int s) { return smem + s * kTcOpStage; };
+    auto stage_b = [&](int s) { return smem + s * kTcOpStage + kTcA; };
+    auto stage_ws = [&](int q) { return reinterpret_cast<float2*>(sc_base + q * kTcScStage); };
+    auto stage_as = [&](int q) { return sc_base + q * kTcScStage + kTcWS; };
     auto fail = [&]() {
         record_error(err, kErrTimeout);
         atomicExch(&abort_flag, 1);
@@ -255,8 +295,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
         };
         fetch(0);
         for (int u = 0; u < upr; ++u) {
-            const int s = u & 1;
-            if (u >= 2 && !mbar_wait(&empty[s], ((u >> 1) - 1) & 1)) fail();
+            const int s = u & (kTcOpStages - 1);                     // operand stage
+            const int ss = u & (kTcScaleStages - 1);                 // scale stage
+            if (u >= kTcOpStages && !mbar_wait(&empty[s], ((u / kTcOpStages) - 1) & 1)) fail();
+            if (u >= kTcScaleStages && !mbar_wait(&sempty[ss], ((u / kTcScaleStages) - 1) & 1)) fail();
             if (*(volatile int*)&abort_flag) break;
             // tokens' quants straight into the B tile (asynchronous), then their scalars
             uint8_t* bt = stage_b(s);
@@ -288,40 +330,44 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
                 if (u + 1 < upr) fetch(u + 1);
             }
             if (row_ok) {
-                tc_unpack<T>(kAhead ? cur : q, stage_a(s), r, stage_ws(s));
+                tc_unpack<T>(kAhead ? cur : q, stage_a(s), r, stage_ws(ss));
             } else {
                 for (int kc = 0; kc < 16; ++kc)
                     *reinterpret_cast<uint4*>(stage_a(s) + tile_off(r, kc, 2048)) = make_uint4(0, 0, 0, 0);
-                for (int j = 0; j < 8; ++j) stage_ws(s)[j * kTcM + r] = make_float2(0.0f, 0.0f);
+                for (int j = 0; j < 8; ++j) stage_ws(ss)[j * kTcM + r] = make_float2(0.0f, 0.0f);
             }
             if constexpr (!kAhead) {
                 if (u + 1 < upr) fetch(u + 1);
             }
-            uint8_t* as = stage_as(s);
+            uint8_t* as = stage_as(ss);
 #pragma unroll
             for (int k = 0; k < (kTcN * 8 + NL - 1) / NL; ++k) {
                 const int p = r + k * NL;
                 if (p < kTcN * 8) {
                     const int b = p / kTcN, t = p % kTcN;
                     const float ad = __uint_as_float(hdr[k].x), sq = i2f((int)hdr[k].y + (int)hdr[k].z);
-                    if constexpr (T == kQ4_K)  // per 64-input chunk and token: {d_lo, S_lo, d_hi, S_hi}
-                        *reinterpret_cast<float2*>(as + (((b >> 1) * kTcN + t) * 16 + (b & 1) * 8)) =
-                            make_float2(ad, sq);
-                    else
-                        *reinterpret_cast<float2*>(as + (b * kTcN + t) * 8) = make_float2(ad, sq);
+                    // token pairs side by side for the packed products:
+                    // Q4_K, per 64-input chunk and token pair: {d_lo x2, S_lo x2}, {d_hi x2, S_hi x2};
+                    // Q4_0 / Q8_0, per block and token pair: {d_a x2, sum q x2}
+                    float* af = reinterpret_cast<float*>(as);
+                    const int slot = (T == kQ4_K) ? (((b >> 1) * (kTcN / 2) + (t >> 1)) * 8 + (b & 1) * 4)
+                                                  : ((b * (kTcN / 2) + (t >> 1)) * 4);
+                    af[slot + (t & 1)] = ad;
+                    af[slot + 2 + (t & 1)] = sq;
                 }
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
             fence_async_smem();  // the tensor cores read these tiles through the async proxy
             mbar_arrive(&full[s]);
+            mbar_arrive(&sfull[ss]);
         }
     } else if (warp == kTcMmaWarp) {
         // ---------------- MMA issue (one thread) ----------------
         if (lane == 0) {
             int issued = 0;
             for (int u = 0; u < upr; ++u) {
-                const int s = u & 1, hb = u & 1;
-                if (!mbar_wait(&full[s], (u >> 1) & 1)) fail();
+                const int s = u & (kTcOpStages - 1), hb = u & 1;
+                if (!mbar_wait(&full[s], (u / kTcOpStages) & 1)) fail();
                 if (u >= 2 && !mbar_wait(&acce[hb], ((u >> 1) - 1) & 1)) fail();
                 if (*(volatile int*)&abort_flag) break;
                 tc_fence_after();
@@ -352,15 +398,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
 #pragma unroll
         for (int t = 0; t < TN; ++t) acc[t] = 0.0f;
         for (int u = 0; u < upr; ++u) {
-            const int s = u & 1, hb = u & 1;
-            // accf: this unit's dots are in TMEM; full: the stage's scales are
-            // visible (that phase has completed, and the stage cannot be refilled
-            // before this warp releases it)
-            if (!mbar_wait(&accf[hb], (u >> 1) & 1) || !mbar_wait(&full[s], (u >> 1) & 1)) fail();
+            const int q = u & (kTcScaleStages - 1), hb = u & 1;
+            // accf: this unit's dots are in TMEM; sfull: its scales are written
+            // (the scale stage cannot be refilled before this warp releases it)
+            if (!mbar_wait(&accf[hb], (u >> 1) & 1) || !mbar_wait(&sfull[q], (u / kTcScaleStages) & 1)) fail();
             if (*(volatile int*)&abort_flag) break;
             tc_fence_after();
-            const float2* ws = stage_ws(s);
-            const uint8_t* as = stage_as(s);
+            const float2* ws = stage_ws(q);
+            const uint8_t* as = stage_as(q);
             if constexpr (T == kQ4_K) {
                 // per 64-input chunk c: st = (0 + lo) + hi, a half skipped when its act scale
                 // is 0 (:1546-1618).  Adding such a half instead changes nothing for finite
@@ -373,13 +418,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
                     tmem_ld16(tlane + (uint32_t)((hb * 8 + 2 * c + 1) * kTcN), dh);
                     tmem_wait_ld();
                     const float2 w1 = ws[(2 * c) * kTcM + r], w2 = ws[(2 * c + 1) * kTcM + r];
-                    const float4* a4 = reinterpret_cast<const float4*>(as) + c * kTcN + t0;
+                    const unsigned long long W1X = pk2(w1.x, w1.x), W1Y = pk2(w1.y, w1.y);
+                    const unsigned long long W2X = pk2(w2.x, w2.x), W2Y = pk2(w2.y, w2.y);
+                    const float4* a4 = reinterpret_cast<const float4*>(as) + (c * (kTcN / 2) + t0 / 2) * 2;
 #pragma unroll
-                    for (int t = 0; t < TN; ++t) {
-                        const float4 a = a4[t];  // {d_lo, S_lo, d_hi, S_hi}
-                        const float lo = fmul(a.x, fsub(fmul(w1.x, i2f(dl[t])), fmul(w1.y, a.y)));
-                        const float hi = fmul(a.z, fsub(fmul(w2.x, i2f(dh[t])), fmul(w2.y, a.w)));
-                        acc[t] = fadd(acc[t], fadd(lo, hi));
+                    for (int tp = 0; tp < TN / 2; ++tp) {
+                        const float4 L = a4[2 * tp], H = a4[2 * tp + 1];  // {d x2, S x2} of the lo / hi half
+                        // lo = d_lo * ((d1 * dot_lo) - (dm1 * S_lo)), hi likewise, for two tokens
+                        float p1a, p1b, p2a, p2b, p3a, p3b, p4a, p4b;
+                        upk2(mul2_rn(W1X, pk2(i2f(dl[2 * tp]), i2f(dl[2 * tp + 1]))), p1a, p1b);
+                        upk2(mul2_rn(W1Y, pk2(L.z, L.w)), p2a, p2b);
+                        upk2(mul2_rn(W2X, pk2(i2f(dh[2 * tp]), i2f(dh[2 * tp + 1]))), p3a, p3b);
+                        upk2(mul2_rn(W2Y, pk2(H.z, H.w)), p4a, p4b);
+                        float loa, lob, hia, hib;
+                        upk2(mul2_rn(pk2(L.x, L.y), pk2(fsub(p1a, p2a), fsub(p1b, p2b))), loa, lob);
+                        upk2(mul2_rn(pk2(H.x, H.y), pk2(fsub(p3a, p4a), fsub(p3b, p4b))), hia, hib);
+                        acc[2 * tp] = fadd(acc[2 * tp], fadd(loa, hia));
+                        acc[2 * tp + 1] = fadd(acc[2 * tp + 1], fadd(lob, hib));
                     }
                 }
             } else {
@@ -389,26 +444,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) matbatch_tc_kernel(const uint8_
                     tmem_ld16(tlane + (uint32_t)((hb * 8 + b) * kTcN), dv);
                     tmem_wait_ld();
                     const float wd = ws[b * kTcM + r].x;
-                    const float2* a2 = reinterpret_cast<const float2*>(as) + b * kTcN + t0;
+                    const unsigned long long WD = pk2(wd, wd);
+                    const float4* a4 = reinterpret_cast<const float4*>(as) + b * (kTcN / 2) + t0 / 2;
 #pragma unroll
-                    for (int t = 0; t < TN; ++t) {
-                        const float2 a = a2[t];
-                        float term;
+                    for (int tp = 0; tp < TN / 2; ++tp) {
+                        const float4 a = a4[tp];  // {d_a x2, sum q x2}
+                        int f0 = dv[2 * tp], f1 = dv[2 * tp + 1];
                         if constexpr (T == kQ4_0) {
                             // (float)(dot - 8*sum_q) * (d_w * d_a); a block with d_a == 0 has a zero
                             // dot and sum, so it adds +0 like the reference's skip
-                            const int folded = dv[t] - 8 * __float2int_rn(a.y);
-                            term = fmul(i2f(folded), fmul(wd, a.x));
-                        } else {
-                            term = fmul(i2f(dv[t]), fmul(wd, a.x));
+                            f0 -= 8 * __float2int_rn(a.z);
+                            f1 -= 8 * __float2int_rn(a.w);
                         }
-                        acc[t] = fadd(acc[t], term);
+                        float ta, tb;
+                        upk2(mul2_rn(pk2(i2f(f0), i2f(f1)), mul2_rn(WD, pk2(a.x, a.y))), ta, tb);
+                        acc[2 * tp] = fadd(acc[2 * tp], ta);
+                        acc[2 * tp + 1] = fadd(acc[2 * tp + 1], tb);
                     }
                 }
             }
             tc_fence_before();
             mbar_arrive(&acce[hb]);
-            mbar_arrive(&empty[s]);
+            mbar_arrive(&sempty[q]);
         }
         const int grow = row0 + r;
         if (grow < out_dim && !*(volatile int*)&abort_flag) {
