@@ -30,6 +30,11 @@ struct TokAct {
     }
     __device__ __forceinline__ float d(int j) const { return dd[j]; }
     __device__ __forceinline__ int2 s(int j) const { return ss[j]; }
+    // {d, sum_lo, sum_hi, sum} of block j, as the staged records hold them
+    __device__ __forceinline__ float4 rec(int j) const {
+        const int2 t = ss[j];
+        return make_float4(dd[j], __int_as_float(t.x), __int_as_float(t.y), __int_as_float(t.x + t.y));
+    }
 };
 
 template <int T>

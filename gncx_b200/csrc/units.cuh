@@ -16,7 +16,17 @@
 namespace gncx {
 
 constexpr uint32_t kLo4 = 0x0F0F0F0Fu;
+constexpr uint32_t kHi4 = 0xF0F0F0F0u;
 constexpr uint32_t kHi2 = 0x30303030u;
+
+// dp4a with unsigned bytes in a and signed bytes in b.  With a = q & kHi4
+// (each byte 16 x a high nibble) the sum is exactly 16 x the high-nibble dot,
+// so one arithmetic shift of the sum replaces a shift per word.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
 
 template <int K>
 __device__ __forceinline__ int byte_of(const uint32_t* w) {
@@ -62,19 +72,20 @@ __device__ __forceinline__ float unit_q4_k(const uint32_t (&w)[36], const A& a) 
         dlo = dp4a((int)(q[5] & kLo4), (int)x1.y, dlo);
         dlo = dp4a((int)(q[6] & kLo4), (int)x1.z, dlo);
         dlo = dp4a((int)(q[7] & kLo4), (int)x1.w, dlo);
-        dhi = dp4a((int)((q[0] >> 4) & kLo4), (int)y0.x, dhi);
-        dhi = dp4a((int)((q[1] >> 4) & kLo4), (int)y0.y, dhi);
-        dhi = dp4a((int)((q[2] >> 4) & kLo4), (int)y0.z, dhi);
-        dhi = dp4a((int)((q[3] >> 4) & kLo4), (int)y0.w, dhi);
-        dhi = dp4a((int)((q[4] >> 4) & kLo4), (int)y1.x, dhi);
-        dhi = dp4a((int)((q[5] >> 4) & kLo4), (int)y1.y, dhi);
-        dhi = dp4a((int)((q[6] >> 4) & kLo4), (int)y1.z, dhi);
-        dhi = dp4a((int)((q[7] >> 4) & kLo4), (int)y1.w, dhi);
-        const int2 slo = a.s(2 * c), shi = a.s(2 * c + 1);
+        dhi = dp4a_us(q[0] & kHi4, (int)y0.x, dhi);
+        dhi = dp4a_us(q[1] & kHi4, (int)y0.y, dhi);
+        dhi = dp4a_us(q[2] & kHi4, (int)y0.z, dhi);
+        dhi = dp4a_us(q[3] & kHi4, (int)y0.w, dhi);
+        dhi = dp4a_us(q[4] & kHi4, (int)y1.x, dhi);
+        dhi = dp4a_us(q[5] & kHi4, (int)y1.y, dhi);
+        dhi = dp4a_us(q[6] & kHi4, (int)y1.z, dhi);
+        dhi = dp4a_us(q[7] & kHi4, (int)y1.w, dhi);
+        dhi >>= 4;  // exact: the sum is 16 x the high-nibble dot
+        const float4 rlo = a.rec(2 * c), rhi = a.rec(2 * c + 1);  // {d, sum_lo, sum_hi, sum}
         const float d1 = fmul(d, i2f(s1)), dm1 = fmul(dmin, i2f(m1));
         const float d2 = fmul(d, i2f(s2)), dm2 = fmul(dmin, i2f(m2));
-        const float ulo = fmul(a.d(2 * c), fsub(fmul(d1, i2f(dlo)), fmul(dm1, i2f(slo.x + slo.y))));
-        const float uhi = fmul(a.d(2 * c + 1), fsub(fmul(d2, i2f(dhi)), fmul(dm2, i2f(shi.x + shi.y))));
+        const float ulo = fmul(rlo.x, fsub(fmul(d1, i2f(dlo)), fmul(dm1, i2f(__float_as_int(rlo.w)))));
+        const float uhi = fmul(rhi.x, fsub(fmul(d2, i2f(dhi)), fmul(dm2, i2f(__float_as_int(rhi.w)))));
         total = fadd(total, fadd(ulo, uhi));
     }
     return total;
@@ -185,13 +196,15 @@ __device__ __forceinline__ float q4_0_block(const uint32_t (&w)[36], const A& a)
     dot = dp4a((int)(q1 & kLo4), (int)x0.y, dot);
     dot = dp4a((int)(q2 & kLo4), (int)x0.z, dot);
     dot = dp4a((int)(q3 & kLo4), (int)x0.w, dot);
-    dot = dp4a((int)((q0 >> 4) & kLo4), (int)x1.x, dot);
-    dot = dp4a((int)((q1 >> 4) & kLo4), (int)x1.y, dot);
-    dot = dp4a((int)((q2 >> 4) & kLo4), (int)x1.z, dot);
-    dot = dp4a((int)((q3 >> 4) & kLo4), (int)x1.w, dot);
-    const float ad = a.d(B);
-    const int2 s = a.s(B);
-    const int folded = dot - 8 * (s.x + s.y);
+    int hi = 0;
+    hi = dp4a_us(q0 & kHi4, (int)x1.x, hi);
+    hi = dp4a_us(q1 & kHi4, (int)x1.y, hi);
+    hi = dp4a_us(q2 & kHi4, (int)x1.z, hi);
+    hi = dp4a_us(q3 & kHi4, (int)x1.w, hi);
+    dot += hi >> 4;  // exact: the sum is 16 x the high-nibble dot
+    const float4 r = a.rec(B);  // {d, sum_lo, sum_hi, sum}
+    const float ad = r.x;
+    const int folded = dot - 8 * __float_as_int(r.w);
     return ad == 0.0f ? 0.0f : fmul(i2f(folded), fmul(wd, ad));
 }
 
@@ -221,7 +234,7 @@ __device__ __forceinline__ float q8_0_block(const uint32_t (&w)[68], const A& a)
     dot = dp4a((int)word_at<34 * B + 22>(w), (int)x1.y, dot);
     dot = dp4a((int)word_at<34 * B + 26>(w), (int)x1.z, dot);
     dot = dp4a((int)word_at<34 * B + 30>(w), (int)x1.w, dot);
-    return fmul(i2f(dot), fmul(wd, a.d(B)));
+    return fmul(i2f(dot), fmul(wd, a.rec(B).x));
 }
 
 template <class A>
@@ -241,6 +254,7 @@ struct UnitAct {
     const ActView& a;
     int u;
     __device__ __forceinline__ uint4 chunk(int k) const { return act_chunk(a, u, k); }
+    __device__ __forceinline__ float4 rec(int j) const { return act_rec(a, u * 8 + j); }
     __device__ __forceinline__ float d(int j) const { return act_rec(a, u * 8 + j).x; }
     __device__ __forceinline__ int2 s(int j) const {
         const float4 r = act_rec(a, u * 8 + j);
