@@ -829,6 +829,105 @@ __global__ void __launch_bounds__(kExactThreads) attn_exact_softmax_kernel(const
     for (int t = tid; t < len; t += kExactThreads) sc[t] = fmul(sc[t], inv);
 }
 
+// Exact mode, one query: softmax and PV in one kernel, one CTA per (KV head,
+// kFusedCols output columns).  The CTA stages its columns of every V row of
+// the window in shared memory -- the rows below the query's position before
+// the dependency wait when they come from earlier steps -- then, for each of
+// the group's G heads, the maximum of the scores, e_t = exp(s_t - max), the
+// serial sum of e_t in position order, inv = 1 / (sum + 1e-12), the weights
+// e_t * inv, and thread (head, column) runs out = sum over t in order of
+// weight_t * v_t[d] (csrc/gncx_llm_kernels.cpp:1960-1988).  The same
+// arithmetic as attn_exact_softmax_kernel + attn_exact_pv_kernel, without
+// their round trip through global memory and with V in flight early: every
+// CTA of a KV group repeats the group's softmax (a few microseconds of serial
+// adds, in parallel across CTAs) instead of waiting for it.
+constexpr int kFusedCols = 8;
+constexpr int kFusedThreads = 256;
+
+__host__ __device__ inline size_t attn_exact_fused_smem(int G, int len) {
+    return ((size_t)len * kFusedCols + (size_t)G * ((len + 3) & ~3) + 64) * 4;
+}
+
+__global__ void __launch_bounds__(kFusedThreads) attn_exact_fused_kernel(const AttnArgs a) {
+    extern __shared__ __align__(16) float fsm[];
+    GNCX_TRACE_SCOPE(kTagAttnExactPv, gridDim.x);
+    const int hd = a.hd, G = a.n_heads / a.n_kv;
+    const int ncb = hd / kFusedCols;
+    const int kvh = blockIdx.x / ncb, d0 = (blockIdx.x - kvh * ncb) * kFusedCols;
+    int t0, len;
+    attn_window(a, 0, t0, len);
+    const int lp = (len + 3) & ~3;
+    float* vsl = fsm;                                // [len][kFusedCols]
+    float* es = vsl + (size_t)len * kFusedCols;      // [G][lp]: scores, then e, then weights
+    float* red = es + (size_t)G * lp;                // [G] max, [G] inv
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const size_t ps = (size_t)a.kv_pos_stride;
+    const float* vbase = a.vc + (size_t)t0 * ps + (size_t)kvh * a.kv_head_stride + d0;
+    constexpr int kPieces = kFusedCols / 4;  // 16-byte pieces per row
+    auto stage_v = [&](int ta, int tb) {
+        for (int i = tid; i < (tb - ta) * kPieces; i += kFusedThreads) {
+            const int t = ta + i / kPieces, c = i % kPieces;
+            cp_async16(vsl + (size_t)t * kFusedCols + 4 * c, vbase + (size_t)t * ps + 4 * c);
+        }
+        cp_async_commit();
+    };
+    // rows below the query's own were written before the preceding kernel ran
+    const int n_old = a.prefetch_old ? len - 1 : 0;
+    if (n_old > 0) stage_v(0, n_old);
+    pdl_launch_dependents();
+    pdl_wait();
+    stage_v(n_old, len);
+    const float* sc = a.scores + (size_t)(kvh * G) * a.score_cap;
+    for (int i = tid; i < G * len; i += kFusedThreads) {
+        const int g = i / len, t = i - g * len;
+        es[(size_t)g * lp + t] = sc[(size_t)g * a.score_cap + t];
+    }
+    __syncthreads();
+    // maxima: warp w takes heads w, w + 8, ...
+    for (int g = warp; g < G; g += kFusedThreads / 32) {
+        float mx = -1e30f;
+        for (int t = lane; t < len; t += 32) mx = fmaxf(mx, es[(size_t)g * lp + t]);
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) red[g] = mx;
+    }
+    __syncthreads();
+    for (int i = tid; i < G * len; i += kFusedThreads) {
+        const int g = i / len, t = i - g * len;
+        es[(size_t)g * lp + t] = exp_cr(fsub(es[(size_t)g * lp + t], red[g]));
+    }
+    __syncthreads();
+    // the serial sum of each head, one thread per head
+    if (tid < G) {
+        const float* e = es + (size_t)tid * lp;
+        float sum = 0.0f;
+        const float4* e4 = reinterpret_cast<const float4*>(e);
+        const int n4 = len >> 2;
+#pragma unroll 8
+        for (int i = 0; i < n4; ++i) {
+            const float4 v = e4[i];
+            sum = fadd(fadd(fadd(fadd(sum, v.x), v.y), v.z), v.w);
+        }
+        for (int t = n4 * 4; t < len; ++t) sum = fadd(sum, e[t]);
+        red[G + tid] = fdiv(1.0f, fadd(sum, 1e-12f));
+    }
+    __syncthreads();
+    for (int i = tid; i < G * len; i += kFusedThreads) {
+        const int g = i / len, t = i - g * len;
+        es[(size_t)g * lp + t] = fmul(es[(size_t)g * lp + t], red[G + g]);
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    // thread (head g, column c): the serial weighted sum over the window
+    if (tid < G * kFusedCols) {
+        const int g = tid / kFusedCols, c = tid - g * kFusedCols;
+        const float* w = es + (size_t)g * lp;
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int t = 0; t < len; ++t) acc = fadd(acc, fmul(w[t], vsl[(size_t)t * kFusedCols + c]));
+        a.out[(size_t)(kvh * G + g) * hd + d0 + c] = acc;
+    }
+}
+
 // out[h][d] = sum over t (serial) of p_t * v_t[d].  One CTA per (KV head,
 // group of up to 8 query heads, slice of kExactSlice output columns, query);
 // thread (g, d) runs one chain.  V rows and p stream through double-buffered
@@ -987,6 +1086,24 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
         if (!a.out) return kErrInvalidArg;
         e = vec ? launch_partial<true, true>(a, grid, smem, st) : launch_partial<false, true>(a, grid, smem, st);
         if (e != cudaSuccess) return kErrCuda;
+        // one query whose window's V columns fit a CTA's shared memory: softmax
+        // and PV fused (the output in fp32 only; no re-quantized act)
+        int len1 = 0;
+        if (n_tok == 1 && !a.pos_dev) {
+            const int t0 = a.window > 0 ? (a.pos0 - a.window + 1 > 0 ? a.pos0 - a.window + 1 : 0) : 0;
+            len1 = a.pos0 + 1 - t0;
+        } else if (n_tok == 1) {
+            len1 = a.score_cap;  // upper bound: the position is read on the device
+        }
+        const size_t fsm = attn_exact_fused_smem(G, len1);
+        if (n_tok == 1 && vec && !act && a.hd % kFusedCols == 0 && G * kFusedCols <= kFusedThreads && len1 > 0 &&
+            fsm <= (size_t)dev.max_smem_optin && !getenv("GNCX_EXACT_UNFUSED")) {
+            if (set_smem_limit(attn_exact_fused_kernel, fsm) != cudaSuccess) return kErrCuda;
+            return launch_k(attn_exact_fused_kernel, dim3(a.n_kv * (a.hd / kFusedCols)), dim3(kFusedThreads), fsm, st,
+                            a) == cudaSuccess
+                       ? kOk
+                       : kErrCuda;
+        }
         if (launch_k(attn_exact_softmax_kernel, dim3(a.n_heads, n_tok), dim3(kExactThreads), 0, st, a) != cudaSuccess)
             return kErrCuda;
         const int slices = (a.hd + kExactSlice - 1) / kExactSlice;

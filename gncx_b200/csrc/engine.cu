@@ -410,9 +410,12 @@ static int decode_step(Engine* e, bool sample, double penalty) {
             a.out_stride = QD;
             a.act_out = ActOut{nullptr, nullptr};
         } else {
-            a.out = e->exact ? e->qkv : nullptr;  // exact mode: the output replaces q
+            // exact mode: the fp32 output replaces q and the O GEMV quantizes it
+            // (the fused softmax + PV kernel writes no act); split-KV: the
+            // combine writes the act only
+            a.out = e->exact ? e->qkv : nullptr;
             a.out_stride = qkv_w;
-            a.act_out = ActOut{nullptr, e->act_q};
+            a.act_out = e->exact ? ActOut{nullptr, nullptr} : ActOut{nullptr, e->act_q};
         }
         a.prefetch_old = 1;  // cache rows below pos come from earlier tokens
         a.err = e->d_err;
@@ -431,6 +434,8 @@ static int decode_step(Engine* e, bool sample, double penalty) {
         } else if (tp) {  // gather the heads, then the whole attn_output on every rank
             CK(gather_row(e, kLlAttn));
             CK(gemv_norm(e, w.wo, w.to, nullptr, gq, QD, e->proj, w.ffn_norm));
+        } else if (e->exact) {
+            CK(gemv_norm(e, w.wo, w.to, nullptr, e->qkv, QD, e->proj, w.ffn_norm));
         } else {
             CK(gemv_norm(e, w.wo, w.to, e->act_q, nullptr, QD, e->proj, w.ffn_norm));
         }
