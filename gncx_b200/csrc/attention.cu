@@ -551,14 +551,17 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     for (int i = 0; i < kPvHeads; ++i) acc[i] = 0.0f;
     const float scale = a.scale;
     for (int j = j0; j < j1; ++j) {
+        if (tid == 0) GNCX_TRACE_MARK(50, j - j0);
         if (j + 1 < j1) cp_async_wait<1>(); else cp_async_wait<0>();
         __syncthreads();  // chunk j landed for every thread; qs / stats written
+        if (tid == 0) GNCX_TRACE_MARK(51, j - j0);
         const int c0 = j * kStreamChunk;
         const int cn = min(kStreamChunk, len - c0);
         const float* ks = kb + (size_t)(j & 1) * kStreamChunk * hd;
         const float* vs = vb + (size_t)(j & 1) * kStreamChunk * hd;
         chunk_scores_warp(ks, hd, qs, qrs, G, cn, NW, [&](int g, int pp, float dot) { sc[g * sld + pp] = fmul(dot, scale); });
         __syncthreads();
+        if (tid == 0) GNCX_TRACE_MARK(52, j - j0);
         for (int g = warp; g < G; g += NW) {
             float mx = -INFINITY;
             for (int pp = lane; pp < cn; pp += 32) mx = fmaxf(mx, sc[g * sld + pp]);
@@ -582,6 +585,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
         for (int i = tid; i < cn * (G4 - G); i += kStreamThreads)
             es[(size_t)(i / (G4 - G)) * G4 + G + i % (G4 - G)] = 0.0f;
         __syncthreads();
+        if (tid == 0) GNCX_TRACE_MARK(53, j - j0);
         if (pg < npg) {
 #pragma unroll
             for (int i = 0; i < kPvHeads; ++i)
@@ -589,6 +593,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
             chunk_pv(vs, hd, es, G4, 0, G, cn, d, pg, npg, acc);
         }
         __syncthreads();  // buffer j & 1 is free again
+        if (tid == 0) GNCX_TRACE_MARK(54, j - j0);
         if (j + 2 < j1) issue(j + 2);
     }
     // sum the position groups' partial outputs (through the K buffers) and
@@ -782,6 +787,286 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_prefill_kernel(const Att
             for (int y = 0; y < DJ; ++y) rec[4 + DJ * j + y] = acc[x][y];
             if (j == 0) { rec[0] = red[2 * qr]; rec[1] = red[2 * qr + 1]; }
         }
+    }
+}
+
+// ---- one query over a long window: rows streamed through registers ----
+// Each warp walks batches of B positions of one KV head; lane l holds columns
+// [l*DPL, l*DPL + DPL) of the G query heads, of the running outputs, and of
+// the K and V rows it loads (one coalesced vector load per row and lane,
+// straight into registers: no shared-memory staging and no CTA barrier per
+// batch).  The B*G partial dot products of a batch are summed across the warp
+// by a reduce-scatter butterfly that leaves lane l with the total of
+// (position, head) pair l >> SH; the online softmax (running maximum m, sum l
+// of e^(s - m), outputs rescaled by e^(m_old - m_new)) runs on those lanes,
+// and the batch's weights reach every lane through a per-warp shared-memory
+// row.  After its range, the CTA merges its warps' states and writes one
+// record {m, l, -, -, o[hd]} per head, in the split-KV partial kernel's
+// format, for the combine kernel.  Split-KV softmax mode (sums in a different
+// order from the reference's serial ones; outputs within ~1e-6 relative).
+// Many warps per SM, each with a whole batch of rows in flight, keep HBM busy
+// where the chunked kernels' per-chunk barriers and phases left it idle.
+constexpr int kRowsThreads = 256;
+constexpr int kRowsWarps = kRowsThreads / 32;
+constexpr int kRowsMaxKv = 256;     // KV heads the in-kernel merge counts arrivals for
+constexpr int kRowsMaxParts = 256;  // CTAs per KV head the in-kernel merge takes
+
+// Arrivals per KV head of the CTAs of one attn_rows_kernel launch, for the
+// in-kernel merge: zero when the module loads, and atomicInc wraps each back
+// to zero at the launch's last arrival.
+__device__ unsigned int g_rows_arrive[kRowsMaxKv];
+
+template <int DPL>
+__device__ __forceinline__ void rows_load(const float* p, float (&r)[DPL]) {
+    if constexpr (DPL == 4) {
+        const float4 v = __ldcs(reinterpret_cast<const float4*>(p));
+        r[0] = v.x; r[1] = v.y; r[2] = v.z; r[3] = v.w;
+    } else {
+        const float2 v = __ldcs(reinterpret_cast<const float2*>(p));
+        r[0] = v.x; r[1] = v.y;
+    }
+}
+
+// One batch of B rows of a warp (loaded in kr / vr): scores, the online
+// softmax update, the weighted V sum.  Lane l ends the butterfly with pair
+// l >> SH = (position p, head g) = (my / G, my % G); m and l belong to that head.
+template <int DPL, int G, int B>
+__device__ __forceinline__ void rows_batch(const float (&q)[G][DPL], float (&o)[G][DPL], const float (&kr)[B][DPL],
+                                           const float (&vr)[B][DPL], int n_valid, float scale, float& m, float& l,
+                                           float* wsh, int lane) {
+    constexpr int NV = B * G;
+    constexpr int LNV = NV == 1 ? 0 : NV == 2 ? 1 : NV == 4 ? 2 : NV == 8 ? 3 : NV == 16 ? 4 : 5;
+    constexpr int SH = 5 - LNV;
+    constexpr int LG = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3;
+    const int my = lane >> SH;
+    float v[NV];
+#pragma unroll
+    for (int p = 0; p < B; ++p)
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float c = 0.0f;
+#pragma unroll
+            for (int k = 0; k < DPL; ++k) c = fmaf(q[g][k], kr[p][k], c);
+            v[p * G + g] = c;
+        }
+    // reduce-scatter: at offset o, lanes with bit o set keep the upper half
+#pragma unroll
+    for (int n = NV, lvl = 0; n > 1; n >>= 1, ++lvl) {
+        const int off = 16 >> lvl;
+        const bool up = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+            const float send = up ? v[i] : v[i + n / 2];
+            const float keep = up ? v[i + n / 2] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+    }
+    float sc = v[0];
+#pragma unroll
+    for (int off = (1 << SH) >> 1; off > 0; off >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
+    sc = my / G < n_valid ? sc * scale : -INFINITY;
+    // the head's maximum and sum over the batch: lanes whose pairs differ in position
+    float bm = sc;
+#pragma unroll
+    for (int off = 16; off >= (1 << (SH + LG)); off >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, off));
+    const float m_new = fmaxf(m, bm);
+    const float e = __expf(sc - m_new);
+    const float corr = __expf(m - m_new);  // 0 while m = -inf
+    float bs = e;
+#pragma unroll
+    for (int off = 16; off >= (1 << (SH + LG)); off >>= 1) bs += __shfl_xor_sync(0xffffffffu, bs, off);
+    l = fmaf(l, corr, bs);
+    m = m_new;
+    if ((lane & ((1 << SH) - 1)) == 0) wsh[my] = e;
+    if (lane < (G << SH) && (lane & ((1 << SH) - 1)) == 0) wsh[32 + my] = corr;
+    __syncwarp();
+    float w[NV], cg[G];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) w[i] = wsh[i];
+#pragma unroll
+    for (int g = 0; g < G; ++g) cg[g] = wsh[32 + g];
+    __syncwarp();  // wsh is rewritten by the next batch
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) {
+            float acc = o[g][k] * cg[g];
+#pragma unroll
+            for (int p = 0; p < B; ++p) acc = fmaf(w[p * G + g], vr[p][k], acc);
+            o[g][k] = acc;
+        }
+}
+
+// PF: the next batch's rows are loaded before the current one is computed
+// (two batches of registers in flight per warp).
+template <int DPL, int G, int B, bool PF, bool MERGE>
+__global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnArgs a, int ppc) {
+    constexpr int HD = DPL * 32;
+    constexpr int NV = B * G;  // (position, head) pairs per batch
+    static_assert(NV >= 1 && NV <= 32 && (NV & (NV - 1)) == 0, "pairs per batch: a power of two up to 32");
+    constexpr int LNV = NV == 1 ? 0 : NV == 2 ? 1 : NV == 4 ? 2 : NV == 8 ? 3 : NV == 16 ? 4 : 5;
+    constexpr int SH = 5 - LNV;
+    __shared__ __align__(16) float wsh[kRowsWarps][32 + G];   // a batch's weights, then the heads' corrections
+    __shared__ float mst[kRowsWarps][G], lst[kRowsWarps][G];
+    __shared__ __align__(16) float ost[kRowsWarps][G][HD];
+    GNCX_TRACE_SCOPE(kTagAttnPartial, gridDim.x);
+    pdl_launch_dependents();
+    pdl_wait();
+    const int part = blockIdx.x, kvh = blockIdx.y;
+    int t0, len;
+    attn_window(a, 0, t0, len);
+    const int p0 = part * ppc, p1 = min(len, p0 + ppc);
+    if (p0 >= p1) return;  // uniform per CTA; the launch has none (parts = ceil(len / ppc))
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const size_t ps = (size_t)a.kv_pos_stride;
+    const float* kbase = a.kc + (size_t)t0 * ps + (size_t)kvh * a.kv_head_stride + lane * DPL;
+    const float* vbase = a.vc + (size_t)t0 * ps + (size_t)kvh * a.kv_head_stride + lane * DPL;
+    float q[G][DPL], o[G][DPL];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        rows_load<DPL>(a.q + (size_t)(kvh * G + g) * HD + lane * DPL, q[g]);
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) o[g][k] = 0.0f;
+    }
+    float m = -INFINITY, l = 0.0f;
+    const float scale = a.scale;
+    // rows past the range load a valid row and get weight 0
+    auto load = [&](int b0, float (&kr)[B][DPL], float (&vr)[B][DPL]) {
+#pragma unroll
+        for (int p = 0; p < B; ++p) rows_load<DPL>(kbase + (size_t)min(b0 + p, p1 - 1) * ps, kr[p]);
+#pragma unroll
+        for (int p = 0; p < B; ++p) rows_load<DPL>(vbase + (size_t)min(b0 + p, p1 - 1) * ps, vr[p]);
+    };
+    constexpr int kStep = kRowsWarps * B;
+    int b0 = p0 + warp * B;
+    if constexpr (PF) {
+        float ka[B][DPL], va[B][DPL], kb[B][DPL], vb[B][DPL];
+        if (b0 < p1) load(b0, ka, va);
+        while (b0 < p1) {
+            if (b0 + kStep < p1) load(b0 + kStep, kb, vb);
+            rows_batch<DPL, G, B>(q, o, ka, va, p1 - b0, scale, m, l, wsh[warp], lane);
+            b0 += kStep;
+            if (b0 >= p1) break;
+            if (b0 + kStep < p1) load(b0 + kStep, ka, va);
+            rows_batch<DPL, G, B>(q, o, kb, vb, p1 - b0, scale, m, l, wsh[warp], lane);
+            b0 += kStep;
+        }
+    } else {
+        for (; b0 < p1; b0 += kStep) {
+            float kr[B][DPL], vr[B][DPL];
+            load(b0, kr, vr);
+            rows_batch<DPL, G, B>(q, o, kr, vr, p1 - b0, scale, m, l, wsh[warp], lane);
+        }
+    }
+    // merge the warps' states: lanes 0, 1 << SH, ... (G << SH) - 1 hold head g's m and l
+    if (lane < (G << SH) && (lane & ((1 << SH) - 1)) == 0) {
+        mst[warp][lane >> SH] = m;
+        lst[warp][lane >> SH] = l;
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) ost[warp][g][lane * DPL + k] = o[g][k];
+    __syncthreads();
+    const size_t R = attn_record_floats(HD);
+    for (int t = threadIdx.x; t < G * HD; t += kRowsThreads) {
+        const int g = t / HD, d = t - g * HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kRowsWarps; ++w) M = fmaxf(M, mst[w][g]);
+        float L = 0.0f, O = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kRowsWarps; ++w) {
+            const float f = __expf(mst[w][g] - M);  // 0 for warps with no rows (m = -inf)
+            L = fmaf(lst[w][g], f, L);
+            O = fmaf(ost[w][g][d], f, O);
+        }
+        float* rec = a.part + ((size_t)(kvh * G + g) * a.max_splits + part) * R;
+        rec[4 + d] = O;
+        if (d == 0) { rec[0] = M; rec[1] = L; }
+    }
+    if constexpr (MERGE) {
+        // the last CTA of this KV head to finish merges its heads' records:
+        // out = sum_r o_r e^(m_r - M) / (sum_r l_r e^(m_r - M) + 1e-12), in one
+        // pass per output pair of columns with a running maximum
+        __shared__ int s_last;
+        __syncthreads();  // this CTA's records are written
+        if (threadIdx.x == 0) {
+            __threadfence();
+            s_last = atomicInc(&g_rows_arrive[kvh], gridDim.x - 1) == gridDim.x - 1;
+        }
+        __syncthreads();
+        if (!s_last) return;  // uniform per CTA
+        __threadfence();
+        const int n = gridDim.x;
+        constexpr int kRb = 16;  // records in flight per thread
+        for (int t = threadIdx.x; t < G * HD / 2; t += kRowsThreads) {
+            const int g = t / (HD / 2), d = 2 * (t - g * (HD / 2));
+            const float* r0 = a.part + (size_t)(kvh * G + g) * a.max_splits * R;
+            float M = -INFINITY, L = 0.0f, O0 = 0.0f, O1 = 0.0f;
+            for (int rb = 0; rb < n; rb += kRb) {
+                float2 ml[kRb], ov[kRb];
+#pragma unroll
+                for (int b = 0; b < kRb; ++b) {
+                    const int r = min(rb + b, n - 1);
+                    ml[b] = __ldcg(reinterpret_cast<const float2*>(r0 + (size_t)r * R));
+                    ov[b] = __ldcg(reinterpret_cast<const float2*>(r0 + (size_t)r * R + 4 + d));
+                }
+                float bm = M;
+#pragma unroll
+                for (int b = 0; b < kRb; ++b) bm = fmaxf(bm, ml[b].x);
+                const float c = __expf(M - bm);  // 0 on the first batch
+                L *= c; O0 *= c; O1 *= c;
+#pragma unroll
+                for (int b = 0; b < kRb; ++b) {
+                    const float w = rb + b < n ? __expf(ml[b].x - bm) : 0.0f;
+                    L = fmaf(ml[b].y, w, L);
+                    O0 = fmaf(ov[b].x, w, O0);
+                    O1 = fmaf(ov[b].y, w, O1);
+                }
+                M = bm;
+            }
+            const float inv = 1.0f / (L + 1e-12f);
+            *reinterpret_cast<float2*>(a.out + (size_t)(kvh * G + g) * HD + d) = make_float2(O0 * inv, O1 * inv);
+        }
+    }
+}
+
+template <int DPL, int G, bool MERGE>
+static cudaError_t launch_rows_g(const AttnArgs& a, dim3 grid, int ppc, int B, cudaStream_t st) {
+    constexpr int BMAX = 32 / G < 8 ? 32 / G : 8;
+    constexpr int BPF = BMAX >= 4 ? 4 : BMAX;
+    constexpr int BPP = G >= 8 ? 2 : BPF;  // two batches of registers in flight
+    if (B < 0) return launch_k(attn_rows_kernel<DPL, G, BPP, true, MERGE>, grid, dim3(kRowsThreads), 0, st, a, ppc);
+    if (B >= BMAX)
+        return launch_k(attn_rows_kernel<DPL, G, BMAX, false, MERGE>, grid, dim3(kRowsThreads), 0, st, a, ppc);
+    return launch_k(attn_rows_kernel<DPL, G, BPF, false, MERGE>, grid, dim3(kRowsThreads), 0, st, a, ppc);
+}
+
+// head_dim 64 or 128, G in {1, 2, 4, 8}
+static bool rows_ok(const AttnArgs& a) {
+    const int G = a.n_heads / a.n_kv;
+    return (a.hd == 128 || a.hd == 64) && (G == 1 || G == 2 || G == 4 || G == 8) &&
+           (((uintptr_t)a.kc | (uintptr_t)a.vc | (uintptr_t)a.q) & (a.hd == 128 ? 15 : 7)) == 0 &&
+           a.kv_pos_stride % (a.hd / 32) == 0 && a.kv_head_stride % (a.hd / 32) == 0;
+}
+
+template <bool MERGE>
+static cudaError_t launch_rows(const AttnArgs& a, dim3 grid, int ppc, int B, cudaStream_t st) {
+    const int G = a.n_heads / a.n_kv;
+    if (a.hd == 128) {
+        switch (G) {
+            case 1: return launch_rows_g<4, 1, MERGE>(a, grid, ppc, B, st);
+            case 2: return launch_rows_g<4, 2, MERGE>(a, grid, ppc, B, st);
+            case 4: return launch_rows_g<4, 4, MERGE>(a, grid, ppc, B, st);
+            default: return launch_rows_g<4, 8, MERGE>(a, grid, ppc, B, st);
+        }
+    }
+    switch (G) {
+        case 1: return launch_rows_g<2, 1, MERGE>(a, grid, ppc, B, st);
+        case 2: return launch_rows_g<2, 2, MERGE>(a, grid, ppc, B, st);
+        case 4: return launch_rows_g<2, 4, MERGE>(a, grid, ppc, B, st);
+        default: return launch_rows_g<2, 8, MERGE>(a, grid, ppc, B, st);
     }
 }
 
@@ -1116,6 +1401,36 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
         return kOk;  // the PV kernel also wrote act_out
     }
     const int Gq = a.n_heads / a.n_kv;
+    // One query, window known on the host (the drop-in step): rows streamed
+    // through registers, ~2 CTAs per SM, each a range of positions of one KV head
+    static const bool no_rows = getenv("GNCX_ATTN_NO_ROWS") != nullptr;  // tuning overrides
+    static const int rows_b = getenv("GNCX_ATTN_ROWS_B") ? atoi(getenv("GNCX_ATTN_ROWS_B")) : 8;
+    static const int rows_ctas = getenv("GNCX_ATTN_ROWS_CTAS") ? atoi(getenv("GNCX_ATTN_ROWS_CTAS")) : 2;
+    static const bool no_rows_merge = getenv("GNCX_ATTN_NO_ROWS_MERGE") != nullptr;
+    bool rows = false, rows_merge = false;
+    AttnArgs ra = a;
+    dim3 rgrid;
+    int rppc = 0;
+    if (!no_rows && n_tok == 1 && !a.post_k && !a.pos_dev && rows_ok(a)) {
+        const int t0r = a.window > 0 ? (a.pos0 - a.window + 1 > 0 ? a.pos0 - a.window + 1 : 0) : 0;
+        const int lenr = a.pos0 + 1 - t0r;
+        int parts = (rows_ctas > 0 ? rows_ctas : 2) * dev.sm_count / a.n_kv;
+        if (parts < 1) parts = 1;
+        int ppc = (lenr + parts - 1) / parts;
+        const int gran = ppc >= kRowsWarps * 8 ? kRowsWarps * 8 : 8;  // whole batches for every warp
+        ppc = (ppc + gran - 1) / gran * gran;
+        parts = (lenr + ppc - 1) / ppc;
+        if (parts <= a.max_splits) {  // one record per CTA fits the caller's record space
+            rows = true;
+            rgrid = dim3(parts, a.n_kv, 1);
+            ra.chunk = ppc;  // the merge's "split": one CTA's range of positions
+            rppc = ppc;
+            // the last CTA of each KV head merges (no combine kernel) when the
+            // output is fp32 only
+            rows_merge = !no_rows_merge && a.out && ((uintptr_t)a.out & 7) == 0 && !act && a.n_kv <= kRowsMaxKv &&
+                         parts <= kRowsMaxParts;
+        }
+    }
     // One query over a long window (the drop-in step at thousands of
     // positions): the streaming kernel, one CTA per (range of chunks, KV head),
     // kStreamCtasPerSm resident per SM, when there are at least two chunks per CTA.
@@ -1124,7 +1439,7 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
     dim3 sgrid;
     int cpp = 0;
     size_t ssm = 0;
-    if (n_tok == 1 && !a.post_k && vec && a.hd % 8 == 0 && a.hd <= 128 && (kStreamThreads % a.hd) == 0 &&
+    if (!rows && n_tok == 1 && !a.post_k && vec && a.hd % 8 == 0 && a.hd <= 128 && (kStreamThreads % a.hd) == 0 &&
         (Gq == 1 || Gq == 2 || Gq == 4) && !getenv("GNCX_ATTN_NO_STREAM")) {
         int t0s, lens;
         if (a.pos_dev) {
@@ -1164,13 +1479,16 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
             if (set_smem_limit(attn_prefill_kernel<64>, psm) != cudaSuccess) return kErrCuda;
             e = launch_k(attn_prefill_kernel<64>, pgrid, dim3(kAttnThreads), psm, st, b);
         }
+    } else if (rows) {
+        if (rows_merge) return launch_rows<true>(ra, rgrid, rppc, rows_b, st) == cudaSuccess ? kOk : kErrCuda;
+        e = launch_rows<false>(ra, rgrid, rppc, rows_b, st);
     } else if (stream) {
         e = launch_k(attn_stream_kernel, sgrid, dim3(kStreamThreads), ssm, st, sa, cpp);
     } else {
         e = vec ? launch_partial<true, false>(a, grid, smem, st) : launch_partial<false, false>(a, grid, smem, st);
     }
     if (e != cudaSuccess) return kErrCuda;
-    const AttnArgs& ca = stream ? sa : a;
+    const AttnArgs& ca = rows ? ra : stream ? sa : a;
     const size_t csm = (size_t)ca.max_splits * 8 + kCombineThreads * 4;
     if (set_smem_limit(attn_combine_kernel, csm) != cudaSuccess) return kErrCuda;
     return launch_k(attn_combine_kernel, dim3(a.n_heads, n_tok), dim3(kCombineThreads), csm, st, ca) == cudaSuccess

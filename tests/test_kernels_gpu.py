@@ -308,7 +308,7 @@ def test_attention_config(gpu, oracle, ctx, window):
     assert np.array_equal(host(kc)[(ctx - 1) * nkv * hd:], kc_ref[(ctx - 1) * nkv * hd:])
 
 
-@pytest.mark.parametrize("nh,nkv,hd", [(4, 2, 64), (8, 1, 128), (16, 8, 64), (32, 8, 128)])
+@pytest.mark.parametrize("nh,nkv,hd", [(4, 2, 64), (8, 1, 128), (16, 8, 64), (32, 8, 128), (8, 8, 128), (8, 2, 64)])
 @pytest.mark.parametrize("exact", [0, 1])
 def test_attention_lengths(gpu, oracle, nh, nkv, hd, exact):
     """Every context length up to 70 and the chunk edges around 128 / 1024,
