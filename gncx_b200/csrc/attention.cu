@@ -930,6 +930,20 @@ __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnAr
     }
     float m = -INFINITY, l = 0.0f;
     const float scale = a.scale;
+    // the query's own rows, when given, come from new_k / new_v: the warp whose
+    // batch holds that position stores them in the cache before its loads, and
+    // each lane later reads back only what it stored itself (program order)
+    const int last = len - 1;
+    if (a.new_k && last >= p0 && last < p1 && warp == ((last - p0) / B) % kRowsWarps) {
+        float r[DPL];
+        const size_t at = (size_t)last * ps;
+        rows_load<DPL>(a.new_k + (size_t)kvh * HD + lane * DPL, r);
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) const_cast<float*>(kbase)[at + k] = r[k];
+        rows_load<DPL>(a.new_v + (size_t)kvh * HD + lane * DPL, r);
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) const_cast<float*>(vbase)[at + k] = r[k];
+    }
     // rows past the range load a valid row and get weight 0
     auto load = [&](int b0, float (&kr)[B][DPL], float (&vr)[B][DPL]) {
 #pragma unroll
@@ -1347,6 +1361,21 @@ bool attention_shape_ok(int32_t n_heads, int32_t n_kv, int32_t hd) {
     return n_heads > 0 && n_kv > 0 && hd > 0 && n_heads % n_kv == 0 && hd <= kMaxHeadDim && (hd & 3) == 0;
 }
 
+// The query's new K/V rows into the cache at its position (paths whose
+// kernels read that position from the cache).
+static cudaError_t store_new_rows(const AttnArgs& a, cudaStream_t st) {
+    const size_t row = (size_t)a.hd * 4;
+    float* kd = const_cast<float*>(a.kc) + (size_t)a.pos0 * a.kv_pos_stride;
+    float* vd = const_cast<float*>(a.vc) + (size_t)a.pos0 * a.kv_pos_stride;
+    if (a.kv_head_stride == a.hd) {  // the heads of a position are one contiguous row
+        const cudaError_t e = cudaMemcpyAsync(kd, a.new_k, a.n_kv * row, cudaMemcpyDefault, st);
+        return e != cudaSuccess ? e : cudaMemcpyAsync(vd, a.new_v, a.n_kv * row, cudaMemcpyDefault, st);
+    }
+    const size_t pitch = (size_t)a.kv_head_stride * 4;
+    const cudaError_t e = cudaMemcpy2DAsync(kd, pitch, a.new_k, row, row, a.n_kv, cudaMemcpyDefault, st);
+    return e != cudaSuccess ? e : cudaMemcpy2DAsync(vd, pitch, a.new_v, row, row, a.n_kv, cudaMemcpyDefault, st);
+}
+
 int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
     const AttnArgs& a = args;
     if (!a.q || !a.kc || !a.vc || !a.part || a.n_heads <= 0 || a.n_kv <= 0 || a.hd <= 0 || n_tok <= 0)
@@ -1356,6 +1385,7 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
     const bool act = a.act_out.blocks || a.act_out.staged;
     if (act && a.hd % 32) return kErrInvalidArg;
     if (a.post_k && (n_tok != 1 || !a.post_v || !a.rope_c || !a.rope_s || (a.hd & 1))) return kErrInvalidArg;
+    if (a.new_k && (n_tok != 1 || !a.new_v || a.pos_dev || a.post_k)) return kErrInvalidArg;
     if (a.act_out.staged && (n_tok != 1 || (a.n_heads * a.hd) % 256 || ((uintptr_t)a.act_out.staged & 15)))
         return kErrInvalidArg;
     const DeviceInfo& dev = device_info();
@@ -1369,6 +1399,7 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
     if (a.exact) {
         if (!a.scores || a.score_cap < a.max_splits * a.chunk || (a.score_cap & 3)) return kErrCapacity;
         if (!a.out) return kErrInvalidArg;
+        if (a.new_k && store_new_rows(a, st) != cudaSuccess) return kErrCuda;
         e = vec ? launch_partial<true, true>(a, grid, smem, st) : launch_partial<false, true>(a, grid, smem, st);
         if (e != cudaSuccess) return kErrCuda;
         // one query whose window's V columns fit a CTA's shared memory: softmax
@@ -1429,6 +1460,16 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
             // output is fp32 only
             rows_merge = !no_rows_merge && a.out && ((uintptr_t)a.out & 7) == 0 && !act && a.n_kv <= kRowsMaxKv &&
                          parts <= kRowsMaxParts;
+        }
+    }
+    // the register-streaming kernel reads the new rows in place (vector loads)
+    // and stores them; every other path finds them in the cache
+    if (a.new_k) {
+        const bool in_kernel =
+            rows && (((uintptr_t)a.new_k | (uintptr_t)a.new_v) & (a.hd == 128 ? 15 : 7)) == 0;
+        if (!in_kernel) {
+            if (store_new_rows(a, st) != cudaSuccess) return kErrCuda;
+            ra.new_k = ra.new_v = nullptr;
         }
     }
     // One query over a long window (the drop-in step at thousands of
@@ -1504,7 +1545,8 @@ int32_t attention_scratch_records(int32_t pos, int32_t n_heads, int32_t window) 
 
 int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t n_heads, int32_t n_kv,
                      int32_t head_dim, float scale, int32_t window, float* out, const AttnScratch& scratch,
-                     int32_t* err, cudaStream_t st, float* exact_scores) {
+                     int32_t* err, cudaStream_t st, float* exact_scores, const float* new_k,
+                     const float* new_v) {
     if (!q || !kc || !vc || !out || pos < 0 || n_heads <= 0 || n_kv <= 0 || head_dim <= 0) return kErrInvalidArg;
     const int32_t t0 = window > 0 ? (pos - window + 1 > 0 ? pos - window + 1 : 0) : 0;
     const int32_t len = pos + 1 - t0;
@@ -1534,6 +1576,8 @@ int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t 
     a.scores = exact_scores;
     a.score_cap = a.max_splits * a.chunk;
     a.prefetch_old = 0;  // a caller's kernel just before may have written any row
+    a.new_k = new_k;
+    a.new_v = new_v;
     return attention_run(a, 1, st);
 }
 

@@ -212,6 +212,17 @@ static int32_t finish(int32_t st, bool force_sync = false) {
 #define GNCX_BEGIN()                      \
     if (ensure_init() != kOk) return;     \
     (void)0
+// True when the GPU can read p (device, managed or mapped pinned memory); no error recorded.
+static bool dev_accessible(const void* p) {
+    cudaPointerAttributes a;
+    if (!p || cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged ||
+           (a.type == cudaMemoryTypeHost && a.devicePointer == p);
+}
+
 #define GNCX_CHECK(p)                                \
     if (check_dev((p), #p) != kOk) return;           \
     (void)0
@@ -669,11 +680,18 @@ void gncx_mqa_attention_step_ext(const float* q_vec, const float* k_vec, const f
         return;
     }
     const size_t kvd = (size_t)n_kv * hd;
+    const float* nk = nullptr;
+    const float* nv = nullptr;
     if (write_kv && k_vec && v_vec) {  // :1903-1907
         const float* k = xl(k_vec);
         const float* v = xl(v_vec);
-        cudaMemcpyAsync(kc + (size_t)pos * kvd, k, kvd * 4, cudaMemcpyDefault, stream());
-        cudaMemcpyAsync(vc + (size_t)pos * kvd, v, kvd * 4, cudaMemcpyDefault, stream());
+        if (dev_accessible(k) && dev_accessible(v)) {
+            nk = k;  // the attention launch stores them in the cache
+            nv = v;
+        } else {
+            cudaMemcpyAsync(kc + (size_t)pos * kvd, k, kvd * 4, cudaMemcpyDefault, stream());
+            cudaMemcpyAsync(vc + (size_t)pos * kvd, v, kvd * 4, cudaMemcpyDefault, stream());
+        }
     }
     const int32_t recs = attention_scratch_records(pos, n_heads, window);
     const size_t part_bytes = align256((size_t)recs * attn_record_floats(hd) * 4);
@@ -683,7 +701,7 @@ void gncx_mqa_attention_step_ext(const float* q_vec, const float* k_vec, const f
     float* part = reinterpret_cast<float*>(ws);
     float* scores = g_exact_attention ? reinterpret_cast<float*>(ws + part_bytes) : nullptr;
     finish(attention_launch(q, kc, vc, pos, n_heads, n_kv, hd, attn_scale, window, out, AttnScratch{part, recs},
-                            g_rt.d_err, stream(), scores));
+                            g_rt.d_err, stream(), scores, nk, nv));
 }
 
 // Causal attention of a block of prompt positions: the reference's prefill

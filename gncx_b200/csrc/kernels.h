@@ -122,6 +122,13 @@ struct AttnArgs {
     float post_eps;
     const float* rope_c;
     const float* rope_s;
+    // One query (the drop-in step's write_kv): its own position's new K and V
+    // rows, [n_kv][hd] each, or null.  attention_run stores them in the cache at
+    // the query's position: the register-streaming kernel reads that position
+    // from here and writes the rows itself, every other path copies them into
+    // the cache before its kernels run.
+    const float* new_k;
+    const float* new_v;
 };
 int attention_run(const AttnArgs& a, int32_t n_tok, cudaStream_t st);
 // True when attention_run supports these head counts and head size.
@@ -135,7 +142,8 @@ struct AttnScratch {
 // to 64) floats for the exact serial softmax.
 int attention_launch(const float* q, float* kc, float* vc, int32_t pos, int32_t n_heads, int32_t n_kv,
                      int32_t head_dim, float scale, int32_t window, float* out, const AttnScratch& scratch,
-                     int32_t* err, cudaStream_t st, float* exact_scores = nullptr);
+                     int32_t* err, cudaStream_t st, float* exact_scores = nullptr, const float* new_k = nullptr,
+                     const float* new_v = nullptr);
 int32_t attention_scratch_records(int32_t pos, int32_t n_heads, int32_t window);
 
 // ---- sampling ----

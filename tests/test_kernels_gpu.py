@@ -308,6 +308,38 @@ def test_attention_config(gpu, oracle, ctx, window):
     assert np.array_equal(host(kc)[(ctx - 1) * nkv * hd:], kc_ref[(ctx - 1) * nkv * hd:])
 
 
+@pytest.mark.parametrize("nh,nkv,hd", [(4, 2, 64), (8, 1, 128), (32, 8, 128), (8, 8, 128)])
+@pytest.mark.parametrize("exact", [0, 1])
+def test_attention_write_kv(gpu, oracle, nh, nkv, hd, exact):
+    """write_kv = 1 (:1903-1907): the new K/V rows land in the cache at `pos`
+    and the step attends to them, whether the kernel reads them in place or
+    they are copied first; k/v from device memory and from host memory."""
+    scale = float(np.float32(1.0 / np.sqrt(hd)))
+    gpu.gncx_set_exact_attention(exact)
+    try:
+        for ctx in (1, 2, 17, 63, 64, 65, 129, 1025, 4097):
+            kc_np = synth.random_activations(ctx * nkv * hd, seed=ctx + 11)
+            vc_np = synth.random_activations(ctx * nkv * hd, seed=ctx + 12)
+            q = synth.random_activations(nh * hd, seed=ctx + 13)
+            k = synth.random_activations(nkv * hd, seed=ctx + 14)
+            v = synth.random_activations(nkv * hd, seed=ctx + 15)
+            for window in (0, 17):
+                ref, kc_ref, vc_ref = oracle.attention(q, k, v, kc_np, vc_np, ctx - 1, nh, nkv, hd, scale, window, 1)
+                for on_host in (False, True):
+                    kc, vc = dev(kc_np), dev(vc_np)
+                    kp = k.ctypes.data_as(ctypes.c_void_p) if on_host else P(dev(k))
+                    vp = v.ctypes.data_as(ctypes.c_void_p) if on_host else P(dev(v))
+                    y = out(nh * hd)
+                    gpu.gncx_mqa_attention_step_ext(P(dev(q)), kp, vp, P(kc), P(vc), ctx - 1, nh, nkv, hd, scale,
+                                                    window, 1, P(y))
+                    core.check(gpu)
+                    err = np.max(np.abs(host(y) - ref)) / np.max(np.abs(ref))
+                    assert err <= ATTN_TOL, (ctx, window, on_host, err)
+                    assert np.array_equal(host(kc), kc_ref) and np.array_equal(host(vc), vc_ref), (ctx, on_host)
+    finally:
+        gpu.gncx_set_exact_attention(0)
+
+
 @pytest.mark.parametrize("nh,nkv,hd", [(4, 2, 64), (8, 1, 128), (16, 8, 64), (32, 8, 128), (8, 8, 128), (8, 2, 64)])
 @pytest.mark.parametrize("exact", [0, 1])
 def test_attention_lengths(gpu, oracle, nh, nkv, hd, exact):
