@@ -1227,6 +1227,238 @@ __global__ void __launch_bounds__(kFusedThreads) attn_exact_fused_kernel(const A
     }
 }
 
+// Exact mode, one query, G <= 4, windows up to 4096 positions: two kernels.
+// attn_exact_softmax_reg_kernel (one CTA per head) forms the maximum, the
+// exps, their serial sum and the weights p_t = e_t * inv once per head;
+// attn_exact_reg_kernel (one CTA per (KV head, 8 output columns)) stages its
+// columns of every V row while the softmax runs, then forms each output
+// element's serial sum of p_t * v_t[d].  Every serial chain runs from
+// registers: the window is cut into 32-position segments, a chain's segment
+// s is held by lane s % 32 of the warp that runs the chain (one pass per 32
+// segments), and the segments are added one after the other -- the running
+// sum handed to the next lane by a shuffle -- so the adds are the
+// reference's, in its order, with no shared-memory load on the chain.  Warp w
+// of the PV kernel runs the four output columns 4 (w % 2) .. + 3 of head
+// w / 2 as four interleaved chains, their products formed in registers per
+// pass.  Shared memory keeps 4 floats of padding after every 32 positions (V
+// rows and the weights), so that the 32 lanes' loads of their segments hit
+// different banks.  8B exact-mode decode 3.20 -> 3.07 ms/token against
+// attn_exact_fused_kernel, where every PV CTA formed its group's whole
+// softmax (8200 double-precision exps at ~2050 positions, 16 times per KV
+// head) itself; the same one-kernel design with register chains measured
+// 3.23-3.54.
+constexpr int kXSeg = 32;  // positions per chain segment
+__host__ __device__ inline int xidx(int t) { return t + ((t >> 5) << 2); }
+__host__ __device__ inline size_t attn_exact_reg_smem(int G, int len) {
+    const size_t nseg = (size_t)(len + kXSeg - 1) / kXSeg;
+    return (nseg * (kXSeg * kFusedCols + 4) + (size_t)G * nseg * (kXSeg + 4)) * 4;
+}
+
+// The serial sum over t < len of e[xidx(t)] (non-negative terms) by one warp:
+// lane L holds segment p0 + L of 32 positions in registers, the segments are
+// added one after the other (the running sum handed to the next lane by a
+// shuffle), 32 segments per pass.  Positions past the window add +0, which
+// leaves a sum of non-negative terms unchanged.  Returns the sum in every lane.
+__device__ __forceinline__ float seg_chain_sum(const float* e, int nseg, int len, int lane) {
+    float carry = 0.0f;
+    for (int p0 = 0; p0 < nseg; p0 += 32) {
+        const int sg = p0 + lane;
+        float r[kXSeg];
+#pragma unroll
+        for (int q = 0; q < kXSeg / 4; ++q) {
+            const float4 v = sg < nseg ? *reinterpret_cast<const float4*>(e + (size_t)sg * (kXSeg + 4) + 4 * q)
+                                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            const int tq = sg * kXSeg + 4 * q;
+            r[4 * q] = tq < len ? v.x : 0.0f;
+            r[4 * q + 1] = tq + 1 < len ? v.y : 0.0f;
+            r[4 * q + 2] = tq + 2 < len ? v.z : 0.0f;
+            r[4 * q + 3] = tq + 3 < len ? v.w : 0.0f;
+        }
+        const int nr = min(32, nseg - p0);
+        float ain = lane == 0 ? carry : 0.0f, last = 0.0f;
+        for (int k = 0; k < nr; ++k) {  // round k: lane k's segment continues the chain
+            float x = ain;
+#pragma unroll
+            for (int i = 0; i < kXSeg; ++i) x = fadd(x, r[i]);
+            last = x;
+            ain = __shfl_up_sync(0xffffffffu, x, 1);
+        }
+        carry = __shfl_sync(0xffffffffu, last, nr - 1);
+    }
+    return carry;
+}
+
+constexpr int kXPer = 16;                          // scores per thread per head held in registers
+constexpr int kXMaxLen = kXPer * kFusedThreads;    // windows up to 4096 positions
+
+// One query, one CTA per head: the maximum of the scores, e_t = exp(s_t - max)
+// (every thread 16 positions, the loads all in flight at once), the serial
+// sum of e_t in position order by one warp with the chain in registers
+// (seg_chain_sum), inv = 1 / (sum + 1e-12), and the weights e_t * inv written
+// over the scores for attn_exact_reg_kernel<G, true>.  Computing the exps once
+// per head here, instead of in every CTA of the PV kernel (16 per KV head at
+// head_dim 128), keeps them off each PV CTA's path.
+__global__ void __launch_bounds__(kFusedThreads, 1) attn_exact_softmax_reg_kernel(const AttnArgs a) {
+    __shared__ __align__(16) float es[kXMaxLen / kXSeg * (kXSeg + 4)];
+    __shared__ float wmax[kFusedThreads / 32];
+    __shared__ float s_inv;
+    GNCX_TRACE_SCOPE(kTagAttnExactSoftmax, gridDim.x);
+    pdl_launch_dependents();
+    pdl_wait();
+    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int t0, len;
+    attn_window(a, 0, t0, len);
+    float* sc = a.scores + (size_t)h * a.score_cap;
+    float v[kXPer];
+#pragma unroll
+    for (int k = 0; k < kXPer; ++k) {
+        const int t = tid + k * kFusedThreads;
+        v[k] = t < len ? ld_l2(sc + t) : -1e30f;
+    }
+    float mx = -1e30f;  // the reference's running max starts at -1e30
+#pragma unroll
+    for (int k = 0; k < kXPer; ++k) mx = fmaxf(mx, v[k]);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) wmax[warp] = mx;
+    __syncthreads();
+    mx = wmax[0];
+#pragma unroll
+    for (int w = 1; w < kFusedThreads / 32; ++w) mx = fmaxf(mx, wmax[w]);
+#pragma unroll
+    for (int k = 0; k < kXPer; ++k) {
+        const int t = tid + k * kFusedThreads;
+        if (t < len) {
+            v[k] = exp_cr(fsub(v[k], mx));
+            es[xidx(t)] = v[k];
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const float sum = seg_chain_sum(es, (len + kXSeg - 1) / kXSeg, len, lane);
+        if (lane == 0) s_inv = fdiv(1.0f, fadd(sum, 1e-12f));
+    }
+    __syncthreads();
+    const float inv = s_inv;
+#pragma unroll
+    for (int k = 0; k < kXPer; ++k) {
+        const int t = tid + k * kFusedThreads;
+        if (t < len) sc[t] = fmul(v[k], inv);
+    }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kFusedThreads) attn_exact_reg_kernel(const AttnArgs a) {
+    extern __shared__ __align__(16) float fsm[];
+    GNCX_TRACE_SCOPE(kTagAttnExactPv, gridDim.x);
+    const int hd = a.hd;
+    const int ncb = hd / kFusedCols;
+    const int kvh = blockIdx.x / ncb, d0 = (blockIdx.x - kvh * ncb) * kFusedCols;
+    int t0, len;
+    attn_window(a, 0, t0, len);
+    const int nseg = (len + kXSeg - 1) / kXSeg;
+    const int lp = nseg * (kXSeg + 4);                            // floats per head row of es
+    float* vsl = fsm;                                               // row t at t * 8 + (t / 32) * 4
+    float* es = vsl + (size_t)nseg * (kXSeg * kFusedCols + 4);      // [G][lp] weights, position t at xidx(t)
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const size_t ps = (size_t)a.kv_pos_stride;
+    const float* vbase = a.vc + (size_t)t0 * ps + (size_t)kvh * a.kv_head_stride + d0;
+    constexpr int kPieces = kFusedCols / 4;  // 16-byte pieces per row
+    auto stage_v = [&](int ta, int tb) {
+        for (int i = tid; i < (tb - ta) * kPieces; i += kFusedThreads) {
+            const int t = ta + i / kPieces, c = i % kPieces;
+            cp_async16(vsl + (size_t)t * kFusedCols + ((t >> 5) << 2) + 4 * c, vbase + (size_t)t * ps + 4 * c);
+        }
+        cp_async_commit();
+    };
+    // rows below the query's own were written before the preceding kernel ran
+    const int n_old = a.prefetch_old ? len - 1 : 0;
+    if (n_old > 0) stage_v(0, n_old);
+    pdl_launch_dependents();
+    pdl_wait();
+    stage_v(n_old, len);
+    if (tid == 0) GNCX_TRACE_MARK(60, 0);
+    // the weights p_t, written over the scores by attn_exact_softmax_reg_kernel
+    const float* sc = a.scores + (size_t)(kvh * G) * a.score_cap;
+    float v[G][kXPer];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int k = 0; k < kXPer; ++k) {
+            const int t = tid + k * kFusedThreads;
+            v[g][k] = t < len ? ld_l2(sc + (size_t)g * a.score_cap + t) : 0.0f;
+        }
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int k = 0; k < kXPer; ++k) {
+            const int t = tid + k * kFusedThreads;
+            if (t < len) es[(size_t)g * lp + xidx(t)] = v[g][k];
+        }
+    cp_async_wait<0>();
+    __syncthreads();
+    if (tid == 0) GNCX_TRACE_MARK(63, 0);
+    // out[g][d0 + c0 + ch] = sum over t in order of w_t * v_t[d0 + c0 + ch]
+    if (warp < 2 * G) {
+        const int g = warp >> 1, c0 = (warp & 1) * 4;
+        const float* wr = es + (size_t)g * lp;
+        float carry0 = 0.0f, carry1 = 0.0f, carry2 = 0.0f, carry3 = 0.0f;
+        for (int p0 = 0; p0 < nseg; p0 += 32) {
+            const int sg = p0 + lane;
+            const bool segok = sg < nseg;
+            const float* wseg = wr + (size_t)sg * (kXSeg + 4);
+            const float* vseg = vsl + (size_t)sg * (kXSeg * kFusedCols + 4) + c0;
+            float p0r[kXSeg], p1r[kXSeg], p2r[kXSeg], p3r[kXSeg];
+#pragma unroll
+            for (int q = 0; q < kXSeg / 4; ++q) {
+                const float4 w4 = segok ? *reinterpret_cast<const float4*>(wseg + 4 * q)
+                                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int i = 4 * q + k;
+                    const bool ok = segok && sg * kXSeg + i < len;
+                    const float4 v4 = ok ? *reinterpret_cast<const float4*>(vseg + (size_t)i * kFusedCols)
+                                         : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    const float wv = k == 0 ? w4.x : k == 1 ? w4.y : k == 2 ? w4.z : w4.w;
+                    p0r[i] = ok ? fmul(wv, v4.x) : 0.0f;
+                    p1r[i] = ok ? fmul(wv, v4.y) : 0.0f;
+                    p2r[i] = ok ? fmul(wv, v4.z) : 0.0f;
+                    p3r[i] = ok ? fmul(wv, v4.w) : 0.0f;
+                }
+            }
+            const int nr = min(32, nseg - p0);
+            float a0 = lane == 0 ? carry0 : 0.0f, a1 = lane == 0 ? carry1 : 0.0f;
+            float a2 = lane == 0 ? carry2 : 0.0f, a3 = lane == 0 ? carry3 : 0.0f;
+            float l0 = 0.0f, l1 = 0.0f, l2 = 0.0f, l3 = 0.0f;
+            for (int k = 0; k < nr; ++k) {
+                float x0 = a0, x1 = a1, x2 = a2, x3 = a3;
+#pragma unroll
+                for (int i = 0; i < kXSeg; ++i) {
+                    x0 = fadd(x0, p0r[i]);
+                    x1 = fadd(x1, p1r[i]);
+                    x2 = fadd(x2, p2r[i]);
+                    x3 = fadd(x3, p3r[i]);
+                }
+                l0 = x0; l1 = x1; l2 = x2; l3 = x3;
+                a0 = __shfl_up_sync(0xffffffffu, x0, 1);
+                a1 = __shfl_up_sync(0xffffffffu, x1, 1);
+                a2 = __shfl_up_sync(0xffffffffu, x2, 1);
+                a3 = __shfl_up_sync(0xffffffffu, x3, 1);
+            }
+            carry0 = __shfl_sync(0xffffffffu, l0, nr - 1);
+            carry1 = __shfl_sync(0xffffffffu, l1, nr - 1);
+            carry2 = __shfl_sync(0xffffffffu, l2, nr - 1);
+            carry3 = __shfl_sync(0xffffffffu, l3, nr - 1);
+        }
+        if (lane == 0) {
+            float* o = a.out + (size_t)(kvh * G + g) * hd + d0 + c0;
+            o[0] = carry0;
+            o[1] = carry1;
+            o[2] = carry2;
+            o[3] = carry3;
+        }
+    }
+}
+
 // out[h][d] = sum over t (serial) of p_t * v_t[d].  One CTA per (KV head,
 // group of up to 8 query heads, slice of kExactSlice output columns, query);
 // thread (g, d) runs one chain.  V rows and p stream through double-buffered
@@ -1410,6 +1642,21 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
             len1 = a.pos0 + 1 - t0;
         } else if (n_tok == 1) {
             len1 = a.score_cap;  // upper bound: the position is read on the device
+        }
+        // G <= 4: the register-chain kernel
+        static const bool no_reg = getenv("GNCX_EXACT_SMEM_CHAINS") != nullptr;  // A/B override
+        const size_t rsm = attn_exact_reg_smem(G, len1);
+        if (!no_reg && n_tok == 1 && vec && !act && a.hd % kFusedCols == 0 && (G == 1 || G == 2 || G == 4) &&
+            len1 > 0 && len1 <= kXMaxLen && rsm <= (size_t)dev.max_smem_optin && !getenv("GNCX_EXACT_UNFUSED")) {
+            // the softmax once per head, then the PV per (KV head, 8 columns)
+            void (*k)(const AttnArgs) = G == 4 ? attn_exact_reg_kernel<4>
+                                        : G == 2 ? attn_exact_reg_kernel<2> : attn_exact_reg_kernel<1>;
+            if (set_smem_limit(k, rsm) != cudaSuccess) return kErrCuda;
+            if (launch_k(attn_exact_softmax_reg_kernel, dim3(a.n_heads), dim3(kFusedThreads), 0, st, a) != cudaSuccess)
+                return kErrCuda;
+            return launch_k(k, dim3(a.n_kv * (a.hd / kFusedCols)), dim3(kFusedThreads), rsm, st, a) == cudaSuccess
+                       ? kOk
+                       : kErrCuda;
         }
         const size_t fsm = attn_exact_fused_smem(G, len1);
         if (n_tok == 1 && vec && !act && a.hd % kFusedCols == 0 && G * kFusedCols <= kFusedThreads && len1 > 0 &&
