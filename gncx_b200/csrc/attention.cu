@@ -899,7 +899,15 @@ __device__ __forceinline__ void rows_batch(const float (&q)[G][DPL], float (&o)[
 
 // PF: the next batch's rows are loaded before the current one is computed
 // (two batches of registers in flight per warp).
-template <int DPL, int G, int B, bool PF, bool MERGE>
+// POSTQ (the engine's split-KV decode): q is the QKV GEMV's raw output and the
+// kernel does the Q/K post step itself -- warps 0..G-1 norm and rotate the
+// group's q heads in shared memory (warp_head_norm_rope, the partial kernel's
+// arithmetic), and in the CTA whose range ends the window the last warp makes
+// the new K row (normed, rotated) and stores it with the new V row in the
+// cache at the query's position before the CTA's loads; the launch may hold
+// CTAs past the window (ranges sized for the largest window the records
+// cover), which exit at once and do not arrive at the merge.
+template <int DPL, int G, int B, bool PF, bool MERGE, bool POSTQ>
 __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnArgs a, int ppc) {
     constexpr int HD = DPL * 32;
     constexpr int NV = B * G;  // (position, head) pairs per batch
@@ -922,11 +930,40 @@ __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnAr
     const float* kbase = a.kc + (size_t)t0 * ps + (size_t)kvh * a.kv_head_stride + lane * DPL;
     const float* vbase = a.vc + (size_t)t0 * ps + (size_t)kvh * a.kv_head_stride + lane * DPL;
     float q[G][DPL], o[G][DPL];
+    if constexpr (POSTQ) {
+        __shared__ __align__(16) float qs[G][HD];
+        __shared__ __align__(16) float kx[HD];
+        const int pos = t0 + len - 1;
+        const bool own = p1 == len;  // this CTA's range ends the window
+        for (int i = threadIdx.x; i < G * HD; i += kRowsThreads) qs[i / HD][i % HD] = a.q[(size_t)kvh * G * HD + i];
+        if (own)
+            for (int i = threadIdx.x; i < HD; i += kRowsThreads) kx[i] = a.post_k[(size_t)kvh * HD + i];
+        __syncthreads();
+        if (warp < G)
+            warp_head_norm_rope(qs[warp], HD, a.post_qn, a.post_norm != 0, a.post_eps, a.rope_c, a.rope_s, pos, lane);
+        if (own && warp == kRowsWarps - 1) {
+            warp_head_norm_rope(kx, HD, a.post_kn, a.post_norm != 0, a.post_eps, a.rope_c, a.rope_s, pos, lane);
+            const size_t at = (size_t)pos * ps + (size_t)kvh * a.kv_head_stride;
+            for (int i = lane; i < HD; i += 32) {
+                const_cast<float*>(a.kc)[at + i] = kx[i];
+                const_cast<float*>(a.vc)[at + i] = a.post_v[(size_t)kvh * HD + i];
+            }
+        }
+        __syncthreads();  // q heads ready; the new K/V rows are in the cache for this CTA's loads
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        rows_load<DPL>(a.q + (size_t)(kvh * G + g) * HD + lane * DPL, q[g]);
+        for (int g = 0; g < G; ++g)
 #pragma unroll
-        for (int k = 0; k < DPL; ++k) o[g][k] = 0.0f;
+            for (int k = 0; k < DPL; ++k) {
+                q[g][k] = qs[g][lane * DPL + k];
+                o[g][k] = 0.0f;
+            }
+    } else {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            rows_load<DPL>(a.q + (size_t)(kvh * G + g) * HD + lane * DPL, q[g]);
+#pragma unroll
+            for (int k = 0; k < DPL; ++k) o[g][k] = 0.0f;
+        }
     }
     float m = -INFINITY, l = 0.0f;
     const float scale = a.scale;
@@ -1005,14 +1042,15 @@ __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnAr
         // pass per output pair of columns with a running maximum
         __shared__ int s_last;
         __syncthreads();  // this CTA's records are written
+        const unsigned n_arr = (unsigned)((len + ppc - 1) / ppc);  // the CTAs whose range meets the window
         if (threadIdx.x == 0) {
             __threadfence();
-            s_last = atomicInc(&g_rows_arrive[kvh], gridDim.x - 1) == gridDim.x - 1;
+            s_last = atomicInc(&g_rows_arrive[kvh], n_arr - 1) == n_arr - 1;
         }
         __syncthreads();
         if (!s_last) return;  // uniform per CTA
         __threadfence();
-        const int n = gridDim.x;
+        const int n = (int)n_arr;
         constexpr int kRb = 16;  // records in flight per thread
         for (int t = threadIdx.x; t < G * HD / 2; t += kRowsThreads) {
             const int g = t / (HD / 2), d = 2 * (t - g * (HD / 2));
@@ -1046,15 +1084,21 @@ __global__ void __launch_bounds__(kRowsThreads, 2) attn_rows_kernel(const AttnAr
     }
 }
 
-template <int DPL, int G, bool MERGE>
+template <int DPL, int G, bool MERGE, bool POSTQ>
 static cudaError_t launch_rows_g(const AttnArgs& a, dim3 grid, int ppc, int B, cudaStream_t st) {
     constexpr int BMAX = 32 / G < 8 ? 32 / G : 8;
     constexpr int BPF = BMAX >= 4 ? 4 : BMAX;
     constexpr int BPP = G >= 8 ? 2 : BPF;  // two batches of registers in flight
-    if (B < 0) return launch_k(attn_rows_kernel<DPL, G, BPP, true, MERGE>, grid, dim3(kRowsThreads), 0, st, a, ppc);
-    if (B >= BMAX)
-        return launch_k(attn_rows_kernel<DPL, G, BMAX, false, MERGE>, grid, dim3(kRowsThreads), 0, st, a, ppc);
-    return launch_k(attn_rows_kernel<DPL, G, BPF, false, MERGE>, grid, dim3(kRowsThreads), 0, st, a, ppc);
+    if constexpr (POSTQ) {  // one batch size: the engine's decode
+        return launch_k(attn_rows_kernel<DPL, G, BMAX, false, MERGE, true>, grid, dim3(kRowsThreads), 0, st, a, ppc);
+    } else {
+        if (B < 0)
+            return launch_k(attn_rows_kernel<DPL, G, BPP, true, MERGE, false>, grid, dim3(kRowsThreads), 0, st, a, ppc);
+        if (B >= BMAX)
+            return launch_k(attn_rows_kernel<DPL, G, BMAX, false, MERGE, false>, grid, dim3(kRowsThreads), 0, st, a,
+                            ppc);
+        return launch_k(attn_rows_kernel<DPL, G, BPF, false, MERGE, false>, grid, dim3(kRowsThreads), 0, st, a, ppc);
+    }
 }
 
 // head_dim 64 or 128, G in {1, 2, 4, 8}
@@ -1065,22 +1109,22 @@ static bool rows_ok(const AttnArgs& a) {
            a.kv_pos_stride % (a.hd / 32) == 0 && a.kv_head_stride % (a.hd / 32) == 0;
 }
 
-template <bool MERGE>
+template <bool MERGE, bool POSTQ = false>
 static cudaError_t launch_rows(const AttnArgs& a, dim3 grid, int ppc, int B, cudaStream_t st) {
     const int G = a.n_heads / a.n_kv;
     if (a.hd == 128) {
         switch (G) {
-            case 1: return launch_rows_g<4, 1, MERGE>(a, grid, ppc, B, st);
-            case 2: return launch_rows_g<4, 2, MERGE>(a, grid, ppc, B, st);
-            case 4: return launch_rows_g<4, 4, MERGE>(a, grid, ppc, B, st);
-            default: return launch_rows_g<4, 8, MERGE>(a, grid, ppc, B, st);
+            case 1: return launch_rows_g<4, 1, MERGE, POSTQ>(a, grid, ppc, B, st);
+            case 2: return launch_rows_g<4, 2, MERGE, POSTQ>(a, grid, ppc, B, st);
+            case 4: return launch_rows_g<4, 4, MERGE, POSTQ>(a, grid, ppc, B, st);
+            default: return launch_rows_g<4, 8, MERGE, POSTQ>(a, grid, ppc, B, st);
         }
     }
     switch (G) {
-        case 1: return launch_rows_g<2, 1, MERGE>(a, grid, ppc, B, st);
-        case 2: return launch_rows_g<2, 2, MERGE>(a, grid, ppc, B, st);
-        case 4: return launch_rows_g<2, 4, MERGE>(a, grid, ppc, B, st);
-        default: return launch_rows_g<2, 8, MERGE>(a, grid, ppc, B, st);
+        case 1: return launch_rows_g<2, 1, MERGE, POSTQ>(a, grid, ppc, B, st);
+        case 2: return launch_rows_g<2, 2, MERGE, POSTQ>(a, grid, ppc, B, st);
+        case 4: return launch_rows_g<2, 4, MERGE, POSTQ>(a, grid, ppc, B, st);
+        default: return launch_rows_g<2, 8, MERGE, POSTQ>(a, grid, ppc, B, st);
     }
 }
 
@@ -1773,6 +1817,21 @@ int attention_run(const AttnArgs& args, int32_t n_tok, cudaStream_t st) {
     } else if (stream) {
         e = launch_k(attn_stream_kernel, sgrid, dim3(kStreamThreads), ssm, st, sa, cpp);
     } else {
+        // decode with the fused post step, fp32 output (the engine's split-KV
+        // decode): the register-streaming kernel with the post step and the
+        // in-kernel merge, one CTA per (split of a.chunk positions, KV head)
+        // over the splits the records cover (the position is read on the
+        // device; CTAs past the window exit).  The ranges depend only on the
+        // caller's split size, so a tensor-parallel rank forms every head
+        // exactly as one GPU does.
+        static const bool no_rows_post = getenv("GNCX_ENGINE_ATTN_PARTIAL") != nullptr;  // A/B override
+        if (!no_rows_post && n_tok == 1 && a.post_k && a.window == 0 && a.out && !act && rows_ok(a) &&
+            ((uintptr_t)a.out & 7) == 0 && ((uintptr_t)a.post_k & 15) == 0 && a.n_kv <= kRowsMaxKv &&
+            a.max_splits <= kRowsMaxParts && a.chunk % 8 == 0) {
+            return launch_rows<true, true>(a, dim3(a.max_splits, a.n_kv, 1), a.chunk, 8, st) == cudaSuccess
+                       ? kOk
+                       : kErrCuda;
+        }
         e = vec ? launch_partial<true, false>(a, grid, smem, st) : launch_partial<false, false>(a, grid, smem, st);
     }
     if (e != cudaSuccess) return kErrCuda;

@@ -302,6 +302,13 @@ static int gemv_norm(Engine* e, const uint8_t* w, int t, const uint8_t* act, con
                                  e->stream);
 }
 
+// Split-KV decode attention through the partial + combine kernels instead of
+// the register-streaming kernel (A/B override).
+static bool attn_partial_env() {
+    static const bool on = getenv("GNCX_ENGINE_ATTN_PARTIAL") != nullptr;
+    return on;
+}
+
 static int gather(Engine* e, size_t buf, int rows, int row_floats, int off, int len) {
     return tp_gather_launch(e->tp, buf, rows, row_floats, off, len, e->d_err, e->stream);
 }
@@ -410,12 +417,13 @@ static int decode_step(Engine* e, bool sample, double penalty) {
             a.out_stride = QD;
             a.act_out = ActOut{nullptr, nullptr};
         } else {
-            // exact mode: the fp32 output replaces q and the O GEMV quantizes it
-            // (the fused softmax + PV kernel writes no act); split-KV: the
-            // combine writes the act only
-            a.out = e->exact ? e->qkv : nullptr;
+            // the fp32 output replaces q and the O GEMV quantizes it (the
+            // attention kernels that merge in-kernel write no act);
+            // GNCX_ENGINE_ATTN_PARTIAL: split-KV through the partial + combine
+            // kernels, the combine writing the act only
+            a.out = e->exact || !attn_partial_env() ? e->qkv : nullptr;
             a.out_stride = qkv_w;
-            a.act_out = e->exact ? ActOut{nullptr, nullptr} : ActOut{nullptr, e->act_q};
+            a.act_out = a.out ? ActOut{nullptr, nullptr} : ActOut{nullptr, e->act_q};
         }
         a.prefetch_old = 1;  // cache rows below pos come from earlier tokens
         a.err = e->d_err;
@@ -434,7 +442,7 @@ static int decode_step(Engine* e, bool sample, double penalty) {
         } else if (tp) {  // gather the heads, then the whole attn_output on every rank
             CK(gather_row(e, kLlAttn));
             CK(gemv_norm(e, w.wo, w.to, nullptr, gq, QD, e->proj, w.ffn_norm));
-        } else if (e->exact) {
+        } else if (e->exact || !attn_partial_env()) {
             CK(gemv_norm(e, w.wo, w.to, nullptr, e->qkv, QD, e->proj, w.ffn_norm));
         } else {
             CK(gemv_norm(e, w.wo, w.to, e->act_q, nullptr, QD, e->proj, w.ffn_norm));
