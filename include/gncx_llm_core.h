@@ -19,6 +19,12 @@
  * reference-named call also waits for its GPU work (synchronous mode), so a
  * caller that reads results on the host, as the Lua orchestrator does, sees
  * them complete.  gncx_set_synchronous(0) makes calls stream-ordered.
+ *
+ * Concurrency.  Split-KV decode attention (gncx_mqa_attention_step_ext, its
+ * allocation-free variant and an engine's decode step) merges its records in
+ * the kernel, counting arrivals per KV head in one set of counters per GPU.
+ * Keep such calls on one GPU from running at the same time on different
+ * streams: use one stream per GPU for them, or order the streams.
  */
 #ifndef GNCX_LLM_CORE_H
 #define GNCX_LLM_CORE_H
